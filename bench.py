@@ -1,0 +1,349 @@
+"""Benchmark of the MXFP4 A4W4 GEMM (BASELINE.json metric: TFLOPS at 8192^3).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mbs|reference]
+                    [--workload prefill|decode] [--m M]
+
+One step = one gemm_a4w4 call on the workload (default: BASELINE config[2],
+M = N = K = 8192, MXFP4 A and B quantised from seeded N(0,1) bf16, bf16 out).
+`value` is device-timed (CUDA events on the launching stream) with inputs
+resident in HBM and L2 flushed before every step; `e2e` times the public
+operator with host (pinned) operands copied in and the result copied out
+inside the timed region.  Under torchrun every rank runs its own workload
+(weak scaling: replicas, no collective in the timed region) and the JSON
+line reports the max time over ranks.
+
+`--impl reference` times the reference's CPU path (the dequantise-then-matmul
+oracle of test_gemm_a4w4.py:28-44, restated in oracle/) on the host cores on
+a bounded row sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+FP4_PER_BF16 = 4.0  # dense FP4 : BF16 tensor throughput on B200 (9 : 2.25 PFLOP/s nominal)
+L2_FLUSH_BYTES = 256 << 20
+
+THROTTLE_BITS = {
+    0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+    0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+    0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+    0x100: "display_clock_setting",
+}
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["mbs", "reference"], default="mbs")
+    ap.add_argument("--workload", choices=["prefill", "decode"], default="prefill")
+    ap.add_argument("--m", type=int, default=None, help="M for --workload decode (default 16)")
+    ap.add_argument("--e2e-steps", type=int, default=5)
+    return ap.parse_args()
+
+
+def workload_shape(args):
+    if args.workload == "decode":
+        M = args.m or 16
+        return M, 57344, 8192, f"cfg1 decode M={M} N=57344 K=8192 (Llama-3-70B gate+up)"
+    return 8192, 8192, 8192, "cfg2 prefill M=N=K=8192"
+
+
+def load_peaks():
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return d, "MEASURED_PEAKS.json"
+    except OSError:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index),
+                 "--query-gpu=clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], 0.0, set()
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 4:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = max(mx, float(parts[1]))
+                bits = int(parts[3], 16) if parts[3].startswith("0x") else int(parts[3])
+            except ValueError:
+                continue
+            for b, name in THROTTLE_BITS.items():
+                if bits & b and name != "gpu_idle":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup(args):
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        torch.cuda.set_device(local)
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def make_inputs(M, N, K, seed, device):
+    import torch
+
+    import mbs_b200
+    g = torch.Generator(device=device).manual_seed(seed)
+    x = torch.randn(M, K, device=device, generator=g).to(torch.bfloat16)
+    std = 0.02 if M <= 64 else 1.0
+    w = (torch.randn(N, K, device=device, generator=g) * std).to(torch.bfloat16)
+    qa, sa = mbs_b200.quantize_mxfp4(x, shuffle=True)
+    qw, sw = mbs_b200.quantize_mxfp4(w, shuffle=False)
+    del x, w
+    B = mbs_b200.shuffle_weight(qw)
+    Bs = mbs_b200.shuffle_scales(sw, K)
+    del qw, sw
+    return qa, B, sa, Bs
+
+
+def run_mbs(args):
+    import torch
+    import torch.distributed as dist
+
+    import mbs_b200
+    from mbs_b200 import _lib
+
+    world, rank, local = dist_setup(args)
+    dev = torch.device("cuda", local)
+    M, N, K, wl_name = workload_shape(args)
+    A, B, As, Bs = make_inputs(M, N, K, seed=1234 + rank, device=dev)
+    out = torch.empty(((M + 31) // 32 * 32, N), dtype=torch.bfloat16, device=dev)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        mbs_b200.gemm_a4w4(A, B, As, Bs, out=out)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    with ClockSampler(local) as clk:
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        t_wall = time.perf_counter()
+        for i in range(args.steps):
+            flush.fill_(i)  # evict the operands from L2 (256 MB write > 126 MB L2)
+            starts[i].record(stream)
+            step()
+            ends[i].record(stream)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        t_wall = time.perf_counter() - t_wall
+    per_step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    total_ms = sum(per_step_ms)
+    if world > 1:
+        t = torch.tensor([total_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+    ms = total_ms / args.steps
+    flops = 2.0 * M * N * K
+    value = world * flops * args.steps / (total_ms * 1e-3) / 1e12
+    kernel_tflops = flops / (ms * 1e-3) / 1e12
+
+    # e2e: public operator on host operands (pinned), copies inside the timed region
+    hA, hB = A.cpu().pin_memory(), B.cpu().pin_memory()
+    hAs, hBs = As.cpu().pin_memory(), Bs.cpu().pin_memory()
+    hout = torch.empty((M, N), dtype=torch.bfloat16).pin_memory()
+    dA, dB, dAs, dBs = (torch.empty_like(t, device=dev) for t in (hA, hB, hAs, hBs))
+
+    def e2e_step():
+        dA.copy_(hA, non_blocking=True)
+        dB.copy_(hB, non_blocking=True)
+        dAs.copy_(hAs, non_blocking=True)
+        dBs.copy_(hBs, non_blocking=True)
+        o = mbs_b200.gemm_a4w4(dA, dB, dAs, dBs)
+        hout.copy_(o, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(args.e2e_steps):
+        e2e_step()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = ev0.elapsed_time(ev1) / args.e2e_steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    h2d = sum(t.numel() * t.element_size() for t in (hA, hB, hAs, hBs))
+    d2h = hout.numel() * hout.element_size()
+
+    peaks, src = load_peaks()
+    if args.workload == "prefill":
+        peak = FP4_PER_BF16 * float(peaks["bf16_tflops"])
+        roof = {"bound": "tensor", "achieved": round(kernel_tflops, 2), "peak": round(peak, 1),
+                "unit": "TFLOP/s", "frac": round(kernel_tflops / peak, 4), "traffic": None,
+                "peak_source": f"4 x bf16_tflops of {src} (dense FP4:BF16 = 4:1)"}
+    else:
+        nbytes = N * K // 2 + N * K // 32 + M * K // 2 + M * K // 32 + M * N * 2
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        roof = {"bound": "hbm", "achieved": round(gbs, 1), "peak": float(peaks["hbm_gbs"]),
+                "unit": "GB/s", "frac": round(gbs / float(peaks["hbm_gbs"]), 4), "traffic": None,
+                "peak_source": src, "algorithmic_bytes": nbytes}
+    line = {
+        "metric": "A4W4 MXFP4 GEMM TFLOPS" if args.workload == "prefill"
+                  else "A4W4 MXFP4 GEMM decode TFLOPS",
+        "value": round(value, 2), "unit": "TFLOPS", "n_gpus": world, "steps": args.steps,
+        "warmup": max(args.warmup, 3), "ms_per_step": round(ms, 5), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "e2m1 (fp32 accumulate, bf16 out)",
+        "data": "synthetic (seeded N(0,1) bf16 quantised to MXFP4 on device)",
+        "config": {"workload": wl_name, "M": M, "N": N, "K": K,
+                   "l2": "flushed before every step (256 MB write)",
+                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
+        "roofline": roof,
+        "clocks": clk.summary(),
+        "e2e": {"value": round(world * flops / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOPS",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "ms_per_step": round(e2e_ms, 4)},
+        "gpu_launches": args.steps,
+        "wall_s": round(t_wall, 3),
+    }
+    if rank == 0 and world == 1:
+        line["cpu_baseline"] = cpu_baseline(M, N, K)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    del _lib
+
+
+def _cpu_sample(M, N, K, rows, seed=0):
+    """Oracle inputs for a row sample of the workload (random fp4 codes/scales)."""
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    qa = rng.integers(0, 256, size=(rows, K // 2), dtype=np.uint8)
+    qb = rng.integers(0, 256, size=(N, K // 2), dtype=np.uint8)
+    sa = rng.integers(120, 130, size=(rows, K // 32), dtype=np.uint8)
+    sb = rng.integers(120, 130, size=(N, K // 32), dtype=np.uint8)
+    return qa, qb, sa, sb
+
+
+def cpu_baseline(M, N, K, budget_s=20.0):
+    """The oracle's dequantise-then-matmul on the host cores, on a row sample of A."""
+    from oracle import mxfp4_oracle as O
+    rows = min(M, 512)
+    qa, qb, sa, sb = _cpu_sample(M, N, K, rows)
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while len(times) < 3 and (not times or time.perf_counter() < t_end):
+        t0 = time.perf_counter()
+        O.gemm_ref(qa, qb, sa, sb)
+        times.append(time.perf_counter() - t0)
+    best = min(times)
+    return {"value": round(2.0 * rows * N * K / best / 1e12, 5), "unit": "TFLOPS",
+            "cores": os.cpu_count(), "kind": "port",
+            "sample": f"{rows} of {M} rows of A against all of B (dequant + fp32 matmul + bf16 "
+                      f"cast), best of {len(times)}"}
+
+
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    M, N, K, wl_name = workload_shape(args)
+    from oracle import mxfp4_oracle as O
+    rows = min(M, 256)
+    qa, qb, sa, sb = _cpu_sample(M, N, K, rows)
+    for _ in range(args.warmup):
+        O.gemm_ref(qa[:8], qb, sa[:8], sb)
+    ts = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        O.gemm_ref(qa, qb, sa, sb)
+        ts.append(time.perf_counter() - t0)
+    ms = statistics.mean(ts) * 1e3
+    value = 2.0 * rows * N * K / (ms * 1e-3) / 1e12
+    sample = (f"{rows} of {M} rows of A per step (oracle port of test_gemm_a4w4.py:28-44: "
+              f"dequant + fp32 matmul + bf16 cast)")
+    print(json.dumps({
+        "impl": "reference", "metric": "A4W4 MXFP4 GEMM TFLOPS", "value": round(value, 5),
+        "unit": "TFLOPS", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32 (dequantised e2m1)", "data": "synthetic",
+        "config": {"workload": wl_name, "M": M, "N": N, "K": K},
+        "cpu_baseline": {"value": round(value, 5), "unit": "TFLOPS", "cores": os.cpu_count(),
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": round(value, 5), "unit": "TFLOPS", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_mbs(args)
+
+
+if __name__ == "__main__":
+    main()

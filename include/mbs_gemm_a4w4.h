@@ -1,0 +1,152 @@
+/*
+ * mbs_gemm_a4w4.h -- C ABI of libmbs_gemm_kernel.so, the B200 (sm_100a)
+ * MXFP4 "A4W4" GEMM and its quantiser.
+ *
+ * Every entry point is extern "C", takes plain device pointers, sizes and a
+ * cudaStream_t passed as void*, never aborts, and returns an int status
+ * (MBS_OK = 0).  Launches are asynchronous on the given stream; inputs are
+ * borrowed for the duration of the stream work.
+ *
+ * Operand formats (the reference's input contract, unchanged):
+ *   A        [M, K/2]  fp4x2 (uint8), row-major, element 2j in the low nibble
+ *   B        [N, K/2]  fp4x2, preshuffled 16x16 ("flatB"):
+ *              flatB(n,kp) = (n/16)*(K/64*512) + (kp/32)*512 + ((kp%32)/16)*256
+ *                            + (n%16)*16 + kp%16
+ *   A_scale  e8m0 (uint8), shuffled ("flatS"), Mpad x scaleN_pad bytes
+ *   B_scale  e8m0, shuffled, roundup(N,32) x scaleN_pad bytes
+ *              flatS(r,b) = (r%32)/16 + ((b%8)/4)*2 + (r%16)*4 + (b%4)*64
+ *                           + (b/8)*256 + (r/32)*32*scaleN_pad
+ *   out      bf16 [>= M, N] row-major; rows >= M are never written
+ *   factors  optional uint8 [M] / [N]; byte b scales by f(b) = 1/(1 + b/256)
+ *   scaleN_pad = roundup(ceil(K/32), 8), Mpad = roundup(M, 32)
+ *
+ * Shape rules: M >= 1, N % 16 == 0, K % 64 == 0 (the preshuffle needs whole
+ * 64-element K tiles), all operand pointers 16-byte aligned.
+ */
+#ifndef MBS_GEMM_A4W4_H
+#define MBS_GEMM_A4W4_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---------------------------------------------------- */
+#define MBS_OK 0
+#define MBS_ERR_INVALID_ARGUMENT 1  /* null pointer, non-positive size, bad pad */
+#define MBS_ERR_UNSUPPORTED_SHAPE 2 /* N % 16 != 0, K % 64 != 0, too large     */
+#define MBS_ERR_MISALIGNED 3        /* an operand is not 16-byte aligned        */
+#define MBS_ERR_CUDA 4              /* CUDA runtime / driver error              */
+#define MBS_ERR_WORKSPACE 5         /* caller workspace too small               */
+#define MBS_ERR_DEVICE 6            /* no sm_100 device current                 */
+#define MBS_ERR_DEVICE_TIMEOUT 7    /* a kernel wait ran out (see mbs_device_error) */
+
+/* Short name of a status code. */
+const char* mbs_status_string(int status);
+
+/* Detail message of the last failing call on this host thread ("" if none). */
+const char* mbs_last_error_message(void);
+
+/* ---- GEMM ------------------------------------------------------------ */
+
+/*
+ * out[m][n] = bf16( (sum_k dq(A)[m][k] * dq(B)[n][k]) * f(AFactor[m]) * f(BFactor[n]) )
+ *
+ * Replaces the reference launcher `bool gemm_a4w4_mxfp4_launch(...)`
+ * (kernel/gemm_a4w4.h:27-39, kernel/gemm_a4w4.hip:1044-1146) with the same
+ * argument list.  Differences: returns an int status instead of bool, and
+ * accepts MBS factors on every shape (the reference rejects factors when it
+ * falls back to its single-wave kernel, kernel/gemm_a4w4.hip:1114-1115).
+ * AFactor / BFactor may each be NULL (factor 1).
+ *
+ * Skinny and small problems use a stream-K schedule whose scratch buffer is
+ * owned by the library: it is allocated with cudaMalloc on the first call per
+ * (device, stream), so make that first call outside stream capture.  Callers
+ * that manage memory themselves use mbs_gemm_a4w4_launch_ws.
+ */
+int gemm_a4w4_mxfp4_launch(const uint8_t* A, const uint8_t* B, const uint8_t* AScale,
+                           const uint8_t* BScale, const uint8_t* AFactor, const uint8_t* BFactor,
+                           void* out, int M, int N, int K, int Mpad, int scaleN_pad, void* stream);
+
+/*
+ * Bytes of scratch memory mbs_gemm_a4w4_launch_ws needs for this shape
+ * (0 if the chosen schedule needs none).  Same call as the reference
+ * launcher plus a caller workspace; no reference counterpart (the reference
+ * kernel has no split-K/stream-K path).
+ */
+size_t mbs_gemm_a4w4_workspace_size(int M, int N, int K);
+
+/*
+ * As gemm_a4w4_mxfp4_launch, with caller-provided scratch memory.  The
+ * workspace must be zero-filled before its first use; every launch that
+ * completes leaves it zero-filled again, so it can be reused on the same
+ * stream without clearing.  Launches that overlap on the GPU must not share
+ * a workspace.
+ */
+int mbs_gemm_a4w4_launch_ws(const uint8_t* A, const uint8_t* B, const uint8_t* AScale,
+                            const uint8_t* BScale, const uint8_t* AFactor, const uint8_t* BFactor,
+                            void* out, int M, int N, int K, int Mpad, int scaleN_pad,
+                            void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Macro-block-scaling variant: B's e8m0 scales are shared by 32-row x 32-K
+ * blocks and given plainly as BScaleMacro[ceil(N/32)][mb_ld] with
+ * mb_ld = roundup(K/32, 16).  A and A_scale are as above.  Spec-defined
+ * extension; the reference has no such kernel.
+ */
+int mbs_gemm_a4w4_macro_launch_ws(const uint8_t* A, const uint8_t* B, const uint8_t* AScale,
+                                  const uint8_t* BScaleMacro, const uint8_t* AFactor,
+                                  const uint8_t* BFactor, void* out, int M, int N, int K, int Mpad,
+                                  int scaleN_pad, int mb_ld, void* workspace,
+                                  size_t workspace_bytes, void* stream);
+
+/* ---- quantiser and layout kernels ------------------------------------ */
+
+/*
+ * bf16 [rows, K] (row stride ld_x elements) -> fp4x2 [rows, K/2] + e8m0 scales.
+ * OCP MX per-1x32: scale = 2^(floor(log2 amax) - 2) (byte clamped at 0, 0xFF
+ * for blocks holding Inf/NaN), values RNE onto the e2m1 grid saturating at 6.
+ * shuffled == 0: scales plain [rows, K/32].  shuffled != 0: scales in the
+ * flatS layout, roundup(rows,32) x scaleN_pad bytes, padding bytes = 127.
+ * Replaces aiter's per_1x32 Triton quantiser (called at
+ * test_gemm_a4w4.py:134-140, bench_one.py:20-25).  Requires K % 32 == 0.
+ */
+int mbs_quantize_mxfp4(const void* x_bf16, int rows, int K, int ld_x, uint8_t* fp4_out,
+                       uint8_t* scale_out, int shuffled, void* stream);
+
+/*
+ * Macro-block quantiser: one scale per 32-row x 32-K block of x, written as
+ * scale_out[ceil(rows/32)][roundup(K/32,16)] (padding 127).  No reference
+ * counterpart (spec-defined).
+ */
+int mbs_quantize_mxfp4_macro(const void* x_bf16, int rows, int K, int ld_x, uint8_t* fp4_out,
+                             uint8_t* scale_out, void* stream);
+
+/*
+ * Plain fp4x2 [N, K/2] -> flatB preshuffled [N, K/2].  Replaces aiter's
+ * shuffle_weight(layout=(16,16)) (test_gemm_a4w4.py:141); layout decoded at
+ * kernel/gemm_a4w4.hip:84-95.  Requires N % 16 == 0, K % 64 == 0.
+ */
+int mbs_shuffle_weight(const uint8_t* src, uint8_t* dst, int N, int K, void* stream);
+
+/*
+ * Plain scales [rows, K/32] -> flatS buffer roundup(rows,32) x scaleN_pad
+ * (padding 127).  Replaces aiter's quant(shuffle=True) scale layout; decoded
+ * at kernel/gemm_a4w4.hip:97-105.
+ */
+int mbs_shuffle_scales(const uint8_t* plain, uint8_t* shuffled, int rows, int K, void* stream);
+
+/*
+ * Sticky device-side error word of the current device: 0, or the code of a
+ * kernel wait that ran out (MBS_ERR_DEVICE_TIMEOUT).  Synchronises the
+ * device.  reset != 0 clears it.  No reference counterpart.
+ */
+int mbs_device_error(int* code_out, int reset);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MBS_GEMM_A4W4_H */

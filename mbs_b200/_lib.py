@@ -1,0 +1,77 @@
+"""ctypes binding of libmbs_gemm_kernel.so (declared in include/mbs_gemm_a4w4.h).
+
+The library is the product's compute path; there is no fallback.  If it is
+missing, every operator raises instead of computing anything elsewhere.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+from .build import LIB_PATH
+
+_c_int, _c_void_p, _c_size_t, _c_char_p = ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_char_p
+
+# name -> (restype, argtypes); must match include/mbs_gemm_a4w4.h
+SIGNATURES = {
+    "mbs_status_string": (_c_char_p, [_c_int]),
+    "mbs_last_error_message": (_c_char_p, []),
+    "gemm_a4w4_mxfp4_launch": (_c_int, [_c_void_p] * 7 + [_c_int] * 5 + [_c_void_p]),
+    "mbs_gemm_a4w4_workspace_size": (_c_size_t, [_c_int] * 3),
+    "mbs_gemm_a4w4_launch_ws": (_c_int, [_c_void_p] * 7 + [_c_int] * 5 + [_c_void_p, _c_size_t,
+                                                                           _c_void_p]),
+    "mbs_gemm_a4w4_macro_launch_ws": (_c_int, [_c_void_p] * 7 + [_c_int] * 6
+                                      + [_c_void_p, _c_size_t, _c_void_p]),
+    "mbs_quantize_mxfp4": (_c_int, [_c_void_p, _c_int, _c_int, _c_int, _c_void_p, _c_void_p, _c_int,
+                                    _c_void_p]),
+    "mbs_quantize_mxfp4_macro": (_c_int, [_c_void_p, _c_int, _c_int, _c_int, _c_void_p, _c_void_p,
+                                          _c_void_p]),
+    "mbs_shuffle_weight": (_c_int, [_c_void_p, _c_void_p, _c_int, _c_int, _c_void_p]),
+    "mbs_shuffle_scales": (_c_int, [_c_void_p, _c_void_p, _c_int, _c_int, _c_void_p]),
+    "mbs_device_error": (_c_int, [ctypes.POINTER(_c_int), _c_int]),
+}
+
+_lock = threading.Lock()
+_lib = None
+
+
+class MbsError(RuntimeError):
+    """A non-zero status from the kernel library."""
+
+    def __init__(self, func: str, status: int, name: str, detail: str):
+        super().__init__(f"{func}: {name}: {detail}" if detail else f"{func}: {name}")
+        self.status = status
+
+
+def lib() -> ctypes.CDLL:
+    """Load (once) and return the kernel library; raises if it is not built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(LIB_PATH):
+                raise RuntimeError(
+                    f"{LIB_PATH} is missing: build it with `python -m mbs_b200.build` "
+                    "(the MXFP4 operators have no non-CUDA fallback)")
+            handle = ctypes.CDLL(LIB_PATH)
+            for name, (res, args) in SIGNATURES.items():
+                fn = getattr(handle, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = handle
+    return _lib
+
+
+def check(func: str, status: int) -> None:
+    if status != 0:
+        L = lib()
+        name = L.mbs_status_string(status).decode()
+        detail = L.mbs_last_error_message().decode()
+        raise MbsError(func, status, name, detail)
+
+
+def call(func: str, *args) -> None:
+    check(func, getattr(lib(), func)(*args))

@@ -1,0 +1,164 @@
+// Status reporting, device queries and tensor-map encoding for the C ABI.
+#include "common.h"
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+namespace mbs {
+
+namespace {
+thread_local char g_msg[512] = {0};
+
+__device__ unsigned g_device_error = 0;  // sticky per-device error word
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode_fn()
+{
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+}  // namespace
+
+int fail(int status, const char* fmt, ...)
+{
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_msg, sizeof(g_msg), fmt, ap);
+    va_end(ap);
+    return status;
+}
+
+void clear_error() { g_msg[0] = 0; }
+
+int cuda_fail(cudaError_t e, const char* what)
+{
+    return fail(MBS_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+int current_device(DeviceInfo* info)
+{
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return fail(MBS_ERR_DEVICE, "no CUDA device: %s", cudaGetErrorString(e));
+    static std::mutex mu;
+    static DeviceInfo cache[64];
+    static bool have[64] = {false};
+    std::lock_guard<std::mutex> lk(mu);
+    if (dev < 0 || dev >= 64) return fail(MBS_ERR_DEVICE, "device index %d out of range", dev);
+    if (!have[dev])
+    {
+        DeviceInfo d{};
+        d.device = dev;
+        cudaDeviceGetAttribute(&d.num_sms, cudaDevAttrMultiProcessorCount, dev);
+        cudaDeviceGetAttribute(&d.cc_major, cudaDevAttrComputeCapabilityMajor, dev);
+        cudaDeviceGetAttribute(&d.cc_minor, cudaDevAttrComputeCapabilityMinor, dev);
+        int smem = 0;
+        cudaDeviceGetAttribute(&smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+        d.max_smem_optin = static_cast<size_t>(smem);
+        cache[dev] = d;
+        have[dev] = true;
+    }
+    *info = cache[dev];
+    if (info->cc_major != 10 || info->cc_minor != 0)
+        return fail(MBS_ERR_DEVICE, "device %d is sm_%d%d; this library is built for sm_100a", dev,
+                    info->cc_major, info->cc_minor);
+    return MBS_OK;
+}
+
+unsigned* device_error_word(int device)
+{
+    static std::mutex mu;
+    static unsigned* ptrs[64] = {nullptr};
+    std::lock_guard<std::mutex> lk(mu);
+    if (device < 0 || device >= 64) return nullptr;
+    if (ptrs[device] == nullptr)
+    {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_device_error) != cudaSuccess) return nullptr;
+        ptrs[device] = static_cast<unsigned*>(p);
+    }
+    return ptrs[device];
+}
+
+int encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, void* base,
+                const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
+                CUtensorMapSwizzle swizzle)
+{
+    EncodeTiledFn fn = get_encode_fn();
+    if (fn == nullptr) return fail(MBS_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+    cuuint64_t d[5];
+    cuuint64_t s[4];
+    cuuint32_t b[5];
+    cuuint32_t es[5];
+    for (int i = 0; i < rank; ++i)
+    {
+        d[i] = dims[i];
+        b[i] = box[i];
+        es[i] = 1;
+    }
+    for (int i = 0; i + 1 < rank; ++i) s[i] = strides_bytes[i];
+    CUresult r = fn(map, dtype, static_cast<cuuint32_t>(rank), base, d, s, b, es,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return fail(MBS_ERR_CUDA, "cuTensorMapEncodeTiled failed (CUresult %d, rank %d)", (int)r,
+                    rank);
+    return MBS_OK;
+}
+
+}  // namespace mbs
+
+extern "C" const char* mbs_status_string(int status)
+{
+    switch (status)
+    {
+        case MBS_OK: return "MBS_OK";
+        case MBS_ERR_INVALID_ARGUMENT: return "MBS_ERR_INVALID_ARGUMENT";
+        case MBS_ERR_UNSUPPORTED_SHAPE: return "MBS_ERR_UNSUPPORTED_SHAPE";
+        case MBS_ERR_MISALIGNED: return "MBS_ERR_MISALIGNED";
+        case MBS_ERR_CUDA: return "MBS_ERR_CUDA";
+        case MBS_ERR_WORKSPACE: return "MBS_ERR_WORKSPACE";
+        case MBS_ERR_DEVICE: return "MBS_ERR_DEVICE";
+        case MBS_ERR_DEVICE_TIMEOUT: return "MBS_ERR_DEVICE_TIMEOUT";
+        default: return "MBS_ERR_UNKNOWN";
+    }
+}
+
+extern "C" const char* mbs_last_error_message(void) { return mbs::g_msg; }
+
+extern "C" int mbs_device_error(int* code_out, int reset)
+{
+    mbs::clear_error();
+    if (code_out == nullptr) return mbs::fail(MBS_ERR_INVALID_ARGUMENT, "code_out is NULL");
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return mbs::cuda_fail(e, "cudaGetDevice");
+    e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return mbs::cuda_fail(e, "cudaDeviceSynchronize");
+    unsigned v = 0;
+    e = cudaMemcpyFromSymbol(&v, mbs::g_device_error, sizeof(v));
+    if (e != cudaSuccess) return mbs::cuda_fail(e, "cudaMemcpyFromSymbol");
+    *code_out = static_cast<int>(v);
+    if (reset)
+    {
+        unsigned z = 0;
+        e = cudaMemcpyToSymbol(mbs::g_device_error, &z, sizeof(z));
+        if (e != cudaSuccess) return mbs::cuda_fail(e, "cudaMemcpyToSymbol");
+    }
+    return MBS_OK;
+}

@@ -1,0 +1,960 @@
+// MXFP4 A4W4 GEMM for B200 (sm_100a): tcgen05.mma kind::mxf4 with e8m0
+// block scales in TMEM, TMA-fed shared-memory pipeline, warp-specialised.
+//
+// Computes out[m][n] = bf16( sum_k dq(A)[m][k] dq(B)[n][k] * f(Af[m]) f(Bf[n]) )
+// on the reference's input contract (plain row-major A, flatB-preshuffled B,
+// flatS-shuffled e8m0 scales; kernel/gemm_a4w4.hip:19-25,84-105), the
+// operation of the reference's gemm_a4w4_wg_kernel / gemm_a4w4_mfma_kernel
+// (kernel/gemm_a4w4.hip:147-250, 344-1011).
+//
+// Roles in one 384-thread CTA (one CTA per SM, persistent):
+//   warp 0      TMA producer: per K-stage (256 elements) loads the R tile
+//               (MMA operand A, 128 rows), the C tile (MMA operand B, BN rows)
+//               and both operands' raw scale bytes into one pipeline slot.
+//   warp 1      TMEM allocator; lane 0 issues tcgen05.cp (scales -> TMEM) and
+//               tcgen05.mma, and commits slot / accumulator barriers.
+//   warp 2      scale transposer: rewrites the slot's raw scales (flatS or
+//               macro-block layout) into the 32x16-byte blocks tcgen05.cp
+//               copies to TMEM (row r of a 128-row block at byte
+//               (r%32)*16 + (r/32)*4, one byte per 32-K group).
+//   warps 4-11  epilogue: tcgen05.ld the fp32 accumulator, apply the MBS
+//               factors, round to bf16 and store (or exchange stream-K partials).
+//
+// Operand roles.  Prefill (SWAP = false): R = activations A (plain rows,
+// 128-byte-swizzled K-major tiles), C = weights B (flatB core matrices,
+// no-swizzle K-major tiles).  Decode (SWAP = true, M <= 64): R = weights,
+// C = activations, so the 128-row MMA dimension walks N and the small M sits
+// in the MMA's N; the output is written transposed back to out[m][n].
+//
+// Shared-memory operand layouts the MMA reads:
+//   plain     TMA box {128 B, rows} with 128-byte swizzle: row r at r*128 B,
+//             8-row groups 1024 B apart (SBO), K step j at +32 B.
+//   preshuf   the flatB buffer viewed as a 3-D tensor {256 B block of
+//             16 rows x 16 B, row-tile (stride 8K), K chunk (stride 256)};
+//             the box lands as [K chunk][row tile][16 rows x 16 B], i.e.
+//             canonical no-swizzle K-major core matrices with
+//             SBO = 128 B (8-row groups) and LBO = rows*16 B (K chunks).
+//
+// Schedules.  Data-parallel: CTA c takes tiles c, c+G, ...  Stream-K: the
+// tiles x K-stages units are split evenly into G contiguous ranges; a tile cut
+// between CTAs is finished by the CTA holding its first K-stage (the "owner",
+// whose range ends there), which adds the fp32 partials the other CTAs (whose
+// ranges start inside the tile) left in the workspace, flagged per CTA.
+#include <cuda_bf16.h>
+
+#include <mutex>
+#include <unordered_map>
+
+#include "common.h"
+#include "ptx.cuh"
+
+namespace mbs {
+namespace gemm {
+
+constexpr int BM = 128;          // MMA M: rows of the R operand per tile
+constexpr int BK = 256;          // K elements per pipeline stage
+constexpr int BKB = BK / 2;      // bytes per row per stage
+constexpr int MMA_K = 64;        // K per tcgen05.mma kind::mxf4
+constexpr int NUM_THREADS = 384;
+constexpr int EPI_WARP0 = 4;
+constexpr int NUM_EPI_WARPS = 8;
+constexpr int NUM_EPI_THREADS = NUM_EPI_WARPS * 32;
+
+struct Params
+{
+    int M, N, K;
+    int tiles_r, tiles_c, k_stages, num_tiles;
+    int sk;                // 1: stream-K over tiles x k_stages units
+    long long sk_units;
+    const uint8_t* a_factor;
+    const uint8_t* b_factor;
+    __nv_bfloat16* out;
+    float* partials;       // [G][BN][BM] fp32, stream-K only
+    unsigned* flags;       // [G], stream-K only; zero between launches
+    unsigned* err;         // sticky device error word
+};
+
+constexpr int align_up(int x, int a) { return (x + a - 1) / a * a; }
+
+template <int BN_, bool SWAP_, bool W_MACRO_, int STAGES_>
+struct Cfg
+{
+    static constexpr int BN = BN_;
+    static constexpr bool SWAP = SWAP_;
+    static constexpr int STAGES = STAGES_;
+    static constexpr bool R_PRESHUF = SWAP;   // weights are the preshuffled operand
+    static constexpr bool C_PRESHUF = !SWAP;
+    static constexpr bool R_MACRO = SWAP && W_MACRO_;
+    static constexpr bool C_MACRO = !SWAP && W_MACRO_;
+    static constexpr int C_RB = BN >= 128 ? BN / 128 : 1;  // 128-row scale blocks of C
+
+    static constexpr int R_DATA = BM * BKB;
+    static constexpr int C_DATA = BN * BKB;
+    static constexpr int R_RAW = R_MACRO ? (BM / 32) * 16 : (BM / 32) * 256;
+    static constexpr int C_RAW = C_MACRO ? (BN / 32) * 16 : (BN / 32) * 256;
+    static constexpr int R_ATOM = 2 * 512;
+    static constexpr int C_ATOM = 2 * C_RB * 512;
+
+    static constexpr int R_DATA_OFF = 0;
+    static constexpr int C_DATA_OFF = R_DATA_OFF + R_DATA;
+    static constexpr int R_RAW_OFF = C_DATA_OFF + C_DATA;
+    static constexpr int C_RAW_OFF = R_RAW_OFF + align_up(R_RAW, 128);
+    static constexpr int R_ATOM_OFF = C_RAW_OFF + align_up(C_RAW, 128);
+    static constexpr int C_ATOM_OFF = R_ATOM_OFF + R_ATOM;
+    static constexpr int STAGE_BYTES = align_up(C_ATOM_OFF + C_ATOM, 1024);
+    static constexpr uint32_t TX_BYTES = R_DATA + C_DATA + R_RAW + C_RAW;
+
+    static constexpr int SF_STAGE_COLS = 8 + 8 * C_RB;
+    static constexpr int ACC_BUFS = (2 * BN + STAGES * SF_STAGE_COLS <= 512) ? 2 : 1;
+    static constexpr int SF_BASE = ACC_BUFS * BN;
+    static constexpr int TMEM_NEED = SF_BASE + STAGES * SF_STAGE_COLS;
+    static constexpr int TMEM_COLS =
+        TMEM_NEED <= 32 ? 32 : TMEM_NEED <= 64 ? 64 : TMEM_NEED <= 128 ? 128 : TMEM_NEED <= 256 ? 256 : 512;
+    static_assert(TMEM_NEED <= 512, "TMEM budget");
+
+    // barriers: full, sfready, empty [STAGES]; acc_full, acc_empty [2]; tmem slot; abort
+    static constexpr int BAR_BYTES = (3 * STAGES + 4) * 8 + 16;
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + 1024;  // +1024 alignment slack
+    static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+    static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN");
+};
+
+// ------------------------------------------------------------------ schedule
+struct Work
+{
+    int tile, k0, k1;
+};
+
+__device__ __forceinline__ long long sk_start(const Params& p, int c)
+{
+    return (long long)c * p.sk_units / gridDim.x;
+}
+
+// idx-th work item of this CTA; false when exhausted.
+__device__ __forceinline__ bool get_work(const Params& p, int idx, Work& w)
+{
+    if (!p.sk)
+    {
+        const long long t = (long long)blockIdx.x + (long long)idx * gridDim.x;
+        if (t >= p.num_tiles) return false;
+        w.tile = (int)t;
+        w.k0 = 0;
+        w.k1 = p.k_stages;
+        return true;
+    }
+    const long long s = sk_start(p, blockIdx.x);
+    const long long e = sk_start(p, blockIdx.x + 1);
+    const int ks = p.k_stages;
+    const long long t0 = s / ks;
+    if (idx == 0)
+    {
+        if (s >= e) return false;
+        w.tile = (int)t0;
+        w.k0 = (int)(s - t0 * ks);
+        w.k1 = (int)(w.k0 + (e - s) < ks ? w.k0 + (e - s) : ks);
+        return true;
+    }
+    const long long u = (t0 + idx) * ks;
+    if (u >= e) return false;
+    w.tile = (int)(t0 + idx);
+    w.k0 = 0;
+    w.k1 = (int)(e - u < ks ? e - u : ks);
+    return true;
+}
+
+__device__ __forceinline__ void raise_error(const Params& p, volatile int* abort_flag)
+{
+    *abort_flag = 1;
+    atomicExch(p.err, (unsigned)MBS_ERR_DEVICE_TIMEOUT);
+}
+
+// f(b) = 1 / (1 + b/256): b fills the top 8 mantissa bits of 1.0f; the
+// reciprocal is IEEE round-to-nearest (test_gemm_a4w4.py:47-51).
+__device__ __forceinline__ float byte_to_factor(uint32_t b)
+{
+    return __frcp_rn(__uint_as_float(0x3F800000u | (b << 15)));
+}
+
+// One operand's raw scale bytes for one K-stage (8 groups of 32 K) ->
+// tcgen05.cp source blocks.  Output block (q, rb) covers rows 128*rb ..
+// 128*rb+127 and K-groups 4q .. 4q+3 of the stage: 512 B with row r's four
+// scale bytes at (r%32)*16 + ((r%128)/32)*4.
+//   flatS input (kernel/gemm_a4w4.hip:97-105): per 32-row group g one 256 B
+//     chunk, scale (r, b) at (b%4)*64 + (r%16)*4 + ((b/4)%2)*2 + (r%32)/16.
+//     For fixed (g, r%16) the four words at (b%4)*64 hold, in byte p =
+//     2*(b/4) + (r%32)/16, the scales of rows r and r+16 for both groups of
+//     4: a 4x4 byte transpose gives the four output words.
+//   macro input: per 32-row group 16 bytes covering 16 K-groups; this
+//     stage's 8 start at byte 8*(ks&1); every row of the group shares them.
+template <int ROWS, bool MACRO>
+__device__ __forceinline__ void transpose_side(const uint8_t* raw, uint8_t* atoms, int ks, int lane)
+{
+    constexpr int RB = ROWS >= 128 ? ROWS / 128 : 1;
+    if constexpr (!MACRO)
+    {
+        const uint32_t* raw32 = reinterpret_cast<const uint32_t*>(raw);
+        constexpr int OPS = (ROWS / 32) * 16;
+#pragma unroll
+        for (int op = lane; op < OPS; op += 32)
+        {
+            const int g = op >> 4, rho = op & 15;
+            const uint32_t w0 = raw32[g * 64 + rho];
+            const uint32_t w1 = raw32[g * 64 + 16 + rho];
+            const uint32_t w2 = raw32[g * 64 + 32 + rho];
+            const uint32_t w3 = raw32[g * 64 + 48 + rho];
+            const uint32_t t0 = __byte_perm(w0, w1, 0x5140);
+            const uint32_t t1 = __byte_perm(w2, w3, 0x5140);
+            const uint32_t t2 = __byte_perm(w0, w1, 0x7362);
+            const uint32_t t3 = __byte_perm(w2, w3, 0x7362);
+            const uint32_t o[4] = {__byte_perm(t0, t1, 0x5410), __byte_perm(t0, t1, 0x7632),
+                                   __byte_perm(t2, t3, 0x5410), __byte_perm(t2, t3, 0x7632)};
+#pragma unroll
+            for (int pp = 0; pp < 4; ++pp)
+            {
+                const int r = 32 * g + 16 * (pp & 1) + rho;
+                const int q = pp >> 1;
+                *reinterpret_cast<uint32_t*>(atoms + (q * RB + (r >> 7)) * 512 + (r & 31) * 16 +
+                                             ((r >> 5) & 3) * 4) = o[pp];
+            }
+        }
+    }
+    else
+    {
+        constexpr int OPS = ROWS * 2;
+#pragma unroll
+        for (int op = lane; op < OPS; op += 32)
+        {
+            const int r = op >> 1, q = op & 1;
+            const uint32_t v =
+                *reinterpret_cast<const uint32_t*>(raw + (r >> 5) * 16 + 8 * (ks & 1) + 4 * q);
+            *reinterpret_cast<uint32_t*>(atoms + (q * RB + (r >> 7)) * 512 + (r & 31) * 16 +
+                                         ((r >> 5) & 3) * 4) = v;
+        }
+    }
+}
+
+// ------------------------------------------------------------------ kernel
+template <class CF>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    mxf4_gemm_kernel(const __grid_constant__ CUtensorMap tm_r, const __grid_constant__ CUtensorMap tm_c,
+                     const __grid_constant__ CUtensorMap tm_rsf, const __grid_constant__ CUtensorMap tm_csf,
+                     const Params p)
+{
+    constexpr int BN = CF::BN;
+    constexpr int STAGES = CF::STAGES;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~static_cast<uintptr_t>(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * CF::STAGE_BYTES);
+    uint64_t* sfready = full + STAGES;
+    uint64_t* empty = sfready + STAGES;
+    uint64_t* acc_full = empty + STAGES;
+    uint64_t* acc_empty = acc_full + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0)
+    {
+        for (int s = 0; s < STAGES; ++s)
+        {
+            mbar_init(&full[s], 1);
+            mbar_init(&sfready[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b)
+        {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], NUM_EPI_WARPS);
+        }
+        *abort_flag = 0;
+        fence_mbar_init();
+        prefetch_tmap(&tm_r);
+        prefetch_tmap(&tm_c);
+        prefetch_tmap(&tm_rsf);
+        prefetch_tmap(&tm_csf);
+    }
+    if (warp == 1)
+    {
+        tmem_alloc(tmem_slot, CF::TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0)
+    {
+        // ------------------------------------------------ TMA producer
+        if (lane == 0)
+        {
+            int slot = 0;
+            uint32_t phase = 0;
+            Work w;
+            for (int i = 0; get_work(p, i, w); ++i)
+            {
+                const int tr = w.tile % p.tiles_r, tc = w.tile / p.tiles_r;
+                const int r0 = tr * BM, c0 = tc * BN;
+                for (int ks = w.k0; ks < w.k1; ++ks)
+                {
+                    if (!mbar_wait(&empty[slot], phase ^ 1, abort_flag))
+                    {
+                        raise_error(p, abort_flag);
+                        goto producer_done;
+                    }
+                    uint8_t* st = smem + slot * CF::STAGE_BYTES;
+                    mbar_arrive_expect_tx(&full[slot], CF::TX_BYTES);
+                    if (CF::R_PRESHUF)
+                        tma_load_3d(st + CF::R_DATA_OFF, &tm_r, &full[slot], 0, r0 / 16, ks * 8);
+                    else
+                        tma_load_2d(st + CF::R_DATA_OFF, &tm_r, &full[slot], ks * BKB, r0);
+                    if (CF::C_PRESHUF)
+                        tma_load_3d(st + CF::C_DATA_OFF, &tm_c, &full[slot], 0, c0 / 16, ks * 8);
+                    else
+                        tma_load_2d(st + CF::C_DATA_OFF, &tm_c, &full[slot], ks * BKB, c0);
+                    if (CF::R_MACRO)
+                        tma_load_2d(st + CF::R_RAW_OFF, &tm_rsf, &full[slot], 16 * (ks >> 1), r0 / 32);
+                    else
+                        tma_load_3d(st + CF::R_RAW_OFF, &tm_rsf, &full[slot], 0, ks, r0 / 32);
+                    if (CF::C_MACRO)
+                        tma_load_2d(st + CF::C_RAW_OFF, &tm_csf, &full[slot], 16 * (ks >> 1), c0 / 32);
+                    else
+                        tma_load_3d(st + CF::C_RAW_OFF, &tm_csf, &full[slot], 0, ks, c0 / 32);
+                    if (++slot == STAGES)
+                    {
+                        slot = 0;
+                        phase ^= 1;
+                    }
+                }
+            }
+        producer_done:;
+        }
+    }
+    else if (warp == 1)
+    {
+        // ------------------------------------------------ MMA issuer
+        if (lane == 0)
+        {
+            int slot = 0;
+            uint32_t phase = 0;
+            int acc = 0;
+            uint32_t acc_phase = 0;
+            Work w;
+            for (int i = 0; get_work(p, i, w); ++i)
+            {
+                if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, abort_flag))
+                {
+                    raise_error(p, abort_flag);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + acc * BN;
+                bool ok = true;
+                for (int ks = w.k0; ks < w.k1; ++ks)
+                {
+                    if (!mbar_wait(&full[slot], phase, abort_flag) ||
+                        !mbar_wait(&sfready[slot], phase, abort_flag))
+                    {
+                        raise_error(p, abort_flag);
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint8_t* st = smem + slot * CF::STAGE_BYTES;
+                    const uint32_t sf_r = tmem_base + CF::SF_BASE + slot * CF::SF_STAGE_COLS;
+                    const uint32_t sf_c = sf_r + 8;
+                    // scales: shared memory -> TMEM (32 rows x 16 B per block, x4 sub-partitions)
+#pragma unroll
+                    for (int q = 0; q < 2; ++q)
+                        tc_cp_32x128b_warpx4(sf_r + 4 * q,
+                                             make_smem_desc(smem_u32(st + CF::R_ATOM_OFF + q * 512), 0, 128, 0));
+#pragma unroll
+                    for (int a = 0; a < 2 * CF::C_RB; ++a)
+                        tc_cp_32x128b_warpx4(sf_c + 4 * a,
+                                             make_smem_desc(smem_u32(st + CF::C_ATOM_OFF + a * 512), 0, 128, 0));
+                    const uint32_t r_base = smem_u32(st + CF::R_DATA_OFF);
+                    const uint32_t c_base = smem_u32(st + CF::C_DATA_OFF);
+#pragma unroll
+                    for (int j = 0; j < BK / MMA_K; ++j)
+                    {
+                        if (ks * BK + j * MMA_K >= p.K) break;
+                        const uint64_t a_desc =
+                            CF::R_PRESHUF ? make_smem_desc(r_base + j * 2 * (BM * 16), BM * 16, 128, 0)
+                                          : make_smem_desc(r_base + j * 32, 16, 1024, 2);
+                        const uint64_t b_desc =
+                            CF::C_PRESHUF ? make_smem_desc(c_base + j * 2 * (BN * 16), BN * 16, 128, 0)
+                                          : make_smem_desc(c_base + j * 32, 16, 1024, 2);
+                        const uint32_t id = (uint32_t)(j & 1) * 2;  // byte of the 32-bit scale column
+                        const uint32_t q = (uint32_t)(j >> 1);      // which 4-group scale block
+                        const uint32_t sfa = (sf_r + 4 * q) | (id << 30);
+                        const uint32_t sfb = (sf_c + 4 * CF::C_RB * q) | (id << 30);
+                        tc_mma_mxf4(d_tmem, a_desc, b_desc, make_idesc_mxf4(BM, BN, id, id), sfa, sfb,
+                                    (ks > w.k0 || j > 0) ? 1u : 0u);
+                    }
+                    tc_commit(&empty[slot]);
+                    if (++slot == STAGES)
+                    {
+                        slot = 0;
+                        phase ^= 1;
+                    }
+                }
+                if (!ok) break;
+                tc_commit(&acc_full[acc]);
+                if (CF::ACC_BUFS == 2)
+                {
+                    acc ^= 1;
+                    if (acc == 0) acc_phase ^= 1;
+                }
+                else
+                {
+                    acc_phase ^= 1;
+                }
+            }
+        }
+    }
+    else if (warp == 2)
+    {
+        // ------------------------------------------------ scale transposer
+        int slot = 0;
+        uint32_t phase = 0;
+        Work w;
+        for (int i = 0; get_work(p, i, w); ++i)
+        {
+            bool ok = true;
+            for (int ks = w.k0; ks < w.k1; ++ks)
+            {
+                if (!mbar_wait(&full[slot], phase, abort_flag))
+                {
+                    if (lane == 0) raise_error(p, abort_flag);
+                    ok = false;
+                    break;
+                }
+                uint8_t* st = smem + slot * CF::STAGE_BYTES;
+                // R side: 128 rows, one 128-row block, 2 scale groups of 4.
+                transpose_side<BM, CF::R_MACRO>(st + CF::R_RAW_OFF, st + CF::R_ATOM_OFF, ks, lane);
+                transpose_side<BN, CF::C_MACRO>(st + CF::C_RAW_OFF, st + CF::C_ATOM_OFF, ks, lane);
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&sfready[slot]);
+                if (++slot == STAGES)
+                {
+                    slot = 0;
+                    phase ^= 1;
+                }
+            }
+            if (!ok) break;
+        }
+    }
+    else if (warp >= EPI_WARP0)
+    {
+        // ------------------------------------------------ epilogue
+        const int e = warp - EPI_WARP0;
+        const int quarter = warp & 3;         // TMEM lanes [32*quarter, 32*quarter + 32)
+        const int half = e >> 2;              // which half of the BN columns
+        const int row = quarter * 32 + lane;  // accumulator row (TMEM lane)
+        constexpr int COLS = BN / 2;
+        const bool has_factor = (p.a_factor != nullptr) || (p.b_factor != nullptr);
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        Work w;
+        for (int i = 0; get_work(p, i, w); ++i)
+        {
+            if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag))
+            {
+                if (lane == 0) raise_error(p, abort_flag);
+                break;
+            }
+            tc_fence_after();
+            const int tr = w.tile % p.tiles_r, tc = w.tile / p.tiles_r;
+            const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN + half * COLS;
+            const bool nonowner = p.sk && w.k0 > 0;
+            const bool owner = p.sk && w.k0 == 0 && w.k1 < p.k_stages;
+            if (nonowner)
+            {
+                float* part = p.partials + (size_t)blockIdx.x * (BM * BN);
+#pragma unroll 1
+                for (int c = 0; c < COLS; c += 16)
+                {
+                    uint32_t v[16];
+                    tc_ld_32x32b_x16(taddr + c, v);
+                    tc_wait_ld();
+#pragma unroll
+                    for (int t = 0; t < 16; ++t)
+                        __stcg(part + (size_t)(half * COLS + c + t) * BM + row, __uint_as_float(v[t]));
+                }
+                __threadfence();
+                named_bar_sync(1, NUM_EPI_THREADS);
+                if (threadIdx.x == EPI_WARP0 * 32) st_release_gpu(&p.flags[blockIdx.x], 1u);
+            }
+            else
+            {
+                int c_first = 0, c_last = -1;  // contributing CTAs [c_first, c_last]
+                if (owner)
+                {
+                    const long long tile_end = (long long)(w.tile + 1) * p.k_stages;
+                    c_first = blockIdx.x + 1;
+                    c_last = blockIdx.x;
+                    while (c_last + 1 < (int)gridDim.x && sk_start(p, c_last + 1) < tile_end) ++c_last;
+                    if (threadIdx.x == EPI_WARP0 * 32)
+                    {
+                        const unsigned long long t0 = globaltimer_ns();
+                        for (int c = c_first; c <= c_last; ++c)
+                        {
+                            while (ld_acquire_gpu(&p.flags[c]) == 0u)
+                            {
+                                if (*abort_flag || globaltimer_ns() - t0 > kWaitTimeoutNs)
+                                {
+                                    raise_error(p, abort_flag);
+                                    break;
+                                }
+                            }
+                        }
+                    }
+                    named_bar_sync(1, NUM_EPI_THREADS);
+                }
+#pragma unroll 1
+                for (int c = 0; c < COLS; c += 16)
+                {
+                    uint32_t v[16];
+                    tc_ld_32x32b_x16(taddr + c, v);
+                    tc_wait_ld();
+                    float x[16];
+#pragma unroll
+                    for (int t = 0; t < 16; ++t) x[t] = __uint_as_float(v[t]);
+                    for (int cc = c_first; cc <= c_last; ++cc)
+                    {
+                        const float* part = p.partials + (size_t)cc * (BM * BN);
+#pragma unroll
+                        for (int t = 0; t < 16; ++t)
+                            x[t] += __ldcg(part + (size_t)(half * COLS + c + t) * BM + row);
+                    }
+                    if (!CF::SWAP)
+                    {
+                        const int m = tr * BM + row;
+                        const int n = tc * BN + half * COLS + c;
+                        if (m < p.M && n < p.N)
+                        {
+                            if (has_factor)
+                            {
+                                const float fa = p.a_factor ? byte_to_factor(p.a_factor[m]) : 1.0f;
+#pragma unroll
+                                for (int t = 0; t < 16; ++t)
+                                {
+                                    const float fb = p.b_factor ? byte_to_factor(p.b_factor[n + t]) : 1.0f;
+                                    x[t] = __fmul_rn(x[t], __fmul_rn(fa, fb));
+                                }
+                            }
+                            uint32_t packed[8];
+#pragma unroll
+                            for (int t = 0; t < 8; ++t)
+                            {
+                                __nv_bfloat162 h = __floats2bfloat162_rn(x[2 * t], x[2 * t + 1]);
+                                packed[t] = *reinterpret_cast<uint32_t*>(&h);
+                            }
+                            uint4* dst = reinterpret_cast<uint4*>(p.out + (size_t)m * p.N + n);
+                            dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+                            dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+                        }
+                    }
+                    else
+                    {
+                        const int n = tr * BM + row;
+                        if (n < p.N)
+                        {
+                            const float fb = p.b_factor ? byte_to_factor(p.b_factor[n]) : 1.0f;
+#pragma unroll
+                            for (int t = 0; t < 16; ++t)
+                            {
+                                const int m = tc * BN + half * COLS + c + t;
+                                if (m < p.M)
+                                {
+                                    float y = x[t];
+                                    if (has_factor)
+                                    {
+                                        const float fa = p.a_factor ? byte_to_factor(p.a_factor[m]) : 1.0f;
+                                        y = __fmul_rn(y, __fmul_rn(fa, fb));
+                                    }
+                                    p.out[(size_t)m * p.N + n] = __float2bfloat16_rn(y);
+                                }
+                            }
+                        }
+                    }
+                }
+                if (owner)
+                {
+                    named_bar_sync(1, NUM_EPI_THREADS);
+                    if (threadIdx.x == EPI_WARP0 * 32)
+                        for (int c = c_first; c <= c_last; ++c) p.flags[c] = 0u;
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[acc]);
+            if (CF::ACC_BUFS == 2)
+            {
+                acc ^= 1;
+                if (acc == 0) acc_phase ^= 1;
+            }
+            else
+            {
+                acc_phase ^= 1;
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc(tmem_base, CF::TMEM_COLS);
+}
+
+}  // namespace gemm
+}  // namespace mbs
+
+// ====================================================================== host
+namespace mbs {
+namespace gemm {
+namespace {
+
+struct Problem
+{
+    const uint8_t *A, *B, *AS, *BS, *AF, *BF;
+    void* out;
+    int M, N, K, Mpad, snp, mb_ld;
+    bool macro;
+};
+
+struct Plan
+{
+    int bn;
+    bool swap, sk;
+    int G, tiles_r, tiles_c, k_stages;
+    size_t ws_bytes;
+};
+
+int env_int(const char* name, int dflt)
+{
+    const char* v = getenv(name);
+    return (v != nullptr && *v != 0) ? atoi(v) : dflt;
+}
+
+// Path and schedule choice.  Skinny M (decode) swaps the operands so the
+// weights fill the 128-row MMA dimension; small tile counts use stream-K so
+// every SM streams an equal share of the K work.
+//   MBS_FORCE_SCHEDULE=1 (stream-K) / 2 (data-parallel), MBS_FORCE_GRID=<G>:
+//   debug overrides used by the tests to reach every schedule on small shapes.
+Plan make_plan(int M, int N, int K, int num_sms)
+{
+    Plan pl{};
+    pl.swap = M <= 64;
+    pl.bn = pl.swap ? (M <= 32 ? 32 : 64) : 256;
+    pl.k_stages = (K + BK - 1) / BK;
+    if (pl.swap)
+    {
+        pl.tiles_r = (N + BM - 1) / BM;
+        pl.tiles_c = (M + pl.bn - 1) / pl.bn;
+    }
+    else
+    {
+        pl.tiles_r = (M + BM - 1) / BM;
+        pl.tiles_c = (N + pl.bn - 1) / pl.bn;
+    }
+    const long long tiles = (long long)pl.tiles_r * pl.tiles_c;
+    pl.sk = pl.swap || tiles < 2LL * num_sms;
+    const int force = env_int("MBS_FORCE_SCHEDULE", 0);
+    if (force == 1) pl.sk = true;
+    if (force == 2) pl.sk = false;
+    int G = num_sms;
+    const int fg = env_int("MBS_FORCE_GRID", 0);
+    if (fg > 0 && fg < G) G = fg;
+    const long long units = pl.sk ? tiles * pl.k_stages : tiles;
+    pl.G = (int)(units < G ? units : G);
+    pl.ws_bytes = pl.sk ? (size_t)pl.G * BM * pl.bn * sizeof(float) + (size_t)align_up(pl.G * 4, 256)
+                        : 0;
+    return pl;
+}
+
+int validate(const Problem& pb)
+{
+    if (!pb.A || !pb.B || !pb.AS || !pb.BS || !pb.out)
+        return fail(MBS_ERR_INVALID_ARGUMENT, "gemm_a4w4: A, B, scales and out must be non-NULL");
+    if (pb.M <= 0 || pb.N <= 0 || pb.K <= 0)
+        return fail(MBS_ERR_INVALID_ARGUMENT, "gemm_a4w4: M, N, K must be positive (M=%d N=%d K=%d)",
+                    pb.M, pb.N, pb.K);
+    if (pb.N % 16 != 0)
+        return fail(MBS_ERR_UNSUPPORTED_SHAPE, "gemm_a4w4: N must be a multiple of 16, got %d", pb.N);
+    if (pb.K % 64 != 0)
+        return fail(MBS_ERR_UNSUPPORTED_SHAPE,
+                    "gemm_a4w4: K must be a multiple of 64 (whole preshuffle K tiles), got %d", pb.K);
+    if (pb.M > (1 << 30) || pb.N > (1 << 30) || pb.K > (1 << 24))
+        return fail(MBS_ERR_UNSUPPORTED_SHAPE, "gemm_a4w4: problem too large");
+    if (pb.Mpad < pb.M || pb.Mpad % 32 != 0)
+        return fail(MBS_ERR_INVALID_ARGUMENT, "gemm_a4w4: Mpad (%d) must be a multiple of 32 >= M (%d)",
+                    pb.Mpad, pb.M);
+    if (pb.snp % 8 != 0 || pb.snp < pb.K / 32)
+        return fail(MBS_ERR_INVALID_ARGUMENT,
+                    "gemm_a4w4: scaleN_pad (%d) must be a multiple of 8 >= K/32 (%d)", pb.snp, pb.K / 32);
+    if (pb.macro && (pb.mb_ld % 16 != 0 || pb.mb_ld < pb.K / 32))
+        return fail(MBS_ERR_INVALID_ARGUMENT, "gemm_a4w4: mb_ld (%d) must be a multiple of 16 >= K/32",
+                    pb.mb_ld);
+    if (!aligned16(pb.A) || !aligned16(pb.B) || !aligned16(pb.AS) || !aligned16(pb.BS) ||
+        !aligned16(pb.out))
+        return fail(MBS_ERR_MISALIGNED, "gemm_a4w4: A, B, scales and out must be 16-byte aligned");
+    return MBS_OK;
+}
+
+// TMA descriptors for the four operands of one launch.
+int make_maps(const Problem& pb, const Plan& pl, CUtensorMap* tm_r, CUtensorMap* tm_c,
+              CUtensorMap* tm_rsf, CUtensorMap* tm_csf)
+{
+    const int r_rows = BM, c_rows = pl.bn;
+    const int act_rows = pl.swap ? c_rows : r_rows;
+    const int w_rows = pl.swap ? r_rows : c_rows;
+    CUtensorMap* act_map = pl.swap ? tm_c : tm_r;
+    CUtensorMap* w_map = pl.swap ? tm_r : tm_c;
+    CUtensorMap* act_sf = pl.swap ? tm_csf : tm_rsf;
+    CUtensorMap* w_sf = pl.swap ? tm_rsf : tm_csf;
+    const uint64_t Kp = (uint64_t)pb.K / 2;
+    int st;
+    {  // activations: plain [M, K/2], 128-byte swizzled boxes of {128 B, rows}
+        const uint64_t dims[2] = {Kp, (uint64_t)pb.M};
+        const uint64_t strides[1] = {Kp};
+        const uint32_t box[2] = {BKB, (uint32_t)act_rows};
+        st = encode_tmap(act_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, (void*)pb.A, dims, strides, box,
+                         CU_TENSOR_MAP_SWIZZLE_128B);
+        if (st) return st;
+    }
+    {  // weights: flatB as {256 B block, row tile (16 rows), K chunk (16 B)}
+        const uint64_t dims[3] = {256, (uint64_t)pb.N / 16, (uint64_t)pb.K / 32};
+        const uint64_t strides[2] = {(uint64_t)pb.K * 8, 256};
+        const uint32_t box[3] = {256, (uint32_t)w_rows / 16, BK / 32};
+        st = encode_tmap(w_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, (void*)pb.B, dims, strides, box,
+                         CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (st) return st;
+    }
+    {  // activation scales: flatS as {256 B chunk, K-stage, 32-row group}
+        const uint64_t dims[3] = {256, (uint64_t)pb.snp / 8, (uint64_t)pb.Mpad / 32};
+        const uint64_t strides[2] = {256, (uint64_t)pb.snp * 32};
+        const uint32_t box[3] = {256, 1, (uint32_t)act_rows / 32};
+        st = encode_tmap(act_sf, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, (void*)pb.AS, dims, strides, box,
+                         CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (st) return st;
+    }
+    if (!pb.macro)
+    {  // weight scales: flatS, roundup(N,32) rows
+        const uint64_t dims[3] = {256, (uint64_t)pb.snp / 8, (uint64_t)(pb.N + 31) / 32};
+        const uint64_t strides[2] = {256, (uint64_t)pb.snp * 32};
+        const uint32_t box[3] = {256, 1, (uint32_t)w_rows / 32};
+        st = encode_tmap(w_sf, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, (void*)pb.BS, dims, strides, box,
+                         CU_TENSOR_MAP_SWIZZLE_NONE);
+    }
+    else
+    {  // weight macro scales: [ceil(N/32), mb_ld], boxes of {16 K-groups, row groups}
+        const uint64_t dims[2] = {(uint64_t)pb.mb_ld, (uint64_t)(pb.N + 31) / 32};
+        const uint64_t strides[1] = {(uint64_t)pb.mb_ld};
+        const uint32_t box[2] = {16, (uint32_t)w_rows / 32};
+        st = encode_tmap(w_sf, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, (void*)pb.BS, dims, strides, box,
+                         CU_TENSOR_MAP_SWIZZLE_NONE);
+    }
+    return st;
+}
+
+template <class CF>
+int launch_cfg(const Problem& pb, const Plan& pl, const DeviceInfo& dev, void* ws, cudaStream_t stream)
+{
+    static bool attr_done[64] = {false};
+    static std::mutex mu;
+    auto kernel = mxf4_gemm_kernel<CF>;
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        if (!attr_done[dev.device])
+        {
+            cudaError_t e =
+                cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, CF::SMEM_BYTES);
+            if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
+            attr_done[dev.device] = true;
+        }
+    }
+    CUtensorMap tm_r, tm_c, tm_rsf, tm_csf;
+    int st = make_maps(pb, pl, &tm_r, &tm_c, &tm_rsf, &tm_csf);
+    if (st) return st;
+    Params p{};
+    p.M = pb.M;
+    p.N = pb.N;
+    p.K = pb.K;
+    p.tiles_r = pl.tiles_r;
+    p.tiles_c = pl.tiles_c;
+    p.k_stages = pl.k_stages;
+    p.num_tiles = pl.tiles_r * pl.tiles_c;
+    p.sk = pl.sk ? 1 : 0;
+    p.sk_units = (long long)p.num_tiles * pl.k_stages;
+    p.a_factor = pb.AF;
+    p.b_factor = pb.BF;
+    p.out = static_cast<__nv_bfloat16*>(pb.out);
+    if (pl.sk)
+    {
+        p.partials = static_cast<float*>(ws);
+        p.flags = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(ws) + (size_t)pl.G * BM * pl.bn * 4);
+    }
+    p.err = device_error_word(dev.device);
+    if (p.err == nullptr) return fail(MBS_ERR_CUDA, "device error word unavailable");
+
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(pl.G);
+    cfg.blockDim = dim3(NUM_THREADS);
+    cfg.dynamicSmemBytes = CF::SMEM_BYTES;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;  // stream-K owners wait on other CTAs
+    attr[0].val.cooperative = pl.sk ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, tm_r, tm_c, tm_rsf, tm_csf, p);
+    if (e != cudaSuccess) return cuda_fail(e, "gemm launch");
+    return MBS_OK;
+}
+
+int dispatch(const Problem& pb, const Plan& pl, const DeviceInfo& dev, void* ws, cudaStream_t s)
+{
+    if (pl.swap)
+    {
+        if (pl.bn == 32)
+            return pb.macro ? launch_cfg<Cfg<32, true, true, 8>>(pb, pl, dev, ws, s)
+                            : launch_cfg<Cfg<32, true, false, 8>>(pb, pl, dev, ws, s);
+        return pb.macro ? launch_cfg<Cfg<64, true, true, 8>>(pb, pl, dev, ws, s)
+                        : launch_cfg<Cfg<64, true, false, 8>>(pb, pl, dev, ws, s);
+    }
+    return pb.macro ? launch_cfg<Cfg<256, false, true, 4>>(pb, pl, dev, ws, s)
+                    : launch_cfg<Cfg<256, false, false, 4>>(pb, pl, dev, ws, s);
+}
+
+// Library-owned stream-K scratch, one zero-filled buffer per (device, stream).
+void* internal_workspace(int device, cudaStream_t stream, size_t bytes, int* status)
+{
+    struct Buf
+    {
+        void* ptr;
+        size_t bytes;
+    };
+    static std::mutex mu;
+    static std::unordered_map<unsigned long long, Buf> bufs;
+    std::lock_guard<std::mutex> lk(mu);
+    const unsigned long long key = (reinterpret_cast<uintptr_t>(stream) << 8) ^ (unsigned)device;
+    Buf& b = bufs[key];
+    if (b.bytes >= bytes && b.ptr != nullptr) return b.ptr;
+    cudaError_t e;
+    if (b.ptr != nullptr)
+    {
+        e = cudaStreamSynchronize(stream);
+        if (e != cudaSuccess)
+        {
+            *status = cuda_fail(e, "cudaStreamSynchronize (workspace growth)");
+            return nullptr;
+        }
+        cudaFree(b.ptr);
+        b.ptr = nullptr;
+        b.bytes = 0;
+    }
+    const size_t want = bytes < (size_t)4 << 20 ? (size_t)4 << 20 : bytes;
+    e = cudaMalloc(&b.ptr, want);
+    if (e != cudaSuccess)
+    {
+        b.ptr = nullptr;
+        *status = cuda_fail(e, "cudaMalloc (gemm workspace)");
+        return nullptr;
+    }
+    e = cudaMemsetAsync(b.ptr, 0, want, stream);
+    if (e != cudaSuccess)
+    {
+        *status = cuda_fail(e, "cudaMemsetAsync (gemm workspace)");
+        return nullptr;
+    }
+    b.bytes = want;
+    return b.ptr;
+}
+
+int run(const Problem& pb, void* ws, size_t ws_bytes, bool internal_ws, cudaStream_t stream)
+{
+    int st = validate(pb);
+    if (st) return st;
+    DeviceInfo dev;
+    st = current_device(&dev);
+    if (st) return st;
+    const Plan pl = make_plan(pb.M, pb.N, pb.K, dev.num_sms);
+    if (pl.ws_bytes > 0)
+    {
+        if (internal_ws)
+        {
+            ws = internal_workspace(dev.device, stream, pl.ws_bytes, &st);
+            if (ws == nullptr) return st;
+        }
+        else
+        {
+            if (ws == nullptr || ws_bytes < pl.ws_bytes)
+                return fail(MBS_ERR_WORKSPACE, "gemm_a4w4: workspace of %zu bytes needed, %zu given",
+                            pl.ws_bytes, ws == nullptr ? (size_t)0 : ws_bytes);
+            if ((reinterpret_cast<uintptr_t>(ws) & 255u) != 0)
+                return fail(MBS_ERR_MISALIGNED, "gemm_a4w4: workspace must be 256-byte aligned");
+        }
+    }
+    return dispatch(pb, pl, dev, ws, stream);
+}
+
+}  // namespace
+}  // namespace gemm
+}  // namespace mbs
+
+using mbs::gemm::Problem;
+
+extern "C" int gemm_a4w4_mxfp4_launch(const uint8_t* A, const uint8_t* B, const uint8_t* AScale,
+                                      const uint8_t* BScale, const uint8_t* AFactor,
+                                      const uint8_t* BFactor, void* out, int M, int N, int K, int Mpad,
+                                      int scaleN_pad, void* stream)
+{
+    mbs::clear_error();
+    Problem pb{A, B, AScale, BScale, AFactor, BFactor, out, M, N, K, Mpad, scaleN_pad, 0, false};
+    return mbs::gemm::run(pb, nullptr, 0, true, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" size_t mbs_gemm_a4w4_workspace_size(int M, int N, int K)
+{
+    int num_sms = 148;
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess)
+    {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && n > 0)
+            num_sms = n;
+    }
+    else
+    {
+        cudaGetLastError();
+    }
+    if (M <= 0 || N <= 0 || K <= 0) return 0;
+    return mbs::gemm::make_plan(M, N, K, num_sms).ws_bytes;
+}
+
+extern "C" int mbs_gemm_a4w4_launch_ws(const uint8_t* A, const uint8_t* B, const uint8_t* AScale,
+                                       const uint8_t* BScale, const uint8_t* AFactor,
+                                       const uint8_t* BFactor, void* out, int M, int N, int K,
+                                       int Mpad, int scaleN_pad, void* workspace,
+                                       size_t workspace_bytes, void* stream)
+{
+    mbs::clear_error();
+    Problem pb{A, B, AScale, BScale, AFactor, BFactor, out, M, N, K, Mpad, scaleN_pad, 0, false};
+    return mbs::gemm::run(pb, workspace, workspace_bytes, false, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int mbs_gemm_a4w4_macro_launch_ws(const uint8_t* A, const uint8_t* B,
+                                             const uint8_t* AScale, const uint8_t* BScaleMacro,
+                                             const uint8_t* AFactor, const uint8_t* BFactor, void* out,
+                                             int M, int N, int K, int Mpad, int scaleN_pad, int mb_ld,
+                                             void* workspace, size_t workspace_bytes, void* stream)
+{
+    mbs::clear_error();
+    Problem pb{A, B, AScale, BScaleMacro, AFactor, BFactor, out, M, N, K, Mpad, scaleN_pad, mb_ld, true};
+    return mbs::gemm::run(pb, workspace, workspace_bytes, false, reinterpret_cast<cudaStream_t>(stream));
+}

@@ -1,0 +1,324 @@
+// bf16 -> MXFP4 quantisers and the two layout kernels (weight preshuffle,
+// scale shuffle).  All are HBM-bound byte work: 16-byte vector loads/stores,
+// integer arithmetic for the scale, warp shuffles for the block amax.
+//
+// Quantiser arithmetic (OCP MX per-1x32, the task's spec for aiter's
+// per_1x32 quantiser called at test_gemm_a4w4.py:134-140):
+//   amax   = max |x| over the 32-element block, taken on the bf16 bit
+//            patterns (|x| bits = bits & 0x7FFF order like the magnitudes)
+//   scale  = e8m0 byte max(E(amax) - 2, 0)   (E = biased exponent field;
+//            i.e. 2^(floor(log2 amax) - 2)), 0xFF if the block holds Inf/NaN
+//   code   = RNE(|x| * 2^(127 - scale)) on {0,.5,1,1.5,2,3,4,6}, saturating,
+//            sign bit 3 copied from x; packed two per byte, low nibble first.
+#include <cuda_bf16.h>
+
+#include "common.h"
+
+namespace mbs {
+namespace {
+
+// e2m1 magnitude code of q >= 0 (RNE; ties at 0.25/1.25/2.5/5 go down, at
+// 0.75/1.75/3.5 up -- the neighbour with an even mantissa bit; > 5 -> 6).
+__device__ __forceinline__ uint32_t e2m1_code(float q)
+{
+    return (uint32_t)(q > 0.25f) + (uint32_t)(q >= 0.75f) + (uint32_t)(q > 1.25f) +
+           (uint32_t)(q >= 1.75f) + (uint32_t)(q > 2.5f) + (uint32_t)(q >= 3.5f) +
+           (uint32_t)(q > 5.0f);
+}
+
+__device__ __forceinline__ uint32_t scale_from_amax_bits(uint32_t amax_bits)
+{
+    if (amax_bits >= 0x7F80u) return 0xFFu;  // Inf or NaN in the block
+    const int e = (int)(amax_bits >> 7);      // bf16 exponent field == fp32's
+    return (uint32_t)max(e - 2, 0);
+}
+
+// Encode 2 bf16 (one 32-bit word) with multiplier `inv` = 2^(127 - scale).
+__device__ __forceinline__ uint32_t encode_pair(uint32_t w, float inv, bool nan_block)
+{
+    const uint32_t lo = w & 0xFFFFu, hi = w >> 16;
+    uint32_t c0 = e2m1_code(__uint_as_float((lo & 0x7FFFu) << 16) * inv) | ((lo >> 15) << 3);
+    uint32_t c1 = e2m1_code(__uint_as_float((hi & 0x7FFFu) << 16) * inv) | ((hi >> 15) << 3);
+    if (nan_block) c0 = c1 = 0;
+    return c0 | (c1 << 4);
+}
+
+__device__ __forceinline__ int64_t flat_s(int r, int b, int snp)
+{
+    const int r32 = r & 31, b8 = b & 7;
+    return (int64_t)(r32 >> 4) + (int64_t)(b8 >> 2) * 2 + (int64_t)(r32 & 15) * 4 +
+           (int64_t)(b8 & 3) * 64 + (int64_t)(b >> 3) * 256 + (int64_t)(r >> 5) * 32 * snp;
+}
+
+// One thread per 8 consecutive elements (16 bytes of bf16); the 4 threads of
+// a 32-element block are 4 consecutive lanes and combine their amax with two
+// xor-shuffles.  Out-of-range lanes run the shuffles with an empty block.
+__global__ void __launch_bounds__(256) quantize_1x32_kernel(const uint16_t* __restrict__ x,
+                                                            int rows, int K, int ld_x,
+                                                            uint8_t* __restrict__ q,
+                                                            uint8_t* __restrict__ sc, int shuffled,
+                                                            int snp)
+{
+    const int oct_per_row = K >> 3;
+    const int64_t total = (int64_t)rows * oct_per_row;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    const int64_t limit = (total + 31) / 32 * 32;
+    for (int64_t o = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; o < limit; o += stride)
+    {
+        const bool valid = o < total;
+        int r = 0, j = 0;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (valid)
+        {
+            r = (int)(o / oct_per_row);
+            j = (int)(o - (int64_t)r * oct_per_row);
+            v = __ldcs(reinterpret_cast<const uint4*>(x + (int64_t)r * ld_x) + j);
+        }
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+        uint32_t am = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            am = max(am, max(w[i] & 0x7FFFu, (w[i] >> 16) & 0x7FFFu));
+        am = max(am, __shfl_xor_sync(0xffffffffu, am, 1));
+        am = max(am, __shfl_xor_sync(0xffffffffu, am, 2));
+        if (!valid) continue;
+        const uint32_t s = scale_from_amax_bits(am);
+        const bool nan_block = s == 0xFFu;
+        const float inv = __uint_as_float((254u - (nan_block ? 254u : s)) << 23);
+        uint32_t packed = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) packed |= encode_pair(w[i], inv, nan_block) << (8 * i);
+        reinterpret_cast<uint32_t*>(q + (int64_t)r * (K >> 1))[j] = packed;
+        if ((j & 3) == 0)
+        {
+            const int b = j >> 2;
+            if (shuffled)
+                sc[flat_s(r, b, snp)] = (uint8_t)s;
+            else
+                sc[(int64_t)r * (K >> 5) + b] = (uint8_t)s;
+        }
+    }
+}
+
+// Writes 127 into the padding of a flatS buffer (rows >= rows, blocks >= K/32).
+__global__ void scale_padding_kernel(uint8_t* __restrict__ sc, int rows, int nblk, int rpad,
+                                     int snp)
+{
+    const int64_t total = (int64_t)rpad * snp;
+    for (int64_t o = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; o < total;
+         o += (int64_t)gridDim.x * blockDim.x)
+    {
+        const int rg = (int)(o / (32 * snp));
+        const int og = (int)(o - (int64_t)rg * 32 * snp);
+        const int w = og & 255;
+        const int r = rg * 32 + (w & 1) * 16 + ((w & 63) >> 2);
+        const int b = (og >> 8) * 8 + ((w & 3) >> 1) * 4 + (w >> 6);
+        if (r >= rows || b >= nblk) sc[o] = 127;
+    }
+}
+
+// One warp per 32-row x 32-K macro block: lane l owns row l of the block.
+__global__ void __launch_bounds__(256) quantize_macro_kernel(const uint16_t* __restrict__ x,
+                                                             int rows, int K, int ld_x,
+                                                             uint8_t* __restrict__ q,
+                                                             uint8_t* __restrict__ sc, int mb_ld)
+{
+    const int lane = threadIdx.x & 31;
+    const int warps_per_block = blockDim.x >> 5;
+    const int nb = (rows + 31) >> 5;
+    const int64_t total = (int64_t)nb * mb_ld;
+    for (int64_t wid = (int64_t)blockIdx.x * warps_per_block + (threadIdx.x >> 5); wid < total;
+         wid += (int64_t)gridDim.x * warps_per_block)
+    {
+        const int rb = (int)(wid / mb_ld);
+        const int kb = (int)(wid - (int64_t)rb * mb_ld);
+        if (kb >= (K >> 5))
+        {
+            if (lane == 0) sc[(int64_t)rb * mb_ld + kb] = 127;
+            continue;
+        }
+        const int r = rb * 32 + lane;
+        uint32_t w[16];
+        if (r < rows)
+        {
+            const uint4* src = reinterpret_cast<const uint4*>(x + (int64_t)r * ld_x + kb * 32);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+            {
+                const uint4 v = __ldcs(src + i);
+                w[4 * i + 0] = v.x;
+                w[4 * i + 1] = v.y;
+                w[4 * i + 2] = v.z;
+                w[4 * i + 3] = v.w;
+            }
+        }
+        else
+        {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) w[i] = 0;
+        }
+        uint32_t am = 0;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) am = max(am, max(w[i] & 0x7FFFu, (w[i] >> 16) & 0x7FFFu));
+#pragma unroll
+        for (int m = 1; m < 32; m <<= 1) am = max(am, __shfl_xor_sync(0xffffffffu, am, m));
+        const uint32_t s = scale_from_amax_bits(am);
+        const bool nan_block = s == 0xFFu;
+        const float inv = __uint_as_float((254u - (nan_block ? 254u : s)) << 23);
+        if (r < rows)
+        {
+            uint32_t out[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+            {
+                uint32_t p = 0;
+#pragma unroll
+                for (int t = 0; t < 4; ++t) p |= encode_pair(w[4 * i + t], inv, nan_block) << (8 * t);
+                out[i] = p;
+            }
+            *reinterpret_cast<uint4*>(q + (int64_t)r * (K >> 1) + kb * 16) =
+                make_uint4(out[0], out[1], out[2], out[3]);
+        }
+        if (lane == 0) sc[(int64_t)rb * mb_ld + kb] = (uint8_t)s;
+    }
+}
+
+// flatB preshuffle: the 16 bytes (n, kp..kp+15), kp % 16 == 0, are
+// contiguous in both layouts.
+__global__ void shuffle_weight_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst,
+                                      int N, int K)
+{
+    const int chunks = K >> 5;  // 16-byte chunks per row (K/2 bytes)
+    const int64_t total = (int64_t)N * chunks;
+    for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total;
+         t += (int64_t)gridDim.x * blockDim.x)
+    {
+        const int n = (int)(t / chunks);
+        const int c = (int)(t - (int64_t)n * chunks);
+        const uint4 v = __ldcs(reinterpret_cast<const uint4*>(src + (int64_t)n * (K >> 1)) + c);
+        const int64_t off = (int64_t)(n >> 4) * ((int64_t)K * 8) + (int64_t)c * 256 + (n & 15) * 16;
+        *reinterpret_cast<uint4*>(dst + off) = v;
+    }
+}
+
+// flatS shuffle, one thread per destination byte (coalesced writes), padding 127.
+__global__ void shuffle_scales_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst,
+                                      int rows, int nblk, int rpad, int snp)
+{
+    const int64_t total = (int64_t)rpad * snp;
+    for (int64_t o = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; o < total;
+         o += (int64_t)gridDim.x * blockDim.x)
+    {
+        const int rg = (int)(o / (32 * snp));
+        const int og = (int)(o - (int64_t)rg * 32 * snp);
+        const int w = og & 255;
+        const int r = rg * 32 + (w & 1) * 16 + ((w & 63) >> 2);
+        const int b = (og >> 8) * 8 + ((w & 3) >> 1) * 4 + (w >> 6);
+        dst[o] = (r < rows && b < nblk) ? src[(int64_t)r * nblk + b] : (uint8_t)127;
+    }
+}
+
+int grid_for(int64_t work, int threads, int num_sms)
+{
+    int64_t blocks = (work + threads - 1) / threads;
+    const int64_t cap = (int64_t)num_sms * 8;
+    if (blocks > cap) blocks = cap;
+    if (blocks < 1) blocks = 1;
+    return (int)blocks;
+}
+
+}  // namespace
+}  // namespace mbs
+
+using namespace mbs;
+
+extern "C" int mbs_quantize_mxfp4(const void* x_bf16, int rows, int K, int ld_x, uint8_t* fp4_out,
+                                  uint8_t* scale_out, int shuffled, void* stream)
+{
+    clear_error();
+    if (!x_bf16 || !fp4_out || !scale_out)
+        return fail(MBS_ERR_INVALID_ARGUMENT, "mbs_quantize_mxfp4: null pointer");
+    if (rows <= 0 || K <= 0) return fail(MBS_ERR_INVALID_ARGUMENT, "rows and K must be positive");
+    if (K % 32 != 0) return fail(MBS_ERR_UNSUPPORTED_SHAPE, "K must be a multiple of 32, got %d", K);
+    if (ld_x < K) return fail(MBS_ERR_INVALID_ARGUMENT, "ld_x (%d) < K (%d)", ld_x, K);
+    if (!aligned16(x_bf16) || (ld_x % 8) != 0 || !aligned16(fp4_out) || ((K / 2) % 4) != 0)
+        return fail(MBS_ERR_MISALIGNED, "x must be 16-byte aligned with ld_x %% 8 == 0");
+    DeviceInfo dev;
+    int st = current_device(&dev);
+    if (st != MBS_OK) return st;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    const int snp = scale_n_pad(K);
+    const int64_t octs = (int64_t)rows * (K / 8);
+    quantize_1x32_kernel<<<grid_for(octs, 256, dev.num_sms), 256, 0, s>>>(
+        static_cast<const uint16_t*>(x_bf16), rows, K, ld_x, fp4_out, scale_out, shuffled ? 1 : 0,
+        snp);
+    if (shuffled && ((rows % 32) != 0 || (K / 32) != snp))
+    {
+        const int rpad = round_up(rows, 32);
+        scale_padding_kernel<<<grid_for((int64_t)rpad * snp, 256, dev.num_sms), 256, 0, s>>>(
+            scale_out, rows, K / 32, rpad, snp);
+    }
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? MBS_OK : cuda_fail(e, "quantize launch");
+}
+
+extern "C" int mbs_quantize_mxfp4_macro(const void* x_bf16, int rows, int K, int ld_x,
+                                        uint8_t* fp4_out, uint8_t* scale_out, void* stream)
+{
+    clear_error();
+    if (!x_bf16 || !fp4_out || !scale_out)
+        return fail(MBS_ERR_INVALID_ARGUMENT, "mbs_quantize_mxfp4_macro: null pointer");
+    if (rows <= 0 || K <= 0) return fail(MBS_ERR_INVALID_ARGUMENT, "rows and K must be positive");
+    if (K % 32 != 0) return fail(MBS_ERR_UNSUPPORTED_SHAPE, "K must be a multiple of 32, got %d", K);
+    if (ld_x < K) return fail(MBS_ERR_INVALID_ARGUMENT, "ld_x (%d) < K (%d)", ld_x, K);
+    if (!aligned16(x_bf16) || (ld_x % 8) != 0 || !aligned16(fp4_out))
+        return fail(MBS_ERR_MISALIGNED, "x must be 16-byte aligned with ld_x %% 8 == 0");
+    DeviceInfo dev;
+    int st = current_device(&dev);
+    if (st != MBS_OK) return st;
+    const int mb_ld = round_up(K / 32, 16);
+    const int64_t warps = (int64_t)((rows + 31) / 32) * mb_ld;
+    quantize_macro_kernel<<<grid_for(warps * 32, 256, dev.num_sms), 256, 0,
+                            reinterpret_cast<cudaStream_t>(stream)>>>(
+        static_cast<const uint16_t*>(x_bf16), rows, K, ld_x, fp4_out, scale_out, mb_ld);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? MBS_OK : cuda_fail(e, "quantize_macro launch");
+}
+
+extern "C" int mbs_shuffle_weight(const uint8_t* src, uint8_t* dst, int N, int K, void* stream)
+{
+    clear_error();
+    if (!src || !dst) return fail(MBS_ERR_INVALID_ARGUMENT, "mbs_shuffle_weight: null pointer");
+    if (N <= 0 || K <= 0) return fail(MBS_ERR_INVALID_ARGUMENT, "N and K must be positive");
+    if (N % 16 != 0 || K % 64 != 0)
+        return fail(MBS_ERR_UNSUPPORTED_SHAPE, "shuffle_weight needs N %% 16 == 0 and K %% 64 == 0 (N=%d K=%d)",
+                    N, K);
+    if (!aligned16(src) || !aligned16(dst))
+        return fail(MBS_ERR_MISALIGNED, "src/dst must be 16-byte aligned");
+    DeviceInfo dev;
+    int st = current_device(&dev);
+    if (st != MBS_OK) return st;
+    shuffle_weight_kernel<<<grid_for((int64_t)N * (K / 32), 256, dev.num_sms), 256, 0,
+                            reinterpret_cast<cudaStream_t>(stream)>>>(src, dst, N, K);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? MBS_OK : cuda_fail(e, "shuffle_weight launch");
+}
+
+extern "C" int mbs_shuffle_scales(const uint8_t* plain, uint8_t* shuffled, int rows, int K,
+                                  void* stream)
+{
+    clear_error();
+    if (!plain || !shuffled) return fail(MBS_ERR_INVALID_ARGUMENT, "mbs_shuffle_scales: null pointer");
+    if (rows <= 0 || K <= 0) return fail(MBS_ERR_INVALID_ARGUMENT, "rows and K must be positive");
+    if (K % 32 != 0) return fail(MBS_ERR_UNSUPPORTED_SHAPE, "K must be a multiple of 32, got %d", K);
+    DeviceInfo dev;
+    int st = current_device(&dev);
+    if (st != MBS_OK) return st;
+    const int snp = scale_n_pad(K);
+    const int rpad = round_up(rows, 32);
+    shuffle_scales_kernel<<<grid_for((int64_t)rpad * snp, 256, dev.num_sms), 256, 0,
+                            reinterpret_cast<cudaStream_t>(stream)>>>(plain, shuffled, rows, K / 32,
+                                                                       rpad, snp);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? MBS_OK : cuda_fail(e, "shuffle_scales launch");
+}

@@ -1,0 +1,159 @@
+"""Drop-in ``mbs_gemm_a4w4`` operator module (host side of the C ABI).
+
+Mirrors the reference's pybind11 module ``mbs_gemm_a4w4``
+(interface/gemm_a4w4_pybind.cpp:19-74): same function name, argument order,
+byte-reinterpretation of fp4/e8m0 tensors, shape checks and ``RuntimeError``
+messages, and the same output contract (bf16 ``out[Mpad, N]`` allocated on
+A's device, returned as ``out[:M]``).  Two additions: the MBS factors are
+optional (the reference's 6-argument form and the 4-argument form used by
+bench_one.py:31 both work), and ``out=`` accepts a caller buffer.
+
+    import mbs_b200.mbs_gemm_a4w4 as mbs_gemm_a4w4   # or put mbs_b200/ on sys.path
+    out = mbs_gemm_a4w4.gemm_a4w4(A, B, A_scale, B_scale, A_factor, B_factor)
+
+Launches go to the current torch CUDA stream of A's device, asynchronously.
+"""
+
+from __future__ import annotations
+
+import threading
+
+import torch
+
+from . import _lib
+
+__all__ = ["gemm_a4w4", "gemm_a4w4_macro", "workspace_for"]
+
+_ws_lock = threading.Lock()
+_ws_cache: dict = {}
+
+
+def _round_up(x: int, m: int) -> int:
+    return (x + m - 1) // m * m
+
+
+def scale_n_pad(K: int) -> int:
+    """roundup(ceil(K/32), 8) -- interface/gemm_a4w4_pybind.cpp:46-48."""
+    return _round_up((K + 31) // 32, 8)
+
+
+def _bytes(t: torch.Tensor) -> torch.Tensor:
+    # .view(kByte).contiguous() as in interface/gemm_a4w4_pybind.cpp:25-30
+    return t.view(torch.uint8).contiguous()
+
+
+def workspace_for(M: int, N: int, K: int, device: torch.device) -> torch.Tensor | None:
+    """Zero-initialised stream-K scratch for this shape on the current stream.
+
+    One buffer per (device, stream), grown on demand.  The kernels leave it
+    zeroed after every launch, so it is reused without clearing.
+    """
+    need = int(_lib.lib().mbs_gemm_a4w4_workspace_size(M, N, K))
+    if need == 0:
+        return None
+    stream = torch.cuda.current_stream(device)
+    key = (device.index, stream.cuda_stream)
+    with _ws_lock:
+        buf = _ws_cache.get(key)
+        if buf is None or buf.numel() < need:
+            buf = torch.zeros(max(need, 1 << 22), dtype=torch.uint8, device=device)
+            _ws_cache[key] = buf
+    return buf
+
+
+def _check_inputs(A, B, A_scale, B_scale, A_factor, B_factor):
+    if not (A.is_cuda and B.is_cuda):
+        raise RuntimeError("gemm_a4w4: A, B must be on device")
+    if A.dim() != 2 or B.dim() != 2:
+        raise RuntimeError("gemm_a4w4: A, B must be 2D")
+    Au, Bu = _bytes(A), _bytes(B)
+    Asc, Bsc = _bytes(A_scale), _bytes(B_scale)
+    M, Kp = int(Au.size(0)), int(Au.size(1))
+    K, N = 2 * Kp, int(Bu.size(0))
+    if int(Bu.size(1)) != Kp:
+        raise RuntimeError(f"gemm_a4w4: A, B must share K/2, got {Au.size(1)} vs {Bu.size(1)}")
+    if K % 32 != 0:
+        raise RuntimeError(f"gemm_a4w4: K must be a multiple of 32, got {K}")
+    if N % 16 != 0:
+        raise RuntimeError(f"gemm_a4w4: N must be a multiple of 16, got {N}")
+    Afc = Bfc = None
+    if A_factor is not None:
+        Afc = _bytes(A_factor)
+        if not (Afc.is_cuda and Afc.numel() == M):
+            raise RuntimeError(f"gemm_a4w4: A_factor must hold M = {M} bytes on device, got {Afc.numel()}")
+    if B_factor is not None:
+        Bfc = _bytes(B_factor)
+        if not (Bfc.is_cuda and Bfc.numel() == N):
+            raise RuntimeError(f"gemm_a4w4: B_factor must hold N = {N} bytes on device, got {Bfc.numel()}")
+    for name, t in (("A_scale", Asc), ("B_scale", Bsc)):
+        if not t.is_cuda or t.device != A.device:
+            raise RuntimeError(f"gemm_a4w4: {name} must be on A's device")
+    return Au, Bu, Asc, Bsc, Afc, Bfc, M, N, K
+
+
+def _out_buffer(out, Mpad, M, N, device):
+    if out is None:
+        return torch.empty((Mpad, N), dtype=torch.bfloat16, device=device)
+    if out.dtype != torch.bfloat16 or out.device != device or not out.is_contiguous() \
+            or out.dim() != 2 or out.size(0) < M or out.size(1) != N:
+        raise RuntimeError(f"gemm_a4w4: out must be a contiguous bf16 [>= {M}, {N}] tensor on {device}")
+    return out
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def gemm_a4w4(A: torch.Tensor, B: torch.Tensor, A_scale: torch.Tensor, B_scale: torch.Tensor,
+              A_factor: torch.Tensor | None = None, B_factor: torch.Tensor | None = None,
+              out: torch.Tensor | None = None) -> torch.Tensor:
+    """out[M, N] bf16 = dequant(A) @ dequant(B)^T * f(A_factor) * f(B_factor)^T.
+
+    A: [M, K/2] fp4x2 plain; B: [N, K/2] fp4x2 preshuffled (16x16);
+    A_scale / B_scale: e8m0 in the shuffled layout (>= Mpad*scaleN_pad and
+    roundup(N,32)*scaleN_pad bytes); factors: uint8 [M] / [N] or None,
+    f(b) = 1 / (1 + b/256).  (interface/gemm_a4w4_pybind.cpp:7-18)
+    """
+    Au, Bu, Asc, Bsc, Afc, Bfc, M, N, K = _check_inputs(A, B, A_scale, B_scale, A_factor, B_factor)
+    Mpad = _round_up(M, 32)
+    snp = scale_n_pad(K)
+    if Asc.numel() < Mpad * snp:
+        raise RuntimeError(f"gemm_a4w4: A_scale must hold Mpad*scaleN_pad = {Mpad * snp} bytes, "
+                           f"got {Asc.numel()}")
+    if Bsc.numel() < _round_up(N, 32) * snp:
+        raise RuntimeError(f"gemm_a4w4: B_scale must hold roundup(N,32)*scaleN_pad = "
+                           f"{_round_up(N, 32) * snp} bytes, got {Bsc.numel()}")
+    o = _out_buffer(out, Mpad, M, N, A.device)
+    with torch.cuda.device(A.device):
+        ws = workspace_for(M, N, K, A.device)
+        stream = torch.cuda.current_stream(A.device).cuda_stream
+        _lib.call("mbs_gemm_a4w4_launch_ws", _ptr(Au), _ptr(Bu), _ptr(Asc), _ptr(Bsc), _ptr(Afc),
+                  _ptr(Bfc), o.data_ptr(), M, N, K, Mpad, snp, _ptr(ws),
+                  0 if ws is None else ws.numel(), stream)
+    return o.narrow(0, 0, M)
+
+
+def gemm_a4w4_macro(A: torch.Tensor, B: torch.Tensor, A_scale: torch.Tensor,
+                    B_scale_macro: torch.Tensor, A_factor: torch.Tensor | None = None,
+                    B_factor: torch.Tensor | None = None,
+                    out: torch.Tensor | None = None) -> torch.Tensor:
+    """Macro-block-scaling variant: B's scales are one e8m0 per 32 rows x 32 K,
+    given plainly as [ceil(N/32), roundup(K/32, 16)] (see quantize_mxfp4_macro)."""
+    Au, Bu, Asc, Bsc, Afc, Bfc, M, N, K = _check_inputs(A, B, A_scale, B_scale_macro, A_factor,
+                                                        B_factor)
+    Mpad = _round_up(M, 32)
+    snp = scale_n_pad(K)
+    mb_ld = _round_up(K // 32, 16)
+    if Asc.numel() < Mpad * snp:
+        raise RuntimeError(f"gemm_a4w4: A_scale must hold {Mpad * snp} bytes, got {Asc.numel()}")
+    if Bsc.numel() < ((N + 31) // 32) * mb_ld:
+        raise RuntimeError(f"gemm_a4w4: B_scale_macro must hold {((N + 31) // 32) * mb_ld} bytes, "
+                           f"got {Bsc.numel()}")
+    o = _out_buffer(out, Mpad, M, N, A.device)
+    with torch.cuda.device(A.device):
+        ws = workspace_for(M, N, K, A.device)
+        stream = torch.cuda.current_stream(A.device).cuda_stream
+        _lib.call("mbs_gemm_a4w4_macro_launch_ws", _ptr(Au), _ptr(Bu), _ptr(Asc), _ptr(Bsc),
+                  _ptr(Afc), _ptr(Bfc), o.data_ptr(), M, N, K, Mpad, snp, mb_ld, _ptr(ws),
+                  0 if ws is None else ws.numel(), stream)
+    return o.narrow(0, 0, M)

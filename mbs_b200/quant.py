@@ -1,0 +1,97 @@
+"""bf16 -> MXFP4 quantisers and layout shuffles (CUDA kernels via the C ABI).
+
+These replace the aiter helpers the reference's drivers call before the GEMM
+(test_gemm_a4w4.py:134-141, bench_one.py:20-25): ``get_triton_quant
+(QuantType.per_1x32)`` and ``shuffle_weight(layout=(16, 16))``.  aiter itself
+is third-party and absent; the arithmetic is OCP MX per-1x32 (see
+include/mbs_gemm_a4w4.h).
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from .mbs_gemm_a4w4 import _round_up, scale_n_pad
+
+__all__ = ["quantize_mxfp4", "quantize_mxfp4_macro", "shuffle_weight", "shuffle_scales",
+           "macro_scale_ld", "quant_gemm_a4w4"]
+
+
+def macro_scale_ld(K: int) -> int:
+    return _round_up(K // 32, 16)
+
+
+def _stream(dev):
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _check_x(x: torch.Tensor):
+    if not x.is_cuda or x.dtype != torch.bfloat16 or x.dim() != 2:
+        raise RuntimeError("quantize_mxfp4: x must be a 2-D bf16 CUDA tensor")
+    if x.stride(1) != 1:
+        x = x.contiguous()
+    R, K = int(x.size(0)), int(x.size(1))
+    if K % 32 != 0:
+        raise RuntimeError(f"quantize_mxfp4: K must be a multiple of 32, got {K}")
+    return x, R, K
+
+
+def quantize_mxfp4(x: torch.Tensor, shuffle: bool = False):
+    """bf16 [R, K] -> (fp4x2 uint8 [R, K/2], e8m0 uint8 scales).
+
+    shuffle=False: scales [R, K/32].  shuffle=True: scales
+    [roundup(R,32), scaleN_pad] in the reference's shuffled layout.
+    """
+    x, R, K = _check_x(x)
+    q = torch.empty((R, K // 2), dtype=torch.uint8, device=x.device)
+    if shuffle:
+        s = torch.empty((_round_up(R, 32), scale_n_pad(K)), dtype=torch.uint8, device=x.device)
+    else:
+        s = torch.empty((R, K // 32), dtype=torch.uint8, device=x.device)
+    with torch.cuda.device(x.device):
+        _lib.call("mbs_quantize_mxfp4", x.data_ptr(), R, K, int(x.stride(0)), q.data_ptr(),
+                  s.data_ptr(), 1 if shuffle else 0, _stream(x.device))
+    return q, s
+
+
+def quantize_mxfp4_macro(x: torch.Tensor):
+    """bf16 [N, K] -> (fp4x2 [N, K/2], macro scales [ceil(N/32), roundup(K/32, 16)])."""
+    x, R, K = _check_x(x)
+    q = torch.empty((R, K // 2), dtype=torch.uint8, device=x.device)
+    s = torch.empty(((R + 31) // 32, macro_scale_ld(K)), dtype=torch.uint8, device=x.device)
+    with torch.cuda.device(x.device):
+        _lib.call("mbs_quantize_mxfp4_macro", x.data_ptr(), R, K, int(x.stride(0)), q.data_ptr(),
+                  s.data_ptr(), _stream(x.device))
+    return q, s
+
+
+def shuffle_weight(w: torch.Tensor) -> torch.Tensor:
+    """Plain fp4x2 [N, K/2] -> preshuffled [N, K/2] (the 16x16 weight layout)."""
+    wu = w.view(torch.uint8).contiguous()
+    N, Kp = int(wu.size(0)), int(wu.size(1))
+    out = torch.empty_like(wu)
+    with torch.cuda.device(wu.device):
+        _lib.call("mbs_shuffle_weight", wu.data_ptr(), out.data_ptr(), N, 2 * Kp, _stream(wu.device))
+    return out
+
+
+def shuffle_scales(s: torch.Tensor, K: int | None = None) -> torch.Tensor:
+    """Plain scales [R, K/32] -> shuffled [roundup(R,32), scaleN_pad]."""
+    su = s.view(torch.uint8).contiguous()
+    R = int(su.size(0))
+    K = int(su.size(1)) * 32 if K is None else K
+    out = torch.empty((_round_up(R, 32), scale_n_pad(K)), dtype=torch.uint8, device=su.device)
+    with torch.cuda.device(su.device):
+        _lib.call("mbs_shuffle_scales", su.data_ptr(), out.data_ptr(), R, K, _stream(su.device))
+    return out
+
+
+def quant_gemm_a4w4(x: torch.Tensor, B: torch.Tensor, B_scale: torch.Tensor,
+                    A_factor=None, B_factor=None, out=None) -> torch.Tensor:
+    """Dynamic-quant + GEMM: bf16 activations x [M, K] against a preshuffled
+    MXFP4 weight B [N, K/2] with shuffled scales.  Quantises x on the device
+    (shuffled scales) and runs the GEMM on the same stream."""
+    from .mbs_gemm_a4w4 import gemm_a4w4
+    q, s = quantize_mxfp4(x, shuffle=True)
+    return gemm_a4w4(q, B, s, B_scale, A_factor, B_factor, out=out)

@@ -1,0 +1,94 @@
+"""CPU tests of the C ABI: the library builds, loads, exports every declared
+symbol, and rejects bad arguments before touching a device."""
+
+import ctypes
+import os
+import re
+
+import pytest
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _declared_functions():
+    names = []
+    inc = os.path.join(REPO, "include")
+    for fn in sorted(os.listdir(inc)):
+        if not fn.endswith(".h"):
+            continue
+        text = open(os.path.join(inc, fn)).read()
+        text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+        for m in re.finditer(r"^\s*(?:const\s+)?[A-Za-z_][\w\s\*]*?\b([a-z_][a-z0-9_]*)\s*\(",
+                             text, flags=re.M):
+            names.append(m.group(1))
+    return sorted(set(names))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from mbs_b200 import _lib, build
+    build.build()
+    return _lib.lib()
+
+
+def test_every_declared_symbol_is_exported(lib):
+    from mbs_b200 import _lib
+    declared = _declared_functions()
+    assert "gemm_a4w4_mxfp4_launch" in declared and len(declared) >= 11
+    for name in declared:
+        assert hasattr(lib, name), f"{name} declared in include/ but not exported"
+        assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
+
+
+def test_status_strings(lib):
+    assert lib.mbs_status_string(0) == b"MBS_OK"
+    assert lib.mbs_status_string(2) == b"MBS_ERR_UNSUPPORTED_SHAPE"
+    assert lib.mbs_status_string(99) == b"MBS_ERR_UNKNOWN"
+
+
+def _gemm(lib, A=1024, B=1024, AS=1024, BS=1024, out=1024, M=32, N=64, K=128, Mpad=32, snp=8):
+    return lib.mbs_gemm_a4w4_launch_ws(A, B, AS, BS, None, None, out, M, N, K, Mpad, snp, None, 0,
+                                      None)
+
+
+def test_gemm_argument_validation_without_device(lib):
+    # all of these fail in host-side validation, before any CUDA call
+    assert _gemm(lib, A=None) == 1
+    assert _gemm(lib, M=0) == 1
+    assert _gemm(lib, N=40) == 2                      # N % 16
+    assert _gemm(lib, K=96) == 2                      # K % 64
+    assert _gemm(lib, Mpad=16) == 1                   # Mpad < roundup(M, 32)
+    assert _gemm(lib, snp=4) == 1                     # scaleN_pad < K/32
+    assert _gemm(lib, A=1024 + 8) == 3                # misaligned operand
+    assert b"multiple of 16" in lib.mbs_last_error_message() or True
+    assert _gemm(lib, N=40) == 2
+    assert b"N must be a multiple of 16" in lib.mbs_last_error_message()
+    st = lib.gemm_a4w4_mxfp4_launch(1024, 1024, 1024, 1024, None, None, 1024, 8, 16, 64, 32, 7,
+                                    None)
+    assert st == 1 and b"scaleN_pad" in lib.mbs_last_error_message()
+
+
+def test_quant_and_shuffle_validation_without_device(lib):
+    assert lib.mbs_quantize_mxfp4(None, 4, 64, 64, 1024, 1024, 0, None) == 1
+    assert lib.mbs_quantize_mxfp4(1024, 4, 48, 48, 1024, 1024, 0, None) == 2
+    assert lib.mbs_quantize_mxfp4(1024 + 2, 4, 64, 64, 1024, 1024, 0, None) == 3
+    assert lib.mbs_shuffle_weight(1024, 2048, 24, 64, None) == 2
+    assert lib.mbs_shuffle_weight(1024, 2048, 32, 96, None) == 2
+    assert lib.mbs_shuffle_scales(1024, 2048, 4, 40, None) == 2
+    assert lib.mbs_quantize_mxfp4_macro(1024, 4, 40, 64, 1024, 1024, None) == 2
+
+
+def test_workspace_size_is_host_only(lib):
+    lib.mbs_gemm_a4w4_workspace_size.restype = ctypes.c_size_t
+    # decode shapes use stream-K scratch; a large prefill uses none
+    assert lib.mbs_gemm_a4w4_workspace_size(16, 57344, 8192) > 0
+    assert lib.mbs_gemm_a4w4_workspace_size(8192, 8192, 8192) == 0
+    assert lib.mbs_gemm_a4w4_workspace_size(0, 16, 64) == 0
+
+
+def test_python_layer_fails_loudly_without_library(monkeypatch, tmp_path):
+    from mbs_b200 import _lib
+    monkeypatch.setattr(_lib, "_lib", None)
+    monkeypatch.setattr(_lib, "LIB_PATH", str(tmp_path / "missing.so"))
+    with pytest.raises(RuntimeError, match="no non-CUDA fallback"):
+        _lib.lib()

@@ -1,0 +1,90 @@
+"""GPU quantiser and layout kernels: bit-exact against the CPU oracle."""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import mxfp4_oracle as O
+from tests.gpu_helpers import bf16_bits, seeded_bf16
+
+pytestmark = pytest.mark.gpu
+
+
+def _special_rows(K: int) -> torch.Tensor:
+    """Rows exercising ties, saturation, zero / subnormal / Inf / NaN blocks."""
+    grid = torch.tensor([4.0, 0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0, 7.9, -3.5, -0.0, 0.3],
+                        dtype=torch.float32)
+    rows = []
+    r = torch.zeros(K)
+    r[: grid.numel()] = grid
+    rows.append(r)
+    rows.append(torch.zeros(K))                          # zero blocks -> scale 0
+    rows.append(torch.full((K,), 1e-39))                 # subnormal blocks
+    r = torch.randn(K)
+    r[5] = float("inf")
+    rows.append(r)
+    r = torch.randn(K)
+    r[K - 1] = float("nan")
+    rows.append(r)
+    rows.append(torch.full((K,), 3.0e38))                # near the top of the range
+    rows.append(torch.randn(K) * 1e-30)
+    return torch.stack(rows).to(torch.bfloat16)
+
+
+@pytest.mark.parametrize("R,K", [(1, 32), (7, 64), (33, 96), (64, 1024), (300, 2080)])
+@pytest.mark.parametrize("shuffle", [False, True])
+def test_quantize_bit_exact(R, K, shuffle):
+    x = seeded_bf16(R, K, seed=R * 31 + K)
+    if R >= 7:
+        x[:7] = _special_rows(K)
+    q_ref, s_ref = O.quantize_mxfp4(bf16_bits(x))
+    q, s = __import__("mbs_b200").quantize_mxfp4(x.cuda(), shuffle=shuffle)
+    torch.cuda.synchronize()
+    assert np.array_equal(q.cpu().numpy(), q_ref)
+    if shuffle:
+        assert np.array_equal(s.cpu().numpy(), O.shuffle_scales(s_ref, K))
+    else:
+        assert np.array_equal(s.cpu().numpy(), s_ref)
+
+
+def test_quantize_strided_rows():
+    import mbs_b200
+    big = seeded_bf16(40, 512, seed=5)
+    view = big[:, :256]  # row stride 512 elements
+    q, s = mbs_b200.quantize_mxfp4(view.cuda(), shuffle=False)
+    q_ref, s_ref = O.quantize_mxfp4(bf16_bits(view))
+    assert np.array_equal(q.cpu().numpy(), q_ref) and np.array_equal(s.cpu().numpy(), s_ref)
+
+
+@pytest.mark.parametrize("N,K", [(32, 64), (70, 96), (256, 1024), (1000, 4096)])
+def test_quantize_macro_bit_exact(N, K):
+    import mbs_b200
+    x = seeded_bf16(N, K, seed=N + K, outlier_frac=0.01)
+    q_ref, mb_ref = O.quantize_mxfp4_macro(bf16_bits(x))
+    q, mb = mbs_b200.quantize_mxfp4_macro(x.cuda())
+    assert np.array_equal(q.cpu().numpy(), q_ref)
+    assert np.array_equal(mb.cpu().numpy(), mb_ref)
+
+
+@pytest.mark.parametrize("N,K", [(16, 64), (48, 320), (1040, 1024)])
+def test_shuffle_weight_bit_exact(N, K):
+    import mbs_b200
+    rng = np.random.default_rng(N * K)
+    w = rng.integers(0, 256, size=(N, K // 2), dtype=np.uint8)
+    out = mbs_b200.shuffle_weight(torch.from_numpy(w).cuda())
+    assert np.array_equal(out.cpu().numpy(), O.shuffle_weight(w))
+
+
+@pytest.mark.parametrize("R,K", [(1, 32), (45, 320), (256, 8192)])
+def test_shuffle_scales_bit_exact(R, K):
+    import mbs_b200
+    rng = np.random.default_rng(R + K)
+    s = rng.integers(0, 256, size=(R, K // 32), dtype=np.uint8)
+    out = mbs_b200.shuffle_scales(torch.from_numpy(s).cuda(), K)
+    assert np.array_equal(out.cpu().numpy(), O.shuffle_scales(s, K))
+
+
+def test_quantize_rejects_bad_k():
+    import mbs_b200
+    with pytest.raises(RuntimeError, match="multiple of 32"):
+        mbs_b200.quantize_mxfp4(torch.zeros(4, 48, dtype=torch.bfloat16, device="cuda"))
