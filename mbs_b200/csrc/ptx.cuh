@@ -76,8 +76,8 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
 #pragma unroll 1
         for (int i = 0; i < 32; ++i)
             if (mbar_try_wait(a, parity)) return true;
-        if (abort != nullptr && *abort) return false;
-        if (globaltimer_ns() - t0 > kWaitTimeoutNs) return false;
+        if ((abort != nullptr && *abort) || globaltimer_ns() - t0 > kWaitTimeoutNs)
+            return mbar_try_wait(a, parity);  // last look, then give up
     }
 }
 
