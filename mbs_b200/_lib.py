@@ -52,11 +52,14 @@ def lib() -> ctypes.CDLL:
         return _lib
     with _lock:
         if _lib is None:
-            if not os.path.exists(LIB_PATH):
+            # MBS_LIB selects another build of the same library (e.g. the
+            # MBS_TIMING debug build); it never selects a non-CUDA path.
+            path = os.environ.get("MBS_LIB") or LIB_PATH
+            if not os.path.exists(path):
                 raise RuntimeError(
-                    f"{LIB_PATH} is missing: build it with `python -m mbs_b200.build` "
+                    f"{path} is missing: build it with `python -m mbs_b200.build` "
                     "(the MXFP4 operators have no non-CUDA fallback)")
-            handle = ctypes.CDLL(LIB_PATH)
+            handle = ctypes.CDLL(path)
             for name, (res, args) in SIGNATURES.items():
                 fn = getattr(handle, name)
                 fn.restype = res

@@ -19,6 +19,8 @@ CSRC = os.path.join(PKG_DIR, "csrc")
 REPO = os.path.dirname(PKG_DIR)
 LIB_NAME = "libmbs_gemm_kernel.so"
 LIB_PATH = os.path.join(PKG_DIR, LIB_NAME)
+# Debug variant with per-role cycle counters (-DMBS_TIMING=1, mbs_timing_read()).
+TIMING_LIB_PATH = os.path.join(PKG_DIR, "libmbs_gemm_kernel_timing.so")
 SOURCES = ["common.cu", "quant.cu", "gemm.cu"]
 HEADERS = ["common.h", "ptx.cuh"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -38,24 +40,27 @@ def _inputs() -> list[str]:
     return files
 
 
-def up_to_date() -> bool:
-    if not os.path.exists(LIB_PATH):
+def up_to_date(path: str = LIB_PATH) -> bool:
+    if not os.path.exists(path):
         return False
-    t = os.path.getmtime(LIB_PATH)
+    t = os.path.getmtime(path)
     return all(os.path.getmtime(f) <= t for f in _inputs())
 
 
-def build(force: bool = False, verbose: bool = False) -> str:
+def build(force: bool = False, verbose: bool = False, timing: bool = False) -> str:
     """Compile the library if any source is newer than it; return its path."""
-    if not force and up_to_date():
-        return LIB_PATH
+    path = TIMING_LIB_PATH if timing else LIB_PATH
+    if not force and up_to_date(path):
+        return path
     cuda_home = os.path.dirname(os.path.dirname(_nvcc()))
-    tmp = LIB_PATH + ".tmp"
+    tmp = path + ".tmp"
     cmd = [_nvcc(), *ARCH_FLAGS, "-O3", "-std=c++17", "-lineinfo", "-shared",
            "-Xcompiler", "-fPIC", "-cudart", "shared",
            "-Xlinker", f"-rpath,{os.path.join(cuda_home, 'lib64')}",
            "-I", os.path.join(REPO, "include"),
            "-o", tmp] + [os.path.join(CSRC, s) for s in SOURCES]
+    if timing:
+        cmd.insert(1, "-DMBS_TIMING=1")
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
         print(" ".join(cmd), flush=True)
@@ -63,9 +68,10 @@ def build(force: bool = False, verbose: bool = False) -> str:
     if res.returncode != 0:
         msg = (res.stderr or "") + (res.stdout or "")
         raise RuntimeError(f"nvcc failed ({res.returncode}):\n{msg}")
-    os.replace(tmp, LIB_PATH)
-    return LIB_PATH
+    os.replace(tmp, path)
+    return path
 
 
 if __name__ == "__main__":
-    print(build(force="--force" in sys.argv, verbose="-v" in sys.argv))
+    print(build(force="--force" in sys.argv, verbose="-v" in sys.argv,
+                timing="--timing" in sys.argv))

@@ -168,6 +168,42 @@ __device__ __forceinline__ void raise_error(const Params& p, volatile int* abort
     atomicExch(p.err, (unsigned)MBS_ERR_DEVICE_TIMEOUT);
 }
 
+// Debug instrumentation (build with -DMBS_TIMING=1): cycles per role and
+// wait site, summed per CTA into g_mbs_timing and read with mbs_timing_read.
+//   0 producer waits on `empty`      1 MMA waits on `acc_empty`
+//   2 MMA waits on `full`            3 MMA waits on `sfready`
+//   4 transposer waits on `full`     5 transposer work
+//   6 epilogue waits on `acc_full`   7 epilogue work
+//   8 stream-K owner flag wait       9 CTA lifetime (thread 0)
+//  10 stages issued (producer)      11 MMA issue work
+#ifndef MBS_TIMING
+#define MBS_TIMING 0
+#endif
+#if MBS_TIMING
+__device__ unsigned long long g_mbs_timing[16];
+#define MBS_TSTART() const long long _mbs_t0 = clock64()
+#define MBS_TADD(acc, b) (acc)[b] += (unsigned long long)(clock64() - _mbs_t0)
+#define MBS_TFLUSH(acc)                                              \
+    do                                                               \
+    {                                                                \
+        for (int _b = 0; _b < 16; ++_b)                              \
+            if ((acc)[_b]) atomicAdd(&g_mbs_timing[_b], (acc)[_b]);  \
+    } while (0)
+#else
+#define MBS_TSTART() \
+    do               \
+    {                \
+    } while (0)
+#define MBS_TADD(acc, b) \
+    do                   \
+    {                    \
+    } while (0)
+#define MBS_TFLUSH(acc) \
+    do                  \
+    {                   \
+    } while (0)
+#endif
+
 // f(b) = 1 / (1 + b/256): b fills the top 8 mantissa bits of 1.0f; the
 // reciprocal is IEEE round-to-nearest (test_gemm_a4w4.py:47-51).
 __device__ __forceinline__ float byte_to_factor(uint32_t b)
@@ -255,6 +291,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    unsigned long long tacc[16] = {0};
+#if MBS_TIMING
+    const long long t_kernel0 = clock64();
+#endif
 
     if (threadIdx.x == 0)
     {
@@ -300,11 +340,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 const int r0 = tr * BM, c0 = tc * BN;
                 for (int ks = w.k0; ks < w.k1; ++ks)
                 {
-                    if (!mbar_wait(&empty[slot], phase ^ 1, abort_flag))
+                    bool ok_empty;
+                    {
+                        MBS_TSTART();
+                        ok_empty = mbar_wait(&empty[slot], phase ^ 1, abort_flag);
+                        MBS_TADD(tacc, 0);
+                    }
+                    if (!ok_empty)
                     {
                         raise_error(p, abort_flag);
                         goto producer_done;
                     }
+#if MBS_TIMING
+                    tacc[10] += 1;
+#endif
                     uint8_t* st = smem + slot * CF::STAGE_BYTES;
                     mbar_arrive_expect_tx(&full[slot], CF::TX_BYTES);
                     if (CF::R_PRESHUF)
@@ -345,7 +394,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             Work w;
             for (int i = 0; get_work(p, i, w); ++i)
             {
-                if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, abort_flag))
+                bool ok_acc;
+                {
+                    MBS_TSTART();
+                    ok_acc = mbar_wait(&acc_empty[acc], acc_phase ^ 1, abort_flag);
+                    MBS_TADD(tacc, 1);
+                }
+                if (!ok_acc)
                 {
                     raise_error(p, abort_flag);
                     break;
@@ -355,13 +410,24 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 bool ok = true;
                 for (int ks = w.k0; ks < w.k1; ++ks)
                 {
-                    if (!mbar_wait(&full[slot], phase, abort_flag) ||
-                        !mbar_wait(&sfready[slot], phase, abort_flag))
+                    bool ok_full, ok_sf;
+                    {
+                        MBS_TSTART();
+                        ok_full = mbar_wait(&full[slot], phase, abort_flag);
+                        MBS_TADD(tacc, 2);
+                    }
+                    {
+                        MBS_TSTART();
+                        ok_sf = ok_full && mbar_wait(&sfready[slot], phase, abort_flag);
+                        MBS_TADD(tacc, 3);
+                    }
+                    if (!ok_sf)
                     {
                         raise_error(p, abort_flag);
                         ok = false;
                         break;
                     }
+                    MBS_TSTART();
                     tc_fence_after();
                     const uint8_t* st = smem + slot * CF::STAGE_BYTES;
                     const uint32_t sf_r = tmem_base + CF::SF_BASE + slot * CF::SF_STAGE_COLS;
@@ -395,6 +461,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                                     (ks > w.k0 || j > 0) ? 1u : 0u);
                     }
                     tc_commit(&empty[slot]);
+                    MBS_TADD(tacc, 11);
                     if (++slot == STAGES)
                     {
                         slot = 0;
@@ -426,12 +493,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             bool ok = true;
             for (int ks = w.k0; ks < w.k1; ++ks)
             {
-                if (!mbar_wait(&full[slot], phase, abort_flag))
+                bool ok_full;
+                {
+                    MBS_TSTART();
+                    ok_full = mbar_wait(&full[slot], phase, abort_flag);
+                    MBS_TADD(tacc, 4);
+                }
+                if (!ok_full)
                 {
                     if (lane == 0) raise_error(p, abort_flag);
                     ok = false;
                     break;
                 }
+                MBS_TSTART();
                 uint8_t* st = smem + slot * CF::STAGE_BYTES;
                 // R side: 128 rows, one 128-row block, 2 scale groups of 4.
                 transpose_side<BM, CF::R_MACRO>(st + CF::R_RAW_OFF, st + CF::R_ATOM_OFF, ks, lane);
@@ -439,6 +513,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&sfready[slot]);
+                MBS_TADD(tacc, 5);
                 if (++slot == STAGES)
                 {
                     slot = 0;
@@ -462,11 +537,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         Work w;
         for (int i = 0; get_work(p, i, w); ++i)
         {
-            if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag))
+            bool ok_acc;
+            {
+                MBS_TSTART();
+                ok_acc = mbar_wait(&acc_full[acc], acc_phase, abort_flag);
+                MBS_TADD(tacc, 6);
+            }
+            if (!ok_acc)
             {
                 if (lane == 0) raise_error(p, abort_flag);
                 break;
             }
+            MBS_TSTART();
             tc_fence_after();
             const int tr = w.tile % p.tiles_r, tc = w.tile / p.tiles_r;
             const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN + half * COLS;
@@ -500,6 +582,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     while (c_last + 1 < (int)gridDim.x && sk_start(p, c_last + 1) < tile_end) ++c_last;
                     if (threadIdx.x == EPI_WARP0 * 32)
                     {
+#if MBS_TIMING
+                        const long long t_flag0 = clock64();
+#endif
                         const unsigned long long t0 = globaltimer_ns();
                         for (int c = c_first; c <= c_last; ++c)
                         {
@@ -512,6 +597,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                                 }
                             }
                         }
+#if MBS_TIMING
+                        tacc[8] += (unsigned long long)(clock64() - t_flag0);
+#endif
                     }
                     named_bar_sync(1, NUM_EPI_THREADS);
                 }
@@ -593,6 +681,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&acc_empty[acc]);
+            MBS_TADD(tacc, 7);
             if (CF::ACC_BUFS == 2)
             {
                 acc ^= 1;
@@ -609,6 +698,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     __syncthreads();
     tc_fence_after();
     if (warp == 1) tmem_dealloc(tmem_base, CF::TMEM_COLS);
+#if MBS_TIMING
+    if (threadIdx.x == 0) tacc[9] = (unsigned long long)(clock64() - t_kernel0);
+    if (lane == 0 && (warp <= 2 || warp == EPI_WARP0)) MBS_TFLUSH(tacc);
+#else
+    (void)tacc;
+#endif
 }
 
 }  // namespace gemm
@@ -650,6 +745,8 @@ Plan make_plan(int M, int N, int K, int num_sms)
 {
     Plan pl{};
     pl.swap = M <= 64;
+    const int force_swap = env_int("MBS_FORCE_SWAP", -1);
+    if (force_swap == 0 || force_swap == 1) pl.swap = force_swap == 1;
     pl.bn = pl.swap ? (M <= 32 ? 32 : 64) : 256;
     pl.k_stages = (K + BK - 1) / BK;
     if (pl.swap)
@@ -908,6 +1005,20 @@ int run(const Problem& pb, void* ws, size_t ws_bytes, bool internal_ws, cudaStre
 }  // namespace mbs
 
 using mbs::gemm::Problem;
+
+#if MBS_TIMING
+// Debug builds only: per-role cycle buckets summed over all CTAs (see above).
+extern "C" int mbs_timing_read(unsigned long long* host, int reset)
+{
+    cudaError_t e = cudaMemcpyFromSymbol(host, mbs::gemm::g_mbs_timing, 16 * sizeof(unsigned long long));
+    if (e == cudaSuccess && reset)
+    {
+        unsigned long long z[16] = {0};
+        e = cudaMemcpyToSymbol(mbs::gemm::g_mbs_timing, z, sizeof(z));
+    }
+    return e == cudaSuccess ? MBS_OK : MBS_ERR_CUDA;
+}
+#endif
 
 extern "C" int gemm_a4w4_mxfp4_launch(const uint8_t* A, const uint8_t* B, const uint8_t* AScale,
                                       const uint8_t* BScale, const uint8_t* AFactor,

@@ -175,6 +175,12 @@ __device__ __forceinline__ void tc_cp_32x128b_warpx4(uint32_t taddr, uint64_t sd
                  : "memory");
 }
 
+// Copy 128 rows x 32 bytes of shared memory into 8 TMEM columns: lane i gets row i.
+__device__ __forceinline__ void tc_cp_128x256b(uint32_t taddr, uint64_t sdesc)
+{
+    asm volatile("tcgen05.cp.cta_group::1.128x256b [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+
 __device__ __forceinline__ void tc_wait_ld()
 {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
