@@ -102,6 +102,27 @@ int mbs_gemm_a4w4_macro_launch_ws(const uint8_t* A, const uint8_t* B, const uint
                                   int scaleN_pad, int mb_ld, void* workspace,
                                   size_t workspace_bytes, void* stream);
 
+/*
+ * Allocation-free variant of mbs_gemm_a4w4_launch_ws for callers that may not
+ * allocate device memory (for example a plugin whose host framework owns all
+ * device allocations, or a loop where cudaMalloc's implicit synchronisation
+ * is not acceptable).  No counterpart in the reference.
+ *
+ * Scratch comes from a static 8 MiB __device__ buffer inside the library,
+ * which every GPU that loads the library keeps until the process exits.
+ * Shapes whose schedule needs more scratch than that are rejected with
+ * MBS_ERR_WORKSPACE (use mbs_gemm_a4w4_launch_ws for them); shapes that need
+ * none never touch it.  The first call on each device looks up the buffer's
+ * device address (cudaGetSymbolAddress), so make that first call before any
+ * stream capture.  All calls share the one buffer and it keeps the last
+ * call's contents: calls that overlap on the GPU (e.g. on two streams) race.
+ * The caller still provides A, B, the scales, the factors and out.
+ */
+int mbs_gemm_a4w4_launch_noalloc(const uint8_t* A, const uint8_t* B, const uint8_t* AScale,
+                                 const uint8_t* BScale, const uint8_t* AFactor,
+                                 const uint8_t* BFactor, void* out, int M, int N, int K, int Mpad,
+                                 int scaleN_pad, void* stream);
+
 /* ---- quantiser and layout kernels ------------------------------------ */
 
 /*

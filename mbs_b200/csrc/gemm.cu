@@ -1069,3 +1069,84 @@ extern "C" int mbs_gemm_a4w4_macro_launch_ws(const uint8_t* A, const uint8_t* B,
     Problem pb{A, B, AScale, BScaleMacro, AFactor, BFactor, out, M, N, K, Mpad, scaleN_pad, mb_ld, true};
     return mbs::gemm::run(pb, workspace, workspace_bytes, false, reinterpret_cast<cudaStream_t>(stream));
 }
+
+// ===================================================== allocation-free entry
+// Some callers cannot allocate device memory: a plugin running inside a host
+// framework that owns every device allocation (and its memory budget), or a
+// latency-critical loop where a cudaMalloc (which can synchronise the device)
+// is not allowed.  mbs_gemm_a4w4_launch_noalloc serves them with scratch that
+// lives in the library image itself: a fixed-size __device__ array that every
+// GPU loading the library holds until the process exits.
+namespace mbs {
+namespace gemm {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = (size_t)8 << 20;  // 8 MiB per device
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+// Device address of g_noalloc_scratch on `device` (which must be current).
+// Looked up once per device; in host code the symbol itself is only a
+// host-side stand-in and must never be handed to a kernel.
+void* noalloc_scratch_address(int device, int* status)
+{
+    static std::mutex mu;
+    static void* addr[64] = {nullptr};
+    std::lock_guard<std::mutex> lk(mu);
+    if (device < 0 || device >= 64)
+    {
+        *status = fail(MBS_ERR_DEVICE, "device index %d out of range", device);
+        return nullptr;
+    }
+    if (addr[device] == nullptr)
+    {
+        void* p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || p == nullptr)
+        {
+            *status = cuda_fail(e, "cudaGetSymbolAddress (no-alloc scratch)");
+            return nullptr;
+        }
+        addr[device] = p;
+    }
+    return addr[device];
+}
+
+}  // namespace
+}  // namespace gemm
+}  // namespace mbs
+
+extern "C" int mbs_gemm_a4w4_launch_noalloc(const uint8_t* A, const uint8_t* B,
+                                            const uint8_t* AScale, const uint8_t* BScale,
+                                            const uint8_t* AFactor, const uint8_t* BFactor, void* out,
+                                            int M, int N, int K, int Mpad, int scaleN_pad,
+                                            void* stream)
+{
+    using namespace mbs::gemm;
+    mbs::clear_error();
+    Problem pb{A, B, AScale, BScale, AFactor, BFactor, out, M, N, K, Mpad, scaleN_pad, 0, false};
+    int st = validate(pb);
+    if (st) return st;
+    mbs::DeviceInfo dev;
+    st = mbs::current_device(&dev);
+    if (st) return st;
+    const Plan pl = make_plan(M, N, K, dev.num_sms);
+    if (pl.ws_bytes > kNoAllocScratchBytes)
+        return mbs::fail(MBS_ERR_WORKSPACE,
+                         "mbs_gemm_a4w4_launch_noalloc: this shape needs %zu bytes of scratch, more "
+                         "than the %zu-byte static buffer; use mbs_gemm_a4w4_launch_ws",
+                         pl.ws_bytes, kNoAllocScratchBytes);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    void* ws = nullptr;
+    if (pl.ws_bytes > 0)
+    {
+        ws = noalloc_scratch_address(dev.device, &st);
+        if (ws == nullptr) return st;
+        // The stream-K flags must start at zero.  A completed launch leaves
+        // them zero, but one that stopped early may not have, so clear them.
+        const size_t flags_off = (size_t)pl.G * BM * pl.bn * sizeof(float);
+        cudaError_t e = cudaMemsetAsync(static_cast<uint8_t*>(ws) + flags_off, 0,
+                                        (size_t)pl.G * sizeof(unsigned), s);
+        if (e != cudaSuccess) return mbs::cuda_fail(e, "cudaMemsetAsync (no-alloc flags)");
+    }
+    return dispatch(pb, pl, dev, ws, s);
+}

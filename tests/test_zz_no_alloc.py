@@ -1,0 +1,70 @@
+"""The allocation-free GEMM entry point, through the C ABI.
+
+mbs_gemm_a4w4_launch_noalloc exists for callers that may not allocate device
+memory (a plugin whose host framework owns every device allocation, or a loop
+that cannot afford cudaMalloc's implicit synchronisation).  Its scratch is a
+static buffer inside the library; the caller passes only inputs and outputs.
+Here its output must match the workspace entry point's on the same inputs,
+within the GEMM parity tolerance, on two calls in a row (the second call
+reuses the scratch the first one left behind).  This file is collected last
+and also passes when run alone in a fresh process.
+"""
+
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import mxfp4_oracle as O
+from tests.gpu_helpers import Case
+
+pytestmark = pytest.mark.gpu
+
+
+def _stream():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _args(c, out):
+    return (c.A.data_ptr(), c.B.data_ptr(), c.A_scale.data_ptr(), c.B_scale.data_ptr(),
+            c.A_factor.data_ptr(), c.B_factor.data_ptr(), out.data_ptr(),
+            c.M, c.N, c.K, (c.M + 31) // 32 * 32, O.scale_n_pad(c.K))
+
+
+# (8, 4096, 2048) and (48, 2048, 1024) take the stream-K schedule (scratch in
+# the static buffer); (4096, 4096, 512) the data-parallel one (no scratch).
+@pytest.mark.parametrize("M,N,K", [(8, 4096, 2048), (48, 2048, 1024), (4096, 4096, 512)])
+def test_noalloc_matches_workspace_entry_point(M, N, K):
+    from mbs_b200 import _lib
+    L = _lib.lib()
+    c = Case(M, N, K, seed=M + K, factors=True)
+    Mpad = (M + 31) // 32 * 32
+    ref_out = torch.empty((Mpad, N), dtype=torch.bfloat16, device="cuda")
+    need = int(L.mbs_gemm_a4w4_workspace_size(M, N, K))
+    ws = torch.zeros(max(need, 256), dtype=torch.uint8, device="cuda")
+    st = L.mbs_gemm_a4w4_launch_ws(*_args(c, ref_out), ws.data_ptr(), ws.numel(), _stream())
+    assert st == 0, L.mbs_last_error_message()
+    torch.cuda.synchronize()
+    ref = ref_out[:M].float().cpu().numpy()
+    bound = O.gemm_abs_bound(c.qa, c.qb, c.sa, c.sb)
+    for call in range(2):
+        out = torch.full((Mpad, N), -3.0, dtype=torch.bfloat16, device="cuda")
+        st = L.mbs_gemm_a4w4_launch_noalloc(*_args(c, out), _stream())
+        assert st == 0, L.mbs_last_error_message()
+        torch.cuda.synchronize()
+        ok, ratio, nbad = O.check_gemm(out[:M].float().cpu().numpy(), ref, bound)
+        assert ok, f"call {call}: {nbad} elements differ (max ratio {ratio})"
+        assert torch.all(out[M:] == -3.0), "rows >= M were written"
+
+
+def test_noalloc_rejects_shapes_beyond_its_scratch():
+    from mbs_b200 import _lib
+    L = _lib.lib()
+    # 1024x4096x1024: 128 tiles of 128x256 -> stream-K on 148 CTAs with
+    # 148 x 128 KB of partials, more than the 8 MiB static buffer
+    c = Case(1024, 4096, 1024, seed=5, factors=True)
+    out = torch.empty((1024, 4096), dtype=torch.bfloat16, device="cuda")
+    st = L.mbs_gemm_a4w4_launch_noalloc(*_args(c, out), _stream())
+    assert st == 5  # MBS_ERR_WORKSPACE
+    assert b"static buffer" in L.mbs_last_error_message()
