@@ -114,7 +114,8 @@ struct Cfg
 
     // barriers: full, sfready, empty [STAGES]; acc_full, acc_empty [2]; tmem slot; abort
     static constexpr int BAR_BYTES = (3 * STAGES + 4) * 8 + 16;
-    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + 1024;  // +1024 alignment slack
+    static constexpr int EPI_BYTES = (BM + BN) * 4;  // epilogue factor staging
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + EPI_BYTES + 1024;  // +1024 alignment slack
     static_assert(SMEM_BYTES <= 232448, "shared memory budget");
     static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN");
 };
@@ -288,6 +289,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     uint64_t* acc_empty = acc_full + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    float* epi_f = reinterpret_cast<float*>(smem + STAGES * CF::STAGE_BYTES + CF::BAR_BYTES);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -301,7 +303,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         for (int s = 0; s < STAGES; ++s)
         {
             mbar_init(&full[s], 1);
-            mbar_init(&sfready[s], 1);
+            mbar_init(&sfready[s], 2);
             mbar_init(&empty[s], 1);
         }
         for (int b = 0; b < 2; ++b)
@@ -482,9 +484,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             }
         }
     }
-    else if (warp == 2)
+    else if (warp == 2 || warp == 3)
     {
-        // ------------------------------------------------ scale transposer
+        // ------------------------------------------------ scale transposers
+        // warp 2 rewrites the R operand's scales, warp 3 the C operand's.
+        const bool r_side = warp == 2;
         int slot = 0;
         uint32_t phase = 0;
         Work w;
@@ -507,9 +511,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 }
                 MBS_TSTART();
                 uint8_t* st = smem + slot * CF::STAGE_BYTES;
-                // R side: 128 rows, one 128-row block, 2 scale groups of 4.
-                transpose_side<BM, CF::R_MACRO>(st + CF::R_RAW_OFF, st + CF::R_ATOM_OFF, ks, lane);
-                transpose_side<BN, CF::C_MACRO>(st + CF::C_RAW_OFF, st + CF::C_ATOM_OFF, ks, lane);
+                if (r_side)
+                    transpose_side<BM, CF::R_MACRO>(st + CF::R_RAW_OFF, st + CF::R_ATOM_OFF, ks, lane);
+                else
+                    transpose_side<BN, CF::C_MACRO>(st + CF::C_RAW_OFF, st + CF::C_ATOM_OFF, ks, lane);
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&sfready[slot]);
@@ -526,17 +531,50 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     else if (warp >= EPI_WARP0)
     {
         // ------------------------------------------------ epilogue
+        // Each thread owns one accumulator row (TMEM lane) and half of the
+        // BN columns.  The output path drains its columns from TMEM into
+        // registers (scaled, rounded to bf16), releases the accumulator so
+        // the next tile's MMAs can start, and only then stores.
         const int e = warp - EPI_WARP0;
         const int quarter = warp & 3;         // TMEM lanes [32*quarter, 32*quarter + 32)
         const int half = e >> 2;              // which half of the BN columns
         const int row = quarter * 32 + lane;  // accumulator row (TMEM lane)
+        const int et = threadIdx.x - EPI_WARP0 * 32;  // 0 .. NUM_EPI_THREADS-1
         constexpr int COLS = BN / 2;
+        constexpr int NCH = COLS / 16;
+        constexpr int BATCH = NCH < 4 ? NCH : 4;
         const bool has_factor = (p.a_factor != nullptr) || (p.b_factor != nullptr);
+        // R rows are activations (non-swap) or weights (swap); C columns the other.
+        const uint8_t* r_factor = CF::SWAP ? p.b_factor : p.a_factor;
+        const uint8_t* c_factor = CF::SWAP ? p.a_factor : p.b_factor;
+        const int r_extent = CF::SWAP ? p.N : p.M;
+        const int c_extent = CF::SWAP ? p.M : p.N;
+        float* fr_s = epi_f;       // [BM] row factors of the current tile
+        float* fc_s = epi_f + BM;  // [BN] column factors
         int acc = 0;
         uint32_t acc_phase = 0;
         Work w;
         for (int i = 0; get_work(p, i, w); ++i)
         {
+            const int tr = w.tile % p.tiles_r, tc = w.tile / p.tiles_r;
+            const int r0 = tr * BM, c0 = tc * BN;
+            const bool nonowner = p.sk && w.k0 > 0;
+            const bool owner = p.sk && w.k0 == 0 && w.k1 < p.k_stages;
+            if (has_factor && !nonowner)
+            {
+                named_bar_sync(1, NUM_EPI_THREADS);  // previous tile's readers are done
+                if (et < BM)
+                {
+                    const int r = r0 + et;
+                    fr_s[et] = (r_factor != nullptr && r < r_extent) ? byte_to_factor(r_factor[r]) : 1.0f;
+                }
+                if (et < BN)
+                {
+                    const int c = c0 + et;
+                    fc_s[et] = (c_factor != nullptr && c < c_extent) ? byte_to_factor(c_factor[c]) : 1.0f;
+                }
+                named_bar_sync(1, NUM_EPI_THREADS);
+            }
             bool ok_acc;
             {
                 MBS_TSTART();
@@ -550,10 +588,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             }
             MBS_TSTART();
             tc_fence_after();
-            const int tr = w.tile % p.tiles_r, tc = w.tile / p.tiles_r;
             const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN + half * COLS;
-            const bool nonowner = p.sk && w.k0 > 0;
-            const bool owner = p.sk && w.k0 == 0 && w.k1 < p.k_stages;
+            const bool row_valid = r0 + row < r_extent;
             if (nonowner)
             {
                 float* part = p.partials + (size_t)blockIdx.x * (BM * BN);
@@ -563,13 +599,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     uint32_t v[16];
                     tc_ld_32x32b_x16(taddr + c, v);
                     tc_wait_ld();
+                    if (row_valid)
+                    {
 #pragma unroll
-                    for (int t = 0; t < 16; ++t)
-                        __stcg(part + (size_t)(half * COLS + c + t) * BM + row, __uint_as_float(v[t]));
+                        for (int t = 0; t < 16; ++t)
+                            __stcg(part + (size_t)(half * COLS + c + t) * BM + row, __uint_as_float(v[t]));
+                    }
                 }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&acc_empty[acc]);
                 __threadfence();
                 named_bar_sync(1, NUM_EPI_THREADS);
-                if (threadIdx.x == EPI_WARP0 * 32) st_release_gpu(&p.flags[blockIdx.x], 1u);
+                if (et == 0) st_release_gpu(&p.flags[blockIdx.x], 1u);
             }
             else
             {
@@ -580,7 +622,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     c_first = blockIdx.x + 1;
                     c_last = blockIdx.x;
                     while (c_last + 1 < (int)gridDim.x && sk_start(p, c_last + 1) < tile_end) ++c_last;
-                    if (threadIdx.x == EPI_WARP0 * 32)
+                    if (et == 0)
                     {
 #if MBS_TIMING
                         const long long t_flag0 = clock64();
@@ -603,70 +645,78 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     }
                     named_bar_sync(1, NUM_EPI_THREADS);
                 }
-#pragma unroll 1
-                for (int c = 0; c < COLS; c += 16)
+                uint32_t packed[COLS / 2];
+                const float fr = has_factor ? fr_s[row] : 1.0f;
+#pragma unroll
+                for (int b0 = 0; b0 < NCH; b0 += BATCH)
                 {
-                    uint32_t v[16];
-                    tc_ld_32x32b_x16(taddr + c, v);
+                    uint32_t v[BATCH][16];
+#pragma unroll
+                    for (int b = 0; b < BATCH; ++b) tc_ld_32x32b_x16(taddr + (b0 + b) * 16, v[b]);
                     tc_wait_ld();
-                    float x[16];
 #pragma unroll
-                    for (int t = 0; t < 16; ++t) x[t] = __uint_as_float(v[t]);
-                    for (int cc = c_first; cc <= c_last; ++cc)
+                    for (int b = 0; b < BATCH; ++b)
                     {
-                        const float* part = p.partials + (size_t)cc * (BM * BN);
+                        const int cb = half * COLS + (b0 + b) * 16;  // first tile column of the chunk
+                        float x[16];
 #pragma unroll
-                        for (int t = 0; t < 16; ++t)
-                            x[t] += __ldcg(part + (size_t)(half * COLS + c + t) * BM + row);
+                        for (int t = 0; t < 16; ++t) x[t] = __uint_as_float(v[b][t]);
+                        for (int cc = c_first; cc <= c_last; ++cc)
+                        {
+                            const float* part = p.partials + (size_t)cc * (BM * BN);
+#pragma unroll
+                            for (int t = 0; t < 16; ++t) x[t] += __ldcg(part + (size_t)(cb + t) * BM + row);
+                        }
+                        if (has_factor)
+                        {
+#pragma unroll
+                            for (int t = 0; t < 16; ++t) x[t] = __fmul_rn(x[t], __fmul_rn(fr, fc_s[cb + t]));
+                        }
+#pragma unroll
+                        for (int t = 0; t < 8; ++t)
+                        {
+                            __nv_bfloat162 h = __floats2bfloat162_rn(x[2 * t], x[2 * t + 1]);
+                            packed[(b0 + b) * 8 + t] = *reinterpret_cast<uint32_t*>(&h);
+                        }
                     }
+                }
+                // accumulator drained: let the next tile's MMAs in
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&acc_empty[acc]);
+                if (row_valid)
+                {
                     if (!CF::SWAP)
                     {
-                        const int m = tr * BM + row;
-                        const int n = tc * BN + half * COLS + c;
-                        if (m < p.M && n < p.N)
+                        const int m = r0 + row;
+                        __nv_bfloat16* orow = p.out + (size_t)m * p.N;
+#pragma unroll
+                        for (int ch = 0; ch < NCH; ++ch)
                         {
-                            if (has_factor)
+                            const int n = c0 + half * COLS + ch * 16;
+                            if (n < p.N)
                             {
-                                const float fa = p.a_factor ? byte_to_factor(p.a_factor[m]) : 1.0f;
-#pragma unroll
-                                for (int t = 0; t < 16; ++t)
-                                {
-                                    const float fb = p.b_factor ? byte_to_factor(p.b_factor[n + t]) : 1.0f;
-                                    x[t] = __fmul_rn(x[t], __fmul_rn(fa, fb));
-                                }
+                                uint4* dst = reinterpret_cast<uint4*>(orow + n);
+                                dst[0] = make_uint4(packed[ch * 8 + 0], packed[ch * 8 + 1], packed[ch * 8 + 2],
+                                                    packed[ch * 8 + 3]);
+                                dst[1] = make_uint4(packed[ch * 8 + 4], packed[ch * 8 + 5], packed[ch * 8 + 6],
+                                                    packed[ch * 8 + 7]);
                             }
-                            uint32_t packed[8];
-#pragma unroll
-                            for (int t = 0; t < 8; ++t)
-                            {
-                                __nv_bfloat162 h = __floats2bfloat162_rn(x[2 * t], x[2 * t + 1]);
-                                packed[t] = *reinterpret_cast<uint32_t*>(&h);
-                            }
-                            uint4* dst = reinterpret_cast<uint4*>(p.out + (size_t)m * p.N + n);
-                            dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-                            dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
                         }
                     }
                     else
                     {
-                        const int n = tr * BM + row;
-                        if (n < p.N)
-                        {
-                            const float fb = p.b_factor ? byte_to_factor(p.b_factor[n]) : 1.0f;
+                        const int n = r0 + row;
 #pragma unroll
-                            for (int t = 0; t < 16; ++t)
+                        for (int t = 0; t < COLS; ++t)
+                        {
+                            const int m = c0 + half * COLS + t;
+                            if (m < p.M)
                             {
-                                const int m = tc * BN + half * COLS + c + t;
-                                if (m < p.M)
-                                {
-                                    float y = x[t];
-                                    if (has_factor)
-                                    {
-                                        const float fa = p.a_factor ? byte_to_factor(p.a_factor[m]) : 1.0f;
-                                        y = __fmul_rn(y, __fmul_rn(fa, fb));
-                                    }
-                                    p.out[(size_t)m * p.N + n] = __float2bfloat16_rn(y);
-                                }
+                                const uint32_t pr = packed[t >> 1];
+                                const unsigned short hbits = (t & 1) ? (unsigned short)(pr >> 16)
+                                                                     : (unsigned short)(pr & 0xFFFFu);
+                                p.out[(size_t)m * p.N + n] = __ushort_as_bfloat16(hbits);
                             }
                         }
                     }
@@ -674,13 +724,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 if (owner)
                 {
                     named_bar_sync(1, NUM_EPI_THREADS);
-                    if (threadIdx.x == EPI_WARP0 * 32)
+                    if (et == 0)
                         for (int c = c_first; c <= c_last; ++c) p.flags[c] = 0u;
                 }
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&acc_empty[acc]);
             MBS_TADD(tacc, 7);
             if (CF::ACC_BUFS == 2)
             {
