@@ -212,6 +212,14 @@ __device__ __forceinline__ float byte_to_factor(uint32_t b)
     return __frcp_rn(__uint_as_float(0x3F800000u | (b << 15)));
 }
 
+// Byte offset of scale (r, b) in a flatS buffer (kernel/gemm_a4w4.hip:97-105).
+__device__ __forceinline__ long long flat_s_offset(int r, int b, int snp)
+{
+    const int r32 = r & 31, b8 = b & 7;
+    return (long long)(r32 >> 4) + (long long)(b8 >> 2) * 2 + (long long)(r32 & 15) * 4 +
+           (long long)(b8 & 3) * 64 + (long long)(b >> 3) * 256 + (long long)(r >> 5) * 32 * snp;
+}
+
 // One operand's raw scale bytes for one K-stage (8 groups of 32 K) ->
 // tcgen05.cp source blocks.  Output block (q, rb) covers rows 128*rb ..
 // 128*rb+127 and K-groups 4q .. 4q+3 of the stage: 512 B with row r's four
@@ -267,6 +275,117 @@ __device__ __forceinline__ void transpose_side(const uint8_t* raw, uint8_t* atom
             *reinterpret_cast<uint32_t*>(atoms + (q * RB + (r >> 7)) * 512 + (r & 31) * 16 +
                                          ((r >> 5) & 3) * 4) = v;
         }
+    }
+}
+
+// flatS groups [0, G_TOTAL) of two operands handled by LANES threads: groups
+// below G_A belong to operand A (raw_a/atoms_a, RB_A 128-row blocks), the
+// rest to operand B.  Same per-group transform as transpose_side.
+template <int G_A, int RB_A, int G_TOTAL, int RB_B, int LANES>
+__device__ __forceinline__ void transpose_groups(const uint8_t* raw_a, uint8_t* atoms_a, const uint8_t* raw_b,
+                                                 uint8_t* atoms_b, int t)
+{
+    constexpr int OPS = G_TOTAL * 16;
+#pragma unroll
+    for (int op = t; op < OPS; op += LANES)
+    {
+        const int gg = op >> 4, rho = op & 15;
+        const bool is_a = gg < G_A;
+        const int g = is_a ? gg : gg - G_A;
+        const uint32_t* raw32 = reinterpret_cast<const uint32_t*>(is_a ? raw_a : raw_b);
+        uint8_t* atoms = is_a ? atoms_a : atoms_b;
+        const int RB = is_a ? RB_A : RB_B;
+        const uint32_t w0 = raw32[g * 64 + rho];
+        const uint32_t w1 = raw32[g * 64 + 16 + rho];
+        const uint32_t w2 = raw32[g * 64 + 32 + rho];
+        const uint32_t w3 = raw32[g * 64 + 48 + rho];
+        const uint32_t t0 = __byte_perm(w0, w1, 0x5140);
+        const uint32_t t1 = __byte_perm(w2, w3, 0x5140);
+        const uint32_t t2 = __byte_perm(w0, w1, 0x7362);
+        const uint32_t t3 = __byte_perm(w2, w3, 0x7362);
+        const uint32_t o[4] = {__byte_perm(t0, t1, 0x5410), __byte_perm(t0, t1, 0x7632),
+                               __byte_perm(t2, t3, 0x5410), __byte_perm(t2, t3, 0x7632)};
+#pragma unroll
+        for (int pp = 0; pp < 4; ++pp)
+        {
+            const int r = 32 * g + 16 * (pp & 1) + rho;
+            const int q = pp >> 1;
+            *reinterpret_cast<uint32_t*>(atoms + (q * RB + (r >> 7)) * 512 + (r & 31) * 16 +
+                                         ((r >> 5) & 3) * 4) = o[pp];
+        }
+    }
+}
+
+// Raw scales -> "replicated" blocks for tcgen05.cp.128x256b.  A replicated
+// block is the 512-byte 32x16B block above repeated at +0/+512/+1024/+1536
+// (2 KB = 128 rows x 16 B), so that a 128x256b copy of two such blocks
+// (LBO 2048 B, SBO 128 B) writes exactly what two 32x128b.warpx4 copies would
+// write: lane 32s + l, column c of block j <- row l, bytes 4c..4c+3.
+//   SFA (128 rows): block j = K-group set q   (base + q*2048)
+//   SFB (256 rows): block j = 128-row block b, one 4 KB buffer per q
+// One lane-op = (128-row block b, row-in-16 rho): the four 32-row groups of
+// the block at that rho are transposed together and each (h, q) result row
+// (16 B) is stored to the four replicas.
+template <int G_A, int G_B, int LANES>
+__device__ __forceinline__ void transpose_rep(const uint8_t* raw_a, uint8_t* rep_a, const uint8_t* raw_b,
+                                              uint8_t* rep_b, int t)
+{
+    constexpr int BLK_A = G_A / 4, BLK_B = G_B / 4;
+    constexpr int OPS = (BLK_A + BLK_B) * 16;
+#pragma unroll
+    for (int op = t; op < OPS; op += LANES)
+    {
+        const int blk = op >> 4, rho = op & 15;
+        const bool is_a = blk < BLK_A;
+        const int b = is_a ? blk : blk - BLK_A;
+        const uint32_t* raw32 = reinterpret_cast<const uint32_t*>(is_a ? raw_a : raw_b) + b * 4 * 64;
+        uint32_t o[4][4];  // [group in block][p]
+#pragma unroll
+        for (int gg = 0; gg < 4; ++gg)
+        {
+            const uint32_t w0 = raw32[gg * 64 + rho];
+            const uint32_t w1 = raw32[gg * 64 + 16 + rho];
+            const uint32_t w2 = raw32[gg * 64 + 32 + rho];
+            const uint32_t w3 = raw32[gg * 64 + 48 + rho];
+            const uint32_t t0 = __byte_perm(w0, w1, 0x5140);
+            const uint32_t t1 = __byte_perm(w2, w3, 0x5140);
+            const uint32_t t2 = __byte_perm(w0, w1, 0x7362);
+            const uint32_t t3 = __byte_perm(w2, w3, 0x7362);
+            o[gg][0] = __byte_perm(t0, t1, 0x5410);
+            o[gg][1] = __byte_perm(t0, t1, 0x7632);
+            o[gg][2] = __byte_perm(t2, t3, 0x5410);
+            o[gg][3] = __byte_perm(t2, t3, 0x7632);
+        }
+#pragma unroll
+        for (int pp = 0; pp < 4; ++pp)
+        {
+            const int h = pp & 1, q = pp >> 1;
+            const uint4 v = make_uint4(o[0][pp], o[1][pp], o[2][pp], o[3][pp]);
+            uint8_t* blkp = is_a ? rep_a + q * 2048 : rep_b + q * 4096 + b * 2048;
+            uint8_t* dst = blkp + (16 * h + rho) * 16;
+#pragma unroll
+            for (int s = 0; s < 4; ++s) *reinterpret_cast<uint4*>(dst + s * 512) = v;
+        }
+    }
+}
+
+// Macro-block B scales -> replicated SFB blocks: every row of a 32-row group
+// shares the group's bytes, so each block row is the same 16 bytes.
+template <int LANES>
+__device__ __forceinline__ void transpose_rep_macro_b(const uint8_t* raw, uint8_t* rep_b, int ks, int t)
+{
+    // 2 groups-of-4 x 2 row blocks x 128 rows, 16 B each
+    constexpr int OPS = 2 * 2 * 128;
+#pragma unroll 4
+    for (int op = t; op < OPS; op += LANES)
+    {
+        const int q = op >> 8, b = (op >> 7) & 1, i = op & 127;
+        const uint8_t* src = raw + 8 * (ks & 1) + 4 * q;
+        const uint4 v = make_uint4(*reinterpret_cast<const uint32_t*>(src + (4 * b + 0) * 16),
+                                   *reinterpret_cast<const uint32_t*>(src + (4 * b + 1) * 16),
+                                   *reinterpret_cast<const uint32_t*>(src + (4 * b + 2) * 16),
+                                   *reinterpret_cast<const uint32_t*>(src + (4 * b + 3) * 16));
+        *reinterpret_cast<uint4*>(rep_b + q * 4096 + b * 2048 + i * 16) = v;
     }
 }
 
@@ -741,13 +860,438 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
     }
 
+    __syncwarp();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    __syncwarp();
     if (warp == 1) tmem_dealloc(tmem_base, CF::TMEM_COLS);
 #if MBS_TIMING
     if (threadIdx.x == 0) tacc[9] = (unsigned long long)(clock64() - t_kernel0);
     if (lane == 0 && (warp <= 2 || warp == EPI_WARP0)) MBS_TFLUSH(tacc);
+#else
+    (void)tacc;
+#endif
+}
+
+
+// ====================================================================== CTA pair
+// Prefill kernel on CTA pairs (cluster of 2): one tcgen05.mma.cta_group::2
+// computes a 256 x 256 x 64 block, each CTA contributing 128 rows of A and a
+// 128-row half of B from its own shared memory and holding its 128 x 256
+// accumulator in its own TMEM.  Per SM this halves the B bytes that TMA
+// writes into and the MMA reads out of shared memory compared with the
+// single-CTA 128 x 256 tile.
+//
+// Scales reach it as "scale images" written by scale_image_kernel: per
+// 128-row block of A and per 256-row tile of B, per K stage, the exact bytes
+// tcgen05.cp.128x256b moves into TMEM (see transpose_rep).  Every image is
+// reused by all tiles of its row / column, so building them once per call
+// costs a few microseconds and removes all scale work from the GEMM.
+//
+// Protocol (leader = cluster rank 0):
+//   * both producers wait on their own `empty` slot (the leader's commit
+//     multicasts to both), then TMA their A tile, B half, A-scale image and
+//     the pair's B-scale image with .cta_group::2, completing on the LEADER's
+//     `full` barrier, which the leader's producer arms with both CTAs' bytes;
+//   * the leader's MMA thread issues tcgen05.cp.cta_group::2 (each CTA's
+//     shared memory -> its own TMEM) and the pair MMAs, and multicasts its
+//     commits to both CTAs' `empty` / `acc_full`;
+//   * each CTA's epilogue drains its own TMEM and arrives on the leader's
+//     `acc_empty` (16 warps).
+
+constexpr int IMG_A_BYTES = 2 * 2048;      // per 128 A rows per K stage
+constexpr int IMG_B_BYTES = 2 * 2 * 2048;  // per 256 B rows per K stage
+
+// flatS scales (or macro-block B scales) -> scale images.
+//   A image [rb128][ks][q][s][l][16 B]: word w = SF(128rb + 32w + l, 8ks+4q+k)
+//   B image [tb256][ks][q][b][s][l][16 B]: word w = SF(256tb + 128b + 32w + l, ...)
+// for replicas s = 0..3 (identical).  Rows outside the scale buffer give 0.
+__global__ void __launch_bounds__(256) scale_image_kernel(const uint8_t* __restrict__ sa, int a_rows_buf,
+                                                          int a_blocks, const uint8_t* __restrict__ sb,
+                                                          int b_rows_buf, int b_tiles, int snp, int ks_count,
+                                                          int b_macro, int mb_ld, uint8_t* __restrict__ img_a,
+                                                          uint8_t* __restrict__ img_b)
+{
+    // one thread per (image block, K stage, q, [b], l): 4 words -> 4 replicas
+    const long long na = (long long)a_blocks * ks_count * 2 * 32;
+    const long long nb = (long long)b_tiles * ks_count * 2 * 2 * 32;
+    for (long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x; t < na + nb;
+         t += (long long)gridDim.x * blockDim.x)
+    {
+        const bool is_a = t < na;
+        long long u = is_a ? t : t - na;
+        const int l = (int)(u & 31);
+        u >>= 5;
+        int b = 0;
+        if (!is_a)
+        {
+            b = (int)(u & 1);
+            u >>= 1;
+        }
+        const int q = (int)(u & 1);
+        u >>= 1;
+        const int ks = (int)(u % ks_count);
+        const long long blk = u / ks_count;
+        uint32_t w[4];
+#pragma unroll
+        for (int g = 0; g < 4; ++g)
+        {
+            const long long r = is_a ? blk * 128 + 32 * g + l : blk * 256 + 128 * b + 32 * g + l;
+            uint32_t word = 0;
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+            {
+                const int kb = 8 * ks + 4 * q + k;
+                uint32_t v = 0;
+                if (is_a)
+                {
+                    if (r < a_rows_buf) v = sa[flat_s_offset((int)r, kb, snp)];
+                }
+                else if (b_macro)
+                {
+                    if (r < b_rows_buf) v = sb[(r >> 5) * mb_ld + kb];
+                }
+                else
+                {
+                    if (r < b_rows_buf) v = sb[flat_s_offset((int)r, kb, snp)];
+                }
+                word |= v << (8 * k);
+            }
+            w[g] = word;
+        }
+        const uint4 v4 = make_uint4(w[0], w[1], w[2], w[3]);
+        uint8_t* dst = is_a ? img_a + (blk * ks_count + ks) * IMG_A_BYTES + q * 2048 + l * 16
+                            : img_b + (blk * ks_count + ks) * IMG_B_BYTES + q * 4096 + b * 2048 + l * 16;
+#pragma unroll
+        for (int s = 0; s < 4; ++s) *reinterpret_cast<uint4*>(dst + s * 512) = v4;
+    }
+}
+
+template <int STAGES_>
+struct CfgPair
+{
+    static constexpr int BN = 256;   // pair N (each CTA holds a 128-row half of B)
+    static constexpr int BNH = 128;
+    static constexpr int STAGES = STAGES_;
+    static constexpr int A_DATA = BM * BKB;
+    static constexpr int B_DATA = BNH * BKB;
+    static constexpr int A_DATA_OFF = 0;
+    static constexpr int B_DATA_OFF = A_DATA;
+    static constexpr int A_IMG_OFF = B_DATA_OFF + B_DATA;
+    static constexpr int B_IMG_OFF = A_IMG_OFF + IMG_A_BYTES;
+    static constexpr int STAGE_BYTES = align_up(B_IMG_OFF + IMG_B_BYTES, 1024);
+    static constexpr uint32_t TX = A_DATA + B_DATA + IMG_A_BYTES + IMG_B_BYTES;  // per CTA
+    static constexpr int SF_STAGE_COLS = 8 + 16;
+    static constexpr int SF_BASE = BN;  // one accumulator buffer
+    static constexpr int TMEM_COLS = 512;
+    static_assert(SF_BASE + STAGES * SF_STAGE_COLS <= 512, "TMEM budget");
+    // full, empty [STAGES]; acc_full, acc_empty; tmem slot; abort
+    static constexpr int BAR_BYTES = (2 * STAGES + 2) * 8 + 16;
+    static constexpr int EPI_BYTES = (BM + BN) * 4;
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + EPI_BYTES + 1024;
+    static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+};
+
+template <class CF>
+__global__ void __launch_bounds__(NUM_THREADS, 1) __cluster_dims__(2, 1, 1)
+    mxf4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                          const __grid_constant__ CUtensorMap tm_ia, const __grid_constant__ CUtensorMap tm_ib,
+                          const Params p)
+{
+    constexpr int BN = CF::BN;
+    constexpr int STAGES = CF::STAGES;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~static_cast<uintptr_t>(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * CF::STAGE_BYTES);
+    uint64_t* empty = full + STAGES;
+    uint64_t* acc_full = empty + STAGES;
+    uint64_t* acc_empty = acc_full + 1;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    float* epi_f = reinterpret_cast<float*>(smem + STAGES * CF::STAGE_BYTES + CF::BAR_BYTES);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const bool leader = rank == 0;
+    const int cluster = blockIdx.x >> 1;
+    const int nclusters = gridDim.x >> 1;
+    unsigned long long tacc[16] = {0};
+#if MBS_TIMING
+    const long long t_kernel0 = clock64();
+#endif
+
+    if (threadIdx.x == 0)
+    {
+        for (int s = 0; s < STAGES; ++s)
+        {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(acc_full, 1);
+        mbar_init(acc_empty, 2 * NUM_EPI_WARPS);
+        *abort_flag = 0;
+        fence_mbar_init();
+        prefetch_tmap(&tm_a);
+        prefetch_tmap(&tm_b);
+        prefetch_tmap(&tm_ia);
+        prefetch_tmap(&tm_ib);
+    }
+    if (warp == 1)
+    {
+        tmem_alloc_pair(tmem_slot, CF::TMEM_COLS);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    cluster_sync();  // barriers of both CTAs initialised, TMEM allocated in both
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const int tiles_r2 = (p.M + 2 * BM - 1) / (2 * BM);
+    const int tiles_c = (p.N + BN - 1) / BN;
+    const int ntiles = tiles_r2 * tiles_c;
+
+    if (warp == 0)
+    {
+        if (lane == 0)
+        {
+            const uint32_t full0 = mapa_shared(smem_u32(full), 0);  // leader's full[0]
+            int slot = 0;
+            uint32_t phase = 0;
+            for (int t = cluster; t < ntiles; t += nclusters)
+            {
+                const int tr = t % tiles_r2, tc = t / tiles_r2;
+                const int rb = tr * 2 + (int)rank;  // this CTA's 128-row block of A
+                const int nb0 = tc * BN + (int)rank * CF::BNH;
+                for (int ks = 0; ks < p.k_stages; ++ks)
+                {
+                    bool ok_empty;
+                    {
+                        MBS_TSTART();
+                        ok_empty = mbar_wait(&empty[slot], phase ^ 1, abort_flag);
+                        MBS_TADD(tacc, 0);
+                    }
+                    if (!ok_empty)
+                    {
+                        raise_error(p, abort_flag);
+                        goto pair_producer_done;
+                    }
+                    uint8_t* st = smem + slot * CF::STAGE_BYTES;
+                    const uint32_t fbar = full0 + slot * 8;
+                    if (leader) mbar_arrive_expect_tx(&full[slot], 2 * CF::TX);
+                    tma_load_2d_pair(st + CF::A_DATA_OFF, &tm_a, fbar, ks * BKB, rb * BM);
+                    tma_load_3d_pair(st + CF::B_DATA_OFF, &tm_b, fbar, 0, nb0 / 16, ks * 8);
+                    tma_load_2d_pair(st + CF::A_IMG_OFF, &tm_ia, fbar, 0, (rb * p.k_stages + ks) * (IMG_A_BYTES / 256));
+                    tma_load_2d_pair(st + CF::B_IMG_OFF, &tm_ib, fbar, 0, (tc * p.k_stages + ks) * (IMG_B_BYTES / 256));
+#if MBS_TIMING
+                    tacc[10] += 1;
+#endif
+                    if (++slot == STAGES)
+                    {
+                        slot = 0;
+                        phase ^= 1;
+                    }
+                }
+            }
+        pair_producer_done:;
+        }
+    }
+    else if (warp == 1)
+    {
+        if (lane == 0 && leader)
+        {
+            int slot = 0;
+            uint32_t phase = 0;
+            uint32_t acc_phase = 0;
+            for (int t = cluster; t < ntiles; t += nclusters)
+            {
+                bool ok_acc;
+                {
+                    MBS_TSTART();
+                    ok_acc = mbar_wait(acc_empty, acc_phase ^ 1, abort_flag);
+                    MBS_TADD(tacc, 1);
+                }
+                if (!ok_acc)
+                {
+                    raise_error(p, abort_flag);
+                    break;
+                }
+                tc_fence_after();
+                bool ok = true;
+                for (int ks = 0; ks < p.k_stages; ++ks)
+                {
+                    bool ok_in;
+                    {
+                        MBS_TSTART();
+                        ok_in = mbar_wait(&full[slot], phase, abort_flag);
+                        MBS_TADD(tacc, 2);
+                    }
+                    if (!ok_in)
+                    {
+                        raise_error(p, abort_flag);
+                        ok = false;
+                        break;
+                    }
+                    MBS_TSTART();
+                    tc_fence_after();
+                    const uint8_t* st = smem + slot * CF::STAGE_BYTES;
+                    const uint32_t sf_a = tmem_base + CF::SF_BASE + slot * CF::SF_STAGE_COLS;
+                    const uint32_t sf_b = sf_a + 8;
+                    // 3 copies of 128 rows x 32 B: SFA both K-group sets, SFB one set each
+                    tc_cp_128x256b_pair(sf_a, make_smem_desc(smem_u32(st + CF::A_IMG_OFF), 2048, 128, 0));
+#pragma unroll
+                    for (int q = 0; q < 2; ++q)
+                        tc_cp_128x256b_pair(sf_b + 8 * q,
+                                            make_smem_desc(smem_u32(st + CF::B_IMG_OFF + q * 4096), 2048, 128, 0));
+                    const uint32_t a_base = smem_u32(st + CF::A_DATA_OFF);
+                    const uint32_t b_base = smem_u32(st + CF::B_DATA_OFF);
+#pragma unroll
+                    for (int j = 0; j < BK / MMA_K; ++j)
+                    {
+                        if (ks * BK + j * MMA_K >= p.K) break;
+                        const uint64_t a_desc = make_smem_desc(a_base + j * 32, 16, 1024, 2);
+                        const uint64_t b_desc =
+                            make_smem_desc(b_base + j * 2 * (CF::BNH * 16), CF::BNH * 16, 128, 0);
+                        const uint32_t id = (uint32_t)(j & 1) * 2;
+                        const uint32_t q = (uint32_t)(j >> 1);
+                        tc_mma_mxf4_pair(tmem_base, a_desc, b_desc, make_idesc_mxf4(2 * BM, BN, id, id),
+                                         (sf_a + 4 * q) | (id << 30), (sf_b + 8 * q) | (id << 30),
+                                         (ks > 0 || j > 0) ? 1u : 0u);
+                    }
+                    tc_commit_pair_mc(&empty[slot], 0x3);
+                    MBS_TADD(tacc, 11);
+                    if (++slot == STAGES)
+                    {
+                        slot = 0;
+                        phase ^= 1;
+                    }
+                }
+                if (!ok) break;
+                tc_commit_pair_mc(acc_full, 0x3);
+                acc_phase ^= 1;
+            }
+        }
+    }
+    else if (warp >= EPI_WARP0)
+    {
+        const int e = warp - EPI_WARP0;
+        const int quarter = warp & 3;
+        const int half = e >> 2;
+        const int row = quarter * 32 + lane;
+        const int et = threadIdx.x - EPI_WARP0 * 32;
+        constexpr int COLS = BN / 2;
+        constexpr int NCH = COLS / 16;
+        constexpr int BATCH = 4;
+        const bool has_factor = (p.a_factor != nullptr) || (p.b_factor != nullptr);
+        const uint32_t acc_empty0 = mapa_shared(smem_u32(acc_empty), 0);
+        float* fr_s = epi_f;
+        float* fc_s = epi_f + BM;
+        uint32_t acc_phase = 0;
+        for (int t = cluster; t < ntiles; t += nclusters)
+        {
+            const int tr = t % tiles_r2, tc = t / tiles_r2;
+            const int r0 = tr * 2 * BM + (int)rank * BM;
+            const int c0 = tc * BN;
+            if (has_factor)
+            {
+                named_bar_sync(1, NUM_EPI_THREADS);
+                if (et < BM)
+                {
+                    const int r = r0 + et;
+                    fr_s[et] = (p.a_factor != nullptr && r < p.M) ? byte_to_factor(p.a_factor[r]) : 1.0f;
+                }
+                if (et < BN)
+                {
+                    const int c = c0 + et;
+                    fc_s[et] = (p.b_factor != nullptr && c < p.N) ? byte_to_factor(p.b_factor[c]) : 1.0f;
+                }
+                named_bar_sync(1, NUM_EPI_THREADS);
+            }
+            bool ok_acc;
+            {
+                MBS_TSTART();
+                ok_acc = mbar_wait(acc_full, acc_phase, abort_flag);
+                MBS_TADD(tacc, 6);
+            }
+            if (!ok_acc)
+            {
+                if (lane == 0) raise_error(p, abort_flag);
+                break;
+            }
+            MBS_TSTART();
+            tc_fence_after();
+            const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + half * COLS;
+            uint32_t packed[COLS / 2];
+            const float fr = has_factor ? fr_s[row] : 1.0f;
+#pragma unroll
+            for (int b0 = 0; b0 < NCH; b0 += BATCH)
+            {
+                uint32_t v[BATCH][16];
+#pragma unroll
+                for (int b = 0; b < BATCH; ++b) tc_ld_32x32b_x16(taddr + (b0 + b) * 16, v[b]);
+                tc_wait_ld();
+#pragma unroll
+                for (int b = 0; b < BATCH; ++b)
+                {
+                    const int cb = half * COLS + (b0 + b) * 16;
+                    float x[16];
+#pragma unroll
+                    for (int u = 0; u < 16; ++u) x[u] = __uint_as_float(v[b][u]);
+                    if (has_factor)
+                    {
+#pragma unroll
+                        for (int u = 0; u < 16; ++u) x[u] = __fmul_rn(x[u], __fmul_rn(fr, fc_s[cb + u]));
+                    }
+#pragma unroll
+                    for (int u = 0; u < 8; ++u)
+                    {
+                        __nv_bfloat162 h = __floats2bfloat162_rn(x[2 * u], x[2 * u + 1]);
+                        packed[(b0 + b) * 8 + u] = *reinterpret_cast<uint32_t*>(&h);
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0)
+            {
+                if (leader)
+                    mbar_arrive(acc_empty);
+                else
+                    mbar_arrive_cluster(acc_empty0);
+            }
+            const int m = r0 + row;
+            if (m < p.M)
+            {
+                __nv_bfloat16* orow = p.out + (size_t)m * p.N;
+#pragma unroll
+                for (int ch = 0; ch < NCH; ++ch)
+                {
+                    const int n = c0 + half * COLS + ch * 16;
+                    if (n < p.N)
+                    {
+                        uint4* dst = reinterpret_cast<uint4*>(orow + n);
+                        dst[0] = make_uint4(packed[ch * 8 + 0], packed[ch * 8 + 1], packed[ch * 8 + 2],
+                                            packed[ch * 8 + 3]);
+                        dst[1] = make_uint4(packed[ch * 8 + 4], packed[ch * 8 + 5], packed[ch * 8 + 6],
+                                            packed[ch * 8 + 7]);
+                    }
+                }
+            }
+            MBS_TADD(tacc, 7);
+            acc_phase ^= 1;
+        }
+    }
+
+    __syncwarp();
+    tc_fence_before();
+    cluster_sync();  // no remote arrive or pair MMA can still target this CTA
+    tc_fence_after();
+    __syncwarp();
+    if (warp == 1) tmem_dealloc_pair(tmem_base, CF::TMEM_COLS);
+#if MBS_TIMING
+    if (threadIdx.x == 0) tacc[9] = (unsigned long long)(clock64() - t_kernel0);
+    if (lane == 0 && (warp <= 1 || warp == EPI_WARP0)) MBS_TFLUSH(tacc);
 #else
     (void)tacc;
 #endif
@@ -772,7 +1316,7 @@ struct Problem
 struct Plan
 {
     int bn;
-    bool swap, sk;
+    bool swap, sk, pair;
     int G, tiles_r, tiles_c, k_stages;
     size_t ws_bytes;
 };
@@ -781,6 +1325,18 @@ int env_int(const char* name, int dflt)
 {
     const char* v = getenv(name);
     return (v != nullptr && *v != 0) ? atoi(v) : dflt;
+}
+
+// Workspace of the CTA-pair path: the A and B scale images.
+size_t pair_image_a_bytes(int M, int K)
+{
+    const size_t blocks = (size_t)((M + 2 * BM - 1) / (2 * BM)) * 2;
+    return blocks * ((K + BK - 1) / BK) * IMG_A_BYTES;
+}
+
+size_t pair_image_b_bytes(int N, int K)
+{
+    return (size_t)((N + 255) / 256) * ((K + BK - 1) / BK) * IMG_B_BYTES;
 }
 
 // Path and schedule choice.  Skinny M (decode) swaps the operands so the
@@ -818,6 +1374,16 @@ Plan make_plan(int M, int N, int K, int num_sms)
     pl.G = (int)(units < G ? units : G);
     pl.ws_bytes = pl.sk ? (size_t)pl.G * BM * pl.bn * sizeof(float) + (size_t)align_up(pl.G * 4, 256)
                         : 0;
+    // Large data-parallel problems run on CTA pairs (256 x 256 tiles); their
+    // workspace holds the scale images.
+    pl.pair = !pl.swap && !pl.sk && env_int("MBS_FORCE_PAIR", 1) != 0;
+    if (pl.pair)
+    {
+        const long long t2 = (long long)((M + 2 * BM - 1) / (2 * BM)) * ((N + 255) / 256);
+        const int c = G / 2;
+        pl.G = 2 * (int)(t2 < c ? t2 : c);
+        pl.ws_bytes = pair_image_a_bytes(M, K) + pair_image_b_bytes(N, K);
+    }
     return pl;
 }
 
@@ -906,6 +1472,106 @@ int make_maps(const Problem& pb, const Plan& pl, CUtensorMap* tm_r, CUtensorMap*
     return st;
 }
 
+// TMA descriptors of the CTA-pair kernel: A boxes of 128 rows, B boxes of a
+// 128-row half, and the scale images as rows of 256 bytes.
+int make_maps_pair(const Problem& pb, void* img_a, size_t img_a_bytes, void* img_b, size_t img_b_bytes,
+                   CUtensorMap* tm_a, CUtensorMap* tm_b, CUtensorMap* tm_ia, CUtensorMap* tm_ib)
+{
+    const uint64_t Kp = (uint64_t)pb.K / 2;
+    int st;
+    {
+        const uint64_t dims[2] = {Kp, (uint64_t)pb.M};
+        const uint64_t strides[1] = {Kp};
+        const uint32_t box[2] = {BKB, BM};
+        st = encode_tmap(tm_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, (void*)pb.A, dims, strides, box,
+                         CU_TENSOR_MAP_SWIZZLE_128B);
+        if (st) return st;
+    }
+    {
+        const uint64_t dims[3] = {256, (uint64_t)pb.N / 16, (uint64_t)pb.K / 32};
+        const uint64_t strides[2] = {(uint64_t)pb.K * 8, 256};
+        const uint32_t box[3] = {256, 128 / 16, BK / 32};
+        st = encode_tmap(tm_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, (void*)pb.B, dims, strides, box,
+                         CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (st) return st;
+    }
+    {
+        const uint64_t dims[2] = {256, (uint64_t)(img_a_bytes / 256)};
+        const uint64_t strides[1] = {256};
+        const uint32_t box[2] = {256, IMG_A_BYTES / 256};
+        st = encode_tmap(tm_ia, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, img_a, dims, strides, box,
+                         CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (st) return st;
+    }
+    {
+        const uint64_t dims[2] = {256, (uint64_t)(img_b_bytes / 256)};
+        const uint64_t strides[1] = {256};
+        const uint32_t box[2] = {256, IMG_B_BYTES / 256};
+        st = encode_tmap(tm_ib, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, img_b, dims, strides, box,
+                         CU_TENSOR_MAP_SWIZZLE_NONE);
+    }
+    return st;
+}
+
+template <class CF>
+int launch_pair(const Problem& pb, const Plan& pl, const DeviceInfo& dev, void* ws, cudaStream_t stream)
+{
+    static bool attr_done[64] = {false};
+    static std::mutex mu;
+    auto kernel = mxf4_gemm_pair_kernel<CF>;
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        if (!attr_done[dev.device])
+        {
+            cudaError_t e =
+                cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, CF::SMEM_BYTES);
+            if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute (pair)");
+            attr_done[dev.device] = true;
+        }
+    }
+    const size_t ia = pair_image_a_bytes(pb.M, pb.K);
+    const size_t ib = pair_image_b_bytes(pb.N, pb.K);
+    uint8_t* img_a = static_cast<uint8_t*>(ws);
+    uint8_t* img_b = img_a + ia;
+    CUtensorMap tm_a, tm_b, tm_ia, tm_ib;
+    int st = make_maps_pair(pb, img_a, ia, img_b, ib, &tm_a, &tm_b, &tm_ia, &tm_ib);
+    if (st) return st;
+    // 1) scale images
+    {
+        const int a_blocks = (int)(ia / ((size_t)pl.k_stages * IMG_A_BYTES));
+        const int b_tiles = (int)(ib / ((size_t)pl.k_stages * IMG_B_BYTES));
+        const long long threads = (long long)a_blocks * pl.k_stages * 64 + (long long)b_tiles * pl.k_stages * 128;
+        long long blocks = (threads + 255) / 256;
+        if (blocks > (long long)dev.num_sms * 8) blocks = (long long)dev.num_sms * 8;
+        scale_image_kernel<<<(int)blocks, 256, 0, stream>>>(pb.AS, pb.Mpad, a_blocks, pb.BS,
+                                                            round_up(pb.N, 32), b_tiles, pb.snp, pl.k_stages,
+                                                            pb.macro ? 1 : 0, pb.mb_ld, img_a, img_b);
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return cuda_fail(e, "scale image launch");
+    }
+    // 2) the GEMM on CTA pairs
+    Params p{};
+    p.M = pb.M;
+    p.N = pb.N;
+    p.K = pb.K;
+    p.k_stages = pl.k_stages;
+    p.a_factor = pb.AF;
+    p.b_factor = pb.BF;
+    p.out = static_cast<__nv_bfloat16*>(pb.out);
+    p.err = device_error_word(dev.device);
+    if (p.err == nullptr) return fail(MBS_ERR_CUDA, "device error word unavailable");
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(pl.G);
+    cfg.blockDim = dim3(NUM_THREADS);
+    cfg.dynamicSmemBytes = CF::SMEM_BYTES;
+    cfg.stream = stream;
+    cfg.attrs = nullptr;
+    cfg.numAttrs = 0;  // cluster shape comes from __cluster_dims__
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, tm_a, tm_b, tm_ia, tm_ib, p);
+    if (e != cudaSuccess) return cuda_fail(e, "gemm launch (pair)");
+    return MBS_OK;
+}
+
 template <class CF>
 int launch_cfg(const Problem& pb, const Plan& pl, const DeviceInfo& dev, void* ws, cudaStream_t stream)
 {
@@ -963,6 +1629,7 @@ int launch_cfg(const Problem& pb, const Plan& pl, const DeviceInfo& dev, void* w
 
 int dispatch(const Problem& pb, const Plan& pl, const DeviceInfo& dev, void* ws, cudaStream_t s)
 {
+    if (pl.pair) return launch_pair<CfgPair<4>>(pb, pl, dev, ws, s);
     if (pl.swap)
     {
         if (pl.bn == 32)
@@ -1188,6 +1855,9 @@ extern "C" int mbs_gemm_a4w4_launch_noalloc(const uint8_t* A, const uint8_t* B,
     {
         ws = noalloc_scratch_address(dev.device, &st);
         if (ws == nullptr) return st;
+    }
+    if (pl.sk)
+    {
         // The stream-K flags must start at zero.  A completed launch leaves
         // them zero, but one that stopped early may not have, so clear them.
         const size_t flags_off = (size_t)pl.G * BM * pl.bn * sizeof(float);

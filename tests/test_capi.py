@@ -80,9 +80,11 @@ def test_quant_and_shuffle_validation_without_device(lib):
 
 def test_workspace_size_is_host_only(lib):
     lib.mbs_gemm_a4w4_workspace_size.restype = ctypes.c_size_t
-    # decode shapes use stream-K scratch; a large prefill uses none
+    # decode shapes use stream-K partials; a large prefill runs on CTA pairs
+    # whose workspace holds the scale images (4 KB per 128 rows of A and 8 KB
+    # per 256 rows of B, per 256-element K stage)
     assert lib.mbs_gemm_a4w4_workspace_size(16, 57344, 8192) > 0
-    assert lib.mbs_gemm_a4w4_workspace_size(8192, 8192, 8192) == 0
+    assert lib.mbs_gemm_a4w4_workspace_size(8192, 8192, 8192) == 64 * 32 * 4096 + 32 * 32 * 8192
     assert lib.mbs_gemm_a4w4_workspace_size(0, 16, 64) == 0
 
 
