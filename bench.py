@@ -127,6 +127,18 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+def load_traffic(workload, M):
+    """DRAM bytes per launch of the main kernel from the committed ncu summary
+    (profiles/traffic.json: dram__bytes_read.sum + dram__bytes_write.sum)."""
+    try:
+        with open(os.path.join(REPO, "profiles", "traffic.json")) as f:
+            d = json.load(f)
+        key = "prefill_8192" if workload == "prefill" else f"decode_m{M}"
+        return d.get(key)
+    except (OSError, ValueError):
+        return None
+
+
 def dist_setup(args):
     import torch
     import torch.distributed as dist
@@ -192,6 +204,13 @@ def run_mbs(args):
         dist.barrier()
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    # events the library records around the main GEMM kernel of each step
+    k_starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    k_ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    for ev in k_starts + k_ends:
+        ev.record(stream)  # materialise the CUDA events
+    torch.cuda.synchronize()
+    L = _lib.lib()
     with ClockSampler(local) as clk:
         # untimed soak: keeps the GPU under this load while the sampler starts
         t_soak = time.perf_counter() + (0.0 if args.skip_extras else args.soak_s)
@@ -206,9 +225,11 @@ def run_mbs(args):
         t_wall = time.perf_counter()
         for i in range(args.steps):
             flush_l2(i)  # evict the operands from L2 before every timed step
+            L.mbs_set_profile_events(k_starts[i].cuda_event, k_ends[i].cuda_event)
             starts[i].record(stream)
             step()
             ends[i].record(stream)
+        L.mbs_set_profile_events(None, None)
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
@@ -216,6 +237,7 @@ def run_mbs(args):
         if not args.skip_extras:
             time.sleep(0.25)  # let the sampler record the end of the timed region
     per_step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    kernel_ms = sum(s.elapsed_time(e) for s, e in zip(k_starts, k_ends)) / args.steps
     total_ms = sum(per_step_ms)
     if world > 1:
         t = torch.tensor([total_ms], device=dev)
@@ -224,11 +246,11 @@ def run_mbs(args):
     ms = total_ms / args.steps
     flops = 2.0 * M * N * K
     value = world * flops * args.steps / (total_ms * 1e-3) / 1e12
-    kernel_tflops = flops / (ms * 1e-3) / 1e12
+    kernel_tflops = flops / (kernel_ms * 1e-3) / 1e12  # main GEMM kernel alone
 
     if args.skip_extras:
         if rank == 0:
-            print(json.dumps({"metric": "profiling run", "ms_per_step": ms,
+            print(json.dumps({"metric": "profiling run", "ms_per_step": ms, "kernel_ms": kernel_ms,
                               "kernel_tflops": kernel_tflops}), flush=True)
         if world > 1:
             dist.destroy_process_group()
@@ -264,17 +286,19 @@ def run_mbs(args):
     d2h = hout.numel() * hout.element_size()
 
     peaks, src = load_peaks()
+    traffic = load_traffic(args.workload, M)
     if args.workload == "prefill":
         peak = FP4_PER_BF16 * float(peaks["bf16_tflops"])
         roof = {"bound": "tensor", "achieved": round(kernel_tflops, 2), "peak": round(peak, 1),
-                "unit": "TFLOP/s", "frac": round(kernel_tflops / peak, 4), "traffic": None,
-                "peak_source": f"4 x bf16_tflops of {src} (dense FP4:BF16 = 4:1)"}
+                "unit": "TFLOP/s", "frac": round(kernel_tflops / peak, 4), "traffic": traffic,
+                "peak_source": f"4 x bf16_tflops of {src} (dense FP4:BF16 = 4:1)",
+                "kernel_ms": round(kernel_ms, 5)}
     else:
         nbytes = N * K // 2 + N * K // 32 + M * K // 2 + M * K // 32 + M * N * 2
-        gbs = nbytes / (ms * 1e-3) / 1e9
+        gbs = nbytes / (kernel_ms * 1e-3) / 1e9
         roof = {"bound": "hbm", "achieved": round(gbs, 1), "peak": float(peaks["hbm_gbs"]),
-                "unit": "GB/s", "frac": round(gbs / float(peaks["hbm_gbs"]), 4), "traffic": None,
-                "peak_source": src, "algorithmic_bytes": nbytes}
+                "unit": "GB/s", "frac": round(gbs / float(peaks["hbm_gbs"]), 4), "traffic": traffic,
+                "peak_source": src, "algorithmic_bytes": nbytes, "kernel_ms": round(kernel_ms, 5)}
     line = {
         "metric": "A4W4 MXFP4 GEMM TFLOPS" if args.workload == "prefill"
                   else "A4W4 MXFP4 GEMM decode TFLOPS",
@@ -290,7 +314,7 @@ def run_mbs(args):
         "e2e": {"value": round(world * flops / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOPS",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": round(e2e_ms, 4)},
-        "gpu_launches": args.steps,
+        "gpu_launches": args.steps * launches_per_call(M, N, K),
         "wall_s": round(t_wall, 3),
     }
     if rank == 0 and world == 1:
@@ -301,6 +325,16 @@ def run_mbs(args):
         dist.barrier()
         dist.destroy_process_group()
     del _lib
+
+
+def launches_per_call(M, N, K):
+    """Kernels one gemm_a4w4 call launches: the GEMM, plus the scale-image
+    kernel on the CTA-pair (large problem) path, whose workspace is non-zero
+    and not stream-K."""
+    from mbs_b200 import _lib
+    big = M > 64 and _lib.lib().mbs_gemm_a4w4_workspace_size(M, N, K) > 0 and \
+        (M + 127) // 128 * ((N + 255) // 256) >= 296
+    return 2 if big else 1
 
 
 def _cpu_sample(M, N, K, rows, seed=0):

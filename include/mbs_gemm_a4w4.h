@@ -160,6 +160,15 @@ int mbs_shuffle_weight(const uint8_t* src, uint8_t* dst, int N, int K, void* str
 int mbs_shuffle_scales(const uint8_t* plain, uint8_t* shuffled, int rows, int K, void* stream);
 
 /*
+ * Measurement hook: on this host thread, record `before_main` / `after_main`
+ * (cudaEvent_t passed as void*, or NULL to stop) on the launch stream right
+ * before and right after the main GEMM kernel of every following GEMM call,
+ * so a benchmark can time that kernel alone with CUDA events (a call may also
+ * launch a small scale-layout kernel first).  No reference counterpart.
+ */
+int mbs_set_profile_events(void* before_main, void* after_main);
+
+/*
  * Sticky device-side error word of the current device: 0, or the code of a
  * kernel wait that ran out (MBS_ERR_DEVICE_TIMEOUT).  Synchronises the
  * device.  reset != 0 clears it.  No reference counterpart.

@@ -32,6 +32,7 @@ SIGNATURES = {
     "mbs_shuffle_weight": (_c_int, [_c_void_p, _c_void_p, _c_int, _c_int, _c_void_p]),
     "mbs_shuffle_scales": (_c_int, [_c_void_p, _c_void_p, _c_int, _c_int, _c_void_p]),
     "mbs_device_error": (_c_int, [ctypes.POINTER(_c_int), _c_int]),
+    "mbs_set_profile_events": (_c_int, [_c_void_p, _c_void_p]),
 }
 
 _lock = threading.Lock()

@@ -76,21 +76,27 @@ struct Params
 
 constexpr int align_up(int x, int a) { return (x + a - 1) / a * a; }
 
-template <int BN_, bool SWAP_, bool W_MACRO_, int STAGES_>
+// R_ROWS_: rows of the R operand (A, non-swapped) actually loaded per stage.
+// Skinny problems load only their M rows (32 or 64); the MMA still reads 128
+// rows, the rest coming from whatever follows in shared memory, which only
+// feeds accumulator rows that are never stored.
+template <int BN_, bool SWAP_, bool W_MACRO_, int STAGES_, int R_ROWS_ = 128>
 struct Cfg
 {
     static constexpr int BN = BN_;
     static constexpr bool SWAP = SWAP_;
     static constexpr int STAGES = STAGES_;
+    static constexpr int R_ROWS = R_ROWS_;
+    static_assert(R_ROWS == 128 || (!SWAP_ && (R_ROWS == 32 || R_ROWS == 64)), "R rows");
     static constexpr bool R_PRESHUF = SWAP;   // weights are the preshuffled operand
     static constexpr bool C_PRESHUF = !SWAP;
     static constexpr bool R_MACRO = SWAP && W_MACRO_;
     static constexpr bool C_MACRO = !SWAP && W_MACRO_;
     static constexpr int C_RB = BN >= 128 ? BN / 128 : 1;  // 128-row scale blocks of C
 
-    static constexpr int R_DATA = BM * BKB;
+    static constexpr int R_DATA = R_ROWS * BKB;
     static constexpr int C_DATA = BN * BKB;
-    static constexpr int R_RAW = R_MACRO ? (BM / 32) * 16 : (BM / 32) * 256;
+    static constexpr int R_RAW = R_MACRO ? (R_ROWS / 32) * 16 : (R_ROWS / 32) * 256;
     static constexpr int C_RAW = C_MACRO ? (BN / 32) * 16 : (BN / 32) * 256;
     static constexpr int R_ATOM = 2 * 512;
     static constexpr int C_ATOM = 2 * C_RB * 512;
@@ -631,7 +637,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 MBS_TSTART();
                 uint8_t* st = smem + slot * CF::STAGE_BYTES;
                 if (r_side)
-                    transpose_side<BM, CF::R_MACRO>(st + CF::R_RAW_OFF, st + CF::R_ATOM_OFF, ks, lane);
+                    transpose_side<CF::R_ROWS, CF::R_MACRO>(st + CF::R_RAW_OFF, st + CF::R_ATOM_OFF, ks, lane);
                 else
                     transpose_side<BN, CF::C_MACRO>(st + CF::C_RAW_OFF, st + CF::C_ATOM_OFF, ks, lane);
                 fence_proxy_async_smem();
@@ -662,6 +668,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         constexpr int COLS = BN / 2;
         constexpr int NCH = COLS / 16;
         constexpr int BATCH = NCH < 4 ? NCH : 4;
+        // stream-K partial slots hold only the rows that can be valid
+        constexpr int PR = CF::SWAP ? BM : CF::R_ROWS;
         const bool has_factor = (p.a_factor != nullptr) || (p.b_factor != nullptr);
         // R rows are activations (non-swap) or weights (swap); C columns the other.
         const uint8_t* r_factor = CF::SWAP ? p.b_factor : p.a_factor;
@@ -711,18 +719,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             const bool row_valid = r0 + row < r_extent;
             if (nonowner)
             {
-                float* part = p.partials + (size_t)blockIdx.x * (BM * BN);
+                float* part = p.partials + (size_t)blockIdx.x * (PR * BN);
 #pragma unroll 1
                 for (int c = 0; c < COLS; c += 16)
                 {
                     uint32_t v[16];
                     tc_ld_32x32b_x16(taddr + c, v);
                     tc_wait_ld();
-                    if (row_valid)
+                    if (row_valid && row < PR)
                     {
 #pragma unroll
                         for (int t = 0; t < 16; ++t)
-                            __stcg(part + (size_t)(half * COLS + c + t) * BM + row, __uint_as_float(v[t]));
+                            __stcg(part + (size_t)(half * COLS + c + t) * PR + row, __uint_as_float(v[t]));
                     }
                 }
                 tc_fence_before();
@@ -780,11 +788,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         float x[16];
 #pragma unroll
                         for (int t = 0; t < 16; ++t) x[t] = __uint_as_float(v[b][t]);
-                        for (int cc = c_first; cc <= c_last; ++cc)
+                        if (row < PR)
                         {
-                            const float* part = p.partials + (size_t)cc * (BM * BN);
+                            for (int cc = c_first; cc <= c_last; ++cc)
+                            {
+                                const float* part = p.partials + (size_t)cc * (PR * BN);
 #pragma unroll
-                            for (int t = 0; t < 16; ++t) x[t] += __ldcg(part + (size_t)(cb + t) * BM + row);
+                                for (int t = 0; t < 16; ++t) x[t] += __ldcg(part + (size_t)(cb + t) * PR + row);
+                            }
                         }
                         if (has_factor)
                         {
@@ -1059,6 +1070,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) __cluster_dims__(2, 1, 1)
             const uint32_t full0 = mapa_shared(smem_u32(full), 0);  // leader's full[0]
             int slot = 0;
             uint32_t phase = 0;
+#if MBS_TIMING
+            tacc[12] += (unsigned long long)(clock64() - t_kernel0);  // prologue
+#endif
             for (int t = cluster; t < ntiles; t += nclusters)
             {
                 const int tr = t % tiles_r2, tc = t / tiles_r2;
@@ -1104,6 +1118,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) __cluster_dims__(2, 1, 1)
             int slot = 0;
             uint32_t phase = 0;
             uint32_t acc_phase = 0;
+#if MBS_TIMING
+            const long long t_loop0 = clock64();
+#endif
             for (int t = cluster; t < ntiles; t += nclusters)
             {
                 bool ok_acc;
@@ -1168,9 +1185,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) __cluster_dims__(2, 1, 1)
                     }
                 }
                 if (!ok) break;
-                tc_commit_pair_mc(acc_full, 0x3);
+                {
+                    MBS_TSTART();
+                    tc_commit_pair_mc(acc_full, 0x3);
+                    MBS_TADD(tacc, 14);
+                }
                 acc_phase ^= 1;
             }
+#if MBS_TIMING
+            tacc[13] = (unsigned long long)clock64();  // last issue time, turned into a tail below
+            tacc[15] = tacc[13] - (unsigned long long)t_loop0;
+#endif
         }
     }
     else if (warp >= EPI_WARP0)
@@ -1291,6 +1316,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) __cluster_dims__(2, 1, 1)
     if (warp == 1) tmem_dealloc_pair(tmem_base, CF::TMEM_COLS);
 #if MBS_TIMING
     if (threadIdx.x == 0) tacc[9] = (unsigned long long)(clock64() - t_kernel0);
+    if (tacc[13]) tacc[13] = (unsigned long long)clock64() - tacc[13];  // last issue -> exit
     if (lane == 0 && (warp <= 1 || warp == EPI_WARP0)) MBS_TFLUSH(tacc);
 #else
     (void)tacc;
@@ -1316,10 +1342,29 @@ struct Problem
 struct Plan
 {
     int bn;
+    int r_rows;  // rows of A loaded per stage (non-swapped single-CTA path)
     bool swap, sk, pair;
     int G, tiles_r, tiles_c, k_stages;
     size_t ws_bytes;
 };
+
+// Measurement hook (mbs_set_profile_events): events recorded on the launch
+// stream immediately before and after the main GEMM kernel of the next calls.
+thread_local cudaEvent_t g_ev_before = nullptr, g_ev_after = nullptr;
+
+int record_before(cudaStream_t s)
+{
+    if (g_ev_before == nullptr) return MBS_OK;
+    cudaError_t e = cudaEventRecord(g_ev_before, s);
+    return e == cudaSuccess ? MBS_OK : cuda_fail(e, "cudaEventRecord (profile)");
+}
+
+int record_after(cudaStream_t s)
+{
+    if (g_ev_after == nullptr) return MBS_OK;
+    cudaError_t e = cudaEventRecord(g_ev_after, s);
+    return e == cudaSuccess ? MBS_OK : cuda_fail(e, "cudaEventRecord (profile)");
+}
 
 int env_int(const char* name, int dflt)
 {
@@ -1339,6 +1384,9 @@ size_t pair_image_b_bytes(int N, int K)
     return (size_t)((N + 255) / 256) * ((K + BK - 1) / BK) * IMG_B_BYTES;
 }
 
+struct Plan;
+size_t sk_partial_bytes(const Plan& pl);
+
 // Path and schedule choice.  Skinny M (decode) swaps the operands so the
 // weights fill the 128-row MMA dimension; small tile counts use stream-K so
 // every SM streams an equal share of the K work.
@@ -1347,10 +1395,14 @@ size_t pair_image_b_bytes(int N, int K)
 Plan make_plan(int M, int N, int K, int num_sms)
 {
     Plan pl{};
-    pl.swap = M <= 64;
+    // Skinny M keeps the weights in the N = 256 operand (one 128x256x64 MMA
+    // per 8 KB of weights) and loads only the activation rows that exist;
+    // MBS_FORCE_SWAP=1 selects the swapped form (weights as the 128-row operand).
+    pl.swap = false;
     const int force_swap = env_int("MBS_FORCE_SWAP", -1);
-    if (force_swap == 0 || force_swap == 1) pl.swap = force_swap == 1;
+    if (force_swap == 1 && M <= 64) pl.swap = true;
     pl.bn = pl.swap ? (M <= 32 ? 32 : 64) : 256;
+    pl.r_rows = pl.swap ? 128 : (M <= 32 ? 32 : (M <= 64 ? 64 : 128));
     pl.k_stages = (K + BK - 1) / BK;
     if (pl.swap)
     {
@@ -1363,7 +1415,7 @@ Plan make_plan(int M, int N, int K, int num_sms)
         pl.tiles_c = (N + pl.bn - 1) / pl.bn;
     }
     const long long tiles = (long long)pl.tiles_r * pl.tiles_c;
-    pl.sk = pl.swap || tiles < 2LL * num_sms;
+    pl.sk = pl.swap || pl.r_rows < 128 || tiles < 2LL * num_sms;
     const int force = env_int("MBS_FORCE_SCHEDULE", 0);
     if (force == 1) pl.sk = true;
     if (force == 2) pl.sk = false;
@@ -1372,8 +1424,7 @@ Plan make_plan(int M, int N, int K, int num_sms)
     if (fg > 0 && fg < G) G = fg;
     const long long units = pl.sk ? tiles * pl.k_stages : tiles;
     pl.G = (int)(units < G ? units : G);
-    pl.ws_bytes = pl.sk ? (size_t)pl.G * BM * pl.bn * sizeof(float) + (size_t)align_up(pl.G * 4, 256)
-                        : 0;
+    pl.ws_bytes = pl.sk ? sk_partial_bytes(pl) + (size_t)align_up(pl.G * 4, 256) : 0;
     // Large data-parallel problems run on CTA pairs (256 x 256 tiles); their
     // workspace holds the scale images.
     pl.pair = !pl.swap && !pl.sk && env_int("MBS_FORCE_PAIR", 1) != 0;
@@ -1385,6 +1436,14 @@ Plan make_plan(int M, int N, int K, int num_sms)
         pl.ws_bytes = pair_image_a_bytes(M, K) + pair_image_b_bytes(N, K);
     }
     return pl;
+}
+
+// Stream-K partials: one [BN][rows] fp32 slot per CTA, rows = the rows of
+// the R operand that can hold valid outputs.
+size_t sk_partial_bytes(const Plan& pl)
+{
+    const int rows = pl.swap ? BM : pl.r_rows;
+    return (size_t)pl.G * rows * pl.bn * sizeof(float);
 }
 
 int validate(const Problem& pb)
@@ -1420,7 +1479,7 @@ int validate(const Problem& pb)
 int make_maps(const Problem& pb, const Plan& pl, CUtensorMap* tm_r, CUtensorMap* tm_c,
               CUtensorMap* tm_rsf, CUtensorMap* tm_csf)
 {
-    const int r_rows = BM, c_rows = pl.bn;
+    const int r_rows = pl.swap ? BM : pl.r_rows, c_rows = pl.bn;
     const int act_rows = pl.swap ? c_rows : r_rows;
     const int w_rows = pl.swap ? r_rows : c_rows;
     CUtensorMap* act_map = pl.swap ? tm_c : tm_r;
@@ -1567,9 +1626,11 @@ int launch_pair(const Problem& pb, const Plan& pl, const DeviceInfo& dev, void* 
     cfg.stream = stream;
     cfg.attrs = nullptr;
     cfg.numAttrs = 0;  // cluster shape comes from __cluster_dims__
+    st = record_before(stream);
+    if (st) return st;
     cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, tm_a, tm_b, tm_ia, tm_ib, p);
     if (e != cudaSuccess) return cuda_fail(e, "gemm launch (pair)");
-    return MBS_OK;
+    return record_after(stream);
 }
 
 template <class CF>
@@ -1607,7 +1668,7 @@ int launch_cfg(const Problem& pb, const Plan& pl, const DeviceInfo& dev, void* w
     if (pl.sk)
     {
         p.partials = static_cast<float*>(ws);
-        p.flags = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(ws) + (size_t)pl.G * BM * pl.bn * 4);
+        p.flags = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(ws) + sk_partial_bytes(pl));
     }
     p.err = device_error_word(dev.device);
     if (p.err == nullptr) return fail(MBS_ERR_CUDA, "device error word unavailable");
@@ -1622,9 +1683,11 @@ int launch_cfg(const Problem& pb, const Plan& pl, const DeviceInfo& dev, void* w
     attr[0].val.cooperative = pl.sk ? 1 : 0;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+    st = record_before(stream);
+    if (st) return st;
     cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, tm_r, tm_c, tm_rsf, tm_csf, p);
     if (e != cudaSuccess) return cuda_fail(e, "gemm launch");
-    return MBS_OK;
+    return record_after(stream);
 }
 
 int dispatch(const Problem& pb, const Plan& pl, const DeviceInfo& dev, void* ws, cudaStream_t s)
@@ -1638,6 +1701,12 @@ int dispatch(const Problem& pb, const Plan& pl, const DeviceInfo& dev, void* ws,
         return pb.macro ? launch_cfg<Cfg<64, true, true, 8>>(pb, pl, dev, ws, s)
                         : launch_cfg<Cfg<64, true, false, 8>>(pb, pl, dev, ws, s);
     }
+    if (pl.r_rows == 32)
+        return pb.macro ? launch_cfg<Cfg<256, false, true, 5, 32>>(pb, pl, dev, ws, s)
+                        : launch_cfg<Cfg<256, false, false, 5, 32>>(pb, pl, dev, ws, s);
+    if (pl.r_rows == 64)
+        return pb.macro ? launch_cfg<Cfg<256, false, true, 4, 64>>(pb, pl, dev, ws, s)
+                        : launch_cfg<Cfg<256, false, false, 4, 64>>(pb, pl, dev, ws, s);
     return pb.macro ? launch_cfg<Cfg<256, false, true, 4>>(pb, pl, dev, ws, s)
                     : launch_cfg<Cfg<256, false, false, 4>>(pb, pl, dev, ws, s);
 }
@@ -1733,6 +1802,14 @@ extern "C" int mbs_timing_read(unsigned long long* host, int reset)
     return e == cudaSuccess ? MBS_OK : MBS_ERR_CUDA;
 }
 #endif
+
+extern "C" int mbs_set_profile_events(void* before_main, void* after_main)
+{
+    mbs::clear_error();
+    mbs::gemm::g_ev_before = static_cast<cudaEvent_t>(before_main);
+    mbs::gemm::g_ev_after = static_cast<cudaEvent_t>(after_main);
+    return MBS_OK;
+}
 
 extern "C" int gemm_a4w4_mxfp4_launch(const uint8_t* A, const uint8_t* B, const uint8_t* AScale,
                                       const uint8_t* BScale, const uint8_t* AFactor,
@@ -1860,7 +1937,7 @@ extern "C" int mbs_gemm_a4w4_launch_noalloc(const uint8_t* A, const uint8_t* B,
     {
         // The stream-K flags must start at zero.  A completed launch leaves
         // them zero, but one that stopped early may not have, so clear them.
-        const size_t flags_off = (size_t)pl.G * BM * pl.bn * sizeof(float);
+        const size_t flags_off = sk_partial_bytes(pl);
         cudaError_t e = cudaMemsetAsync(static_cast<uint8_t*>(ws) + flags_off, 0,
                                         (size_t)pl.G * sizeof(unsigned), s);
         if (e != cudaSuccess) return mbs::cuda_fail(e, "cudaMemsetAsync (no-alloc flags)");
