@@ -48,7 +48,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["mbs", "reference"], default="mbs")
-    ap.add_argument("--workload", choices=["prefill", "decode"], default="prefill")
+    ap.add_argument("--workload", choices=["prefill", "decode", "sharded"], default="prefill")
     ap.add_argument("--m", type=int, default=None, help="M for --workload decode (default 16)")
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--skip-extras", action="store_true",
@@ -399,10 +399,80 @@ def run_reference(args):
     }), flush=True)
 
 
+def run_sharded(args):
+    """A bf16 [16384, 8192] quantised on every rank, the
+    MXFP4 weight [57344, 8192] N-sharded across the ranks, local GEMM, then an
+    NCCL all-gather of the bf16 C shards.  Timed per step with CUDA events on
+    the current stream; max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    import mbs_b200
+    from mbs_b200.sharded import ShardedA4W4
+
+    world, rank, local = dist_setup(args)
+    dev = torch.device("cuda", local)
+    M, N, K = 16384, 57344, 8192
+    nl = N // world
+    g = torch.Generator(device=dev).manual_seed(77 + rank)
+    x = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
+    w = (torch.randn(nl, K, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    qw, sw = mbs_b200.quantize_mxfp4(w, shuffle=False)
+    B = mbs_b200.shuffle_weight(qw)
+    Bs = mbs_b200.shuffle_scales(sw, K)
+    del w, qw, sw
+    if world == 1:
+        import torch.distributed as _d  # single-rank group so the same code path runs
+        if not _d.is_initialized():
+            os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+            os.environ.setdefault("MASTER_PORT", "29533")
+            _d.init_process_group("nccl", rank=0, world_size=1, device_id=dev)
+    layer = ShardedA4W4(B, Bs, N, K)
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(max(args.warmup, 3)):
+        layer(x)
+    torch.cuda.synchronize()
+    dist.barrier()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
+           torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    for i in range(args.steps):
+        e0, e1, e2 = ev[i]
+        e0.record(stream)
+        c = layer.local(x)
+        e1.record(stream)
+        flat = torch.empty((world * M, nl), dtype=c.dtype, device=dev)
+        dist.all_gather_into_tensor(flat, c)
+        e2.record(stream)
+    torch.cuda.synchronize()
+    dist.barrier()
+    t = torch.tensor([sum(a.elapsed_time(b) for a, b, _ in ev) / args.steps,
+                      sum(a.elapsed_time(c) for a, _, c in ev) / args.steps], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    local_ms, total_ms = float(t[0]), float(t[1])
+    flops = 2.0 * M * N * K
+    if rank == 0:
+        print(json.dumps({
+            "metric": "A4W4 MXFP4 fused quant + N-sharded GEMM + all-gather TFLOPS (config[4])",
+            "value": round(flops / (total_ms * 1e-3) / 1e12, 2), "unit": "TFLOPS", "n_gpus": world,
+            "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": round(total_ms, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "e2m1 (fp32 accumulate, bf16 out)", "data": "synthetic",
+            "config": {"workload": "cfg4 M=16384 N=57344 K=8192 N-sharded", "parallelism": f"N-shards x{world}"},
+            "quant_gemm_ms": round(local_ms, 4),
+            "quant_gemm_tflops": round(flops / world / (local_ms * 1e-3) / 1e12 * world, 2),
+            "allgather_ms": round(total_ms - local_ms, 4),
+            "allgather_bytes_received_per_rank": (world - 1) * M * nl * 2,
+        }), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "sharded":
+        run_sharded(args)
     else:
         run_mbs(args)
 
