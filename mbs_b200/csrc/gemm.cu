@@ -918,64 +918,91 @@ constexpr int IMG_B_BYTES = 2 * 2 * 2048;  // per 256 B rows per K stage
 //   A image [rb128][ks][q][s][l][16 B]: word w = SF(128rb + 32w + l, 8ks+4q+k)
 //   B image [tb256][ks][q][b][s][l][16 B]: word w = SF(256tb + 128b + 32w + l, ...)
 // for replicas s = 0..3 (identical).  Rows outside the scale buffer give 0.
+// One thread per (128-row block, K stage, row-in-16 rho): it loads the 16
+// flatS words of the block's four 32-row groups at that rho (word k*16 + rho
+// of each group's 256-byte chunk holds the scales of rows rho and rho + 16
+// for the K-group k of both sets of 4), transposes them as transpose_rep does
+// and writes four 16-byte rows to each replica.  Macro-block B scales are
+// shared by all rows of a 32-row group, so their image rows are copies.
 __global__ void __launch_bounds__(256) scale_image_kernel(const uint8_t* __restrict__ sa, int a_rows_buf,
                                                           int a_blocks, const uint8_t* __restrict__ sb,
                                                           int b_rows_buf, int b_tiles, int snp, int ks_count,
                                                           int b_macro, int mb_ld, uint8_t* __restrict__ img_a,
                                                           uint8_t* __restrict__ img_b)
 {
-    // one thread per (image block, K stage, q, [b], l): 4 words -> 4 replicas
-    const long long na = (long long)a_blocks * ks_count * 2 * 32;
-    const long long nb = (long long)b_tiles * ks_count * 2 * 2 * 32;
+    const long long na = (long long)a_blocks * ks_count * 16;
+    const long long nb = (long long)b_tiles * ks_count * 2 * 16;
     for (long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x; t < na + nb;
          t += (long long)gridDim.x * blockDim.x)
     {
         const bool is_a = t < na;
         long long u = is_a ? t : t - na;
-        const int l = (int)(u & 31);
-        u >>= 5;
+        const int rho = (int)(u & 15);
+        u >>= 4;
         int b = 0;
         if (!is_a)
         {
             b = (int)(u & 1);
             u >>= 1;
         }
-        const int q = (int)(u & 1);
-        u >>= 1;
         const int ks = (int)(u % ks_count);
         const long long blk = u / ks_count;
-        uint32_t w[4];
-#pragma unroll
-        for (int g = 0; g < 4; ++g)
+        const long long row0 = is_a ? blk * 128 : blk * 256 + 128 * b;  // first row of the 128-row block
+        const int rows_buf = is_a ? a_rows_buf : b_rows_buf;
+        const uint8_t* src = is_a ? sa : sb;
+        uint32_t o[4][4];  // [group][p], p = 2q + h
+        if (!is_a && b_macro)
         {
-            const long long r = is_a ? blk * 128 + 32 * g + l : blk * 256 + 128 * b + 32 * g + l;
-            uint32_t word = 0;
 #pragma unroll
-            for (int k = 0; k < 4; ++k)
+            for (int g = 0; g < 4; ++g)
             {
-                const int kb = 8 * ks + 4 * q + k;
-                uint32_t v = 0;
-                if (is_a)
+                const long long r = row0 + 32 * g;
+                uint32_t w0 = 0, w1 = 0;
+                if (r < rows_buf)
                 {
-                    if (r < a_rows_buf) v = sa[flat_s_offset((int)r, kb, snp)];
+                    const uint8_t* m = src + (r >> 5) * mb_ld + 8 * ks;
+                    w0 = (uint32_t)m[0] | ((uint32_t)m[1] << 8) | ((uint32_t)m[2] << 16) | ((uint32_t)m[3] << 24);
+                    w1 = (uint32_t)m[4] | ((uint32_t)m[5] << 8) | ((uint32_t)m[6] << 16) | ((uint32_t)m[7] << 24);
                 }
-                else if (b_macro)
-                {
-                    if (r < b_rows_buf) v = sb[(r >> 5) * mb_ld + kb];
-                }
-                else
-                {
-                    if (r < b_rows_buf) v = sb[flat_s_offset((int)r, kb, snp)];
-                }
-                word |= v << (8 * k);
+                o[g][0] = o[g][1] = w0;  // q = 0, both h
+                o[g][2] = o[g][3] = w1;  // q = 1
             }
-            w[g] = word;
         }
-        const uint4 v4 = make_uint4(w[0], w[1], w[2], w[3]);
-        uint8_t* dst = is_a ? img_a + (blk * ks_count + ks) * IMG_A_BYTES + q * 2048 + l * 16
-                            : img_b + (blk * ks_count + ks) * IMG_B_BYTES + q * 4096 + b * 2048 + l * 16;
+        else
+        {
 #pragma unroll
-        for (int s = 0; s < 4; ++s) *reinterpret_cast<uint4*>(dst + s * 512) = v4;
+            for (int g = 0; g < 4; ++g)
+            {
+                const long long r = row0 + 32 * g;  // 32-row group start
+                uint32_t w[4] = {0, 0, 0, 0};
+                if (r < rows_buf)
+                {
+                    const uint32_t* chunk =
+                        reinterpret_cast<const uint32_t*>(src + (r >> 5) * 32 * (long long)snp + (long long)ks * 256);
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) w[k] = __ldg(chunk + k * 16 + rho);
+                }
+                const uint32_t t0 = __byte_perm(w[0], w[1], 0x5140);
+                const uint32_t t1 = __byte_perm(w[2], w[3], 0x5140);
+                const uint32_t t2 = __byte_perm(w[0], w[1], 0x7362);
+                const uint32_t t3 = __byte_perm(w[2], w[3], 0x7362);
+                o[g][0] = __byte_perm(t0, t1, 0x5410);
+                o[g][1] = __byte_perm(t0, t1, 0x7632);
+                o[g][2] = __byte_perm(t2, t3, 0x5410);
+                o[g][3] = __byte_perm(t2, t3, 0x7632);
+            }
+        }
+#pragma unroll
+        for (int pp = 0; pp < 4; ++pp)
+        {
+            const int h = pp & 1, q = pp >> 1;
+            const uint4 v4 = make_uint4(o[0][pp], o[1][pp], o[2][pp], o[3][pp]);
+            uint8_t* dst = is_a ? img_a + (blk * ks_count + ks) * IMG_A_BYTES + q * 2048
+                                : img_b + (blk * ks_count + ks) * IMG_B_BYTES + q * 4096 + b * 2048;
+            dst += (16 * h + rho) * 16;
+#pragma unroll
+            for (int s = 0; s < 4; ++s) *reinterpret_cast<uint4*>(dst + s * 512) = v4;
+        }
     }
 }
 
@@ -1599,7 +1626,7 @@ int launch_pair(const Problem& pb, const Plan& pl, const DeviceInfo& dev, void* 
     {
         const int a_blocks = (int)(ia / ((size_t)pl.k_stages * IMG_A_BYTES));
         const int b_tiles = (int)(ib / ((size_t)pl.k_stages * IMG_B_BYTES));
-        const long long threads = (long long)a_blocks * pl.k_stages * 64 + (long long)b_tiles * pl.k_stages * 128;
+        const long long threads = (long long)a_blocks * pl.k_stages * 16 + (long long)b_tiles * pl.k_stages * 32;
         long long blocks = (threads + 255) / 256;
         if (blocks > (long long)dev.num_sms * 8) blocks = (long long)dev.num_sms * 8;
         scale_image_kernel<<<(int)blocks, 256, 0, stream>>>(pb.AS, pb.Mpad, a_blocks, pb.BS,

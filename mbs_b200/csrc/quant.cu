@@ -17,13 +17,21 @@
 namespace mbs {
 namespace {
 
-// e2m1 magnitude code of q >= 0 (RNE; ties at 0.25/1.25/2.5/5 go down, at
-// 0.75/1.75/3.5 up -- the neighbour with an even mantissa bit; > 5 -> 6).
+// e2m1 magnitude code of q in [0, 8) with round-to-nearest-even, saturating
+// at 6 (code 7).  The grid {0, .5, 1, 1.5, 2, 3, 4, 6} is one mantissa bit
+// above 1 and a fixed 0.5 step below it:
+//   q <  1: code = rint(2q)  (ties 0.25 -> 0 and 0.75 -> 2 go to even)
+//   q >= 1: round the fp32 significand to 1 bit, RNE (add 2^21 - 1 plus the
+//           kept bit, so a carry happens above half and at half only when
+//           the kept bit is 1); bits [30:22] are then 2*E + m with E the
+//           biased exponent, and the code is 2*(E-126) + m = (bits>>22) - 252.
+//           Rounding 7.x up gives 8 (code 8), clamped to 6 (code 7).
 __device__ __forceinline__ uint32_t e2m1_code(float q)
 {
-    return (uint32_t)(q > 0.25f) + (uint32_t)(q >= 0.75f) + (uint32_t)(q > 1.25f) +
-           (uint32_t)(q >= 1.75f) + (uint32_t)(q > 2.5f) + (uint32_t)(q >= 3.5f) +
-           (uint32_t)(q > 5.0f);
+    if (q < 1.0f) return (uint32_t)__float2int_rn(q * 2.0f);
+    const uint32_t b = __float_as_uint(q);
+    const uint32_t c = ((b + 0x1FFFFFu + ((b >> 22) & 1u)) >> 22) - 252u;
+    return c < 7u ? c : 7u;
 }
 
 __device__ __forceinline__ uint32_t scale_from_amax_bits(uint32_t amax_bits)
@@ -50,52 +58,65 @@ __device__ __forceinline__ int64_t flat_s(int r, int b, int snp)
            (int64_t)(b8 & 3) * 64 + (int64_t)(b >> 3) * 256 + (int64_t)(r >> 5) * 32 * snp;
 }
 
-// One thread per 8 consecutive elements (16 bytes of bf16); the 4 threads of
-// a 32-element block are 4 consecutive lanes and combine their amax with two
-// xor-shuffles.  Out-of-range lanes run the shuffles with an empty block.
-__global__ void __launch_bounds__(256) quantize_1x32_kernel(const uint16_t* __restrict__ x,
-                                                            int rows, int K, int ld_x,
-                                                            uint8_t* __restrict__ q,
-                                                            uint8_t* __restrict__ sc, int shuffled,
-                                                            int snp)
+// One CTA per row, one thread per 8 consecutive elements (16 bytes of bf16)
+// of that row; the 4 threads of a 32-element block are 4 consecutive lanes
+// and combine their amax with two xor-shuffles.  Each thread keeps
+// QUANT_UNROLL independent 16-byte loads in flight before using them, and no
+// index needs a division.  Lanes past the row end run the shuffles with an
+// empty block.
+constexpr int QUANT_UNROLL = 4;
+constexpr int QUANT_THREADS = 256;
+
+__global__ void __launch_bounds__(QUANT_THREADS) quantize_1x32_kernel(const uint16_t* __restrict__ x,
+                                                                      int rows, int K, int ld_x,
+                                                                      uint8_t* __restrict__ q,
+                                                                      uint8_t* __restrict__ sc, int shuffled,
+                                                                      int snp)
 {
-    const int oct_per_row = K >> 3;
-    const int64_t total = (int64_t)rows * oct_per_row;
-    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-    const int64_t limit = (total + 31) / 32 * 32;
-    for (int64_t o = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; o < limit; o += stride)
+    const int oct = K >> 3;                 // octets in a row (multiple of 4)
+    const int limit = (oct + 31) & ~31;     // whole warps
+    for (int r = blockIdx.x; r < rows; r += gridDim.x)
     {
-        const bool valid = o < total;
-        int r = 0, j = 0;
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (valid)
+        const uint4* xr = reinterpret_cast<const uint4*>(x + (int64_t)r * ld_x);
+        uint32_t* qr = reinterpret_cast<uint32_t*>(q + (int64_t)r * (K >> 1));
+        for (int j0 = threadIdx.x; j0 < limit; j0 += QUANT_THREADS * QUANT_UNROLL)
         {
-            r = (int)(o / oct_per_row);
-            j = (int)(o - (int64_t)r * oct_per_row);
-            v = __ldcs(reinterpret_cast<const uint4*>(x + (int64_t)r * ld_x) + j);
-        }
-        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-        uint32_t am = 0;
+            uint4 v[QUANT_UNROLL];
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-            am = max(am, max(w[i] & 0x7FFFu, (w[i] >> 16) & 0x7FFFu));
-        am = max(am, __shfl_xor_sync(0xffffffffu, am, 1));
-        am = max(am, __shfl_xor_sync(0xffffffffu, am, 2));
-        if (!valid) continue;
-        const uint32_t s = scale_from_amax_bits(am);
-        const bool nan_block = s == 0xFFu;
-        const float inv = __uint_as_float((254u - (nan_block ? 254u : s)) << 23);
-        uint32_t packed = 0;
+            for (int u = 0; u < QUANT_UNROLL; ++u)
+            {
+                const int j = j0 + u * QUANT_THREADS;
+                v[u] = j < oct ? __ldcs(xr + j) : make_uint4(0, 0, 0, 0);
+            }
 #pragma unroll
-        for (int i = 0; i < 4; ++i) packed |= encode_pair(w[i], inv, nan_block) << (8 * i);
-        reinterpret_cast<uint32_t*>(q + (int64_t)r * (K >> 1))[j] = packed;
-        if ((j & 3) == 0)
-        {
-            const int b = j >> 2;
-            if (shuffled)
-                sc[flat_s(r, b, snp)] = (uint8_t)s;
-            else
-                sc[(int64_t)r * (K >> 5) + b] = (uint8_t)s;
+            for (int u = 0; u < QUANT_UNROLL; ++u)
+            {
+                const int j = j0 + u * QUANT_THREADS;
+                if (j - (int)(threadIdx.x & 31) >= limit) break;  // whole warp past the row end
+                const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+                uint32_t am = 0;
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+                    am = max(am, max(w[i] & 0x7FFFu, (w[i] >> 16) & 0x7FFFu));
+                am = max(am, __shfl_xor_sync(0xffffffffu, am, 1));
+                am = max(am, __shfl_xor_sync(0xffffffffu, am, 2));
+                if (j >= oct) continue;
+                const uint32_t s = scale_from_amax_bits(am);
+                const bool nan_block = s == 0xFFu;
+                const float inv = __uint_as_float((254u - (nan_block ? 254u : s)) << 23);
+                uint32_t packed = 0;
+#pragma unroll
+                for (int i = 0; i < 4; ++i) packed |= encode_pair(w[i], inv, nan_block) << (8 * i);
+                qr[j] = packed;
+                if ((j & 3) == 0)
+                {
+                    const int b = j >> 2;
+                    if (shuffled)
+                        sc[flat_s(r, b, snp)] = (uint8_t)s;
+                    else
+                        sc[(int64_t)r * (K >> 5) + b] = (uint8_t)s;
+                }
+            }
         }
     }
 }
@@ -248,8 +269,9 @@ extern "C" int mbs_quantize_mxfp4(const void* x_bf16, int rows, int K, int ld_x,
     if (st != MBS_OK) return st;
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     const int snp = scale_n_pad(K);
-    const int64_t octs = (int64_t)rows * (K / 8);
-    quantize_1x32_kernel<<<grid_for(octs, 256, dev.num_sms), 256, 0, s>>>(
+    // one CTA per row (grid-stride over rows beyond the cap)
+    const int qgrid = rows < dev.num_sms * 64 ? rows : dev.num_sms * 64;
+    quantize_1x32_kernel<<<qgrid, QUANT_THREADS, 0, s>>>(
         static_cast<const uint16_t*>(x_bf16), rows, K, ld_x, fp4_out, scale_out, shuffled ? 1 : 0,
         snp);
     if (shuffled && ((rows % 32) != 0 || (K / 32) != snp))
