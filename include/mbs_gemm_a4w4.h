@@ -79,11 +79,23 @@ int gemm_a4w4_mxfp4_launch(const uint8_t* A, const uint8_t* B, const uint8_t* AS
 size_t mbs_gemm_a4w4_workspace_size(int M, int N, int K);
 
 /*
+ * Workspace layout shared by every schedule: the first
+ * MBS_GEMM_WS_FLAG_BYTES bytes hold the stream-K completion flags (one word
+ * per CTA), which must be zero when a launch starts; the rest is per-launch
+ * scratch (stream-K partial tiles or the CTA-pair path's scale images) that
+ * needs no initialisation.  Any workspace size returned by this library is
+ * either 0 or at least MBS_GEMM_WS_FLAG_BYTES.
+ */
+#define MBS_GEMM_WS_FLAG_BYTES 4096
+
+/*
  * As gemm_a4w4_mxfp4_launch, with caller-provided scratch memory.  The
  * workspace must be zero-filled before its first use; every launch that
- * completes leaves it zero-filled again, so it can be reused on the same
- * stream without clearing.  Launches that overlap on the GPU must not share
- * a workspace.
+ * completes leaves its flag words zero again, so the workspace can be reused
+ * on the same stream, by any shape, without clearing.  A launch that stopped
+ * with a device error (mbs_device_error) may leave flags set: zero the first
+ * MBS_GEMM_WS_FLAG_BYTES bytes before reusing the workspace.  Launches that
+ * overlap on the GPU must not share a workspace.
  */
 int mbs_gemm_a4w4_launch_ws(const uint8_t* A, const uint8_t* B, const uint8_t* AScale,
                             const uint8_t* BScale, const uint8_t* AFactor, const uint8_t* BFactor,
@@ -122,6 +134,31 @@ int mbs_gemm_a4w4_launch_noalloc(const uint8_t* A, const uint8_t* B, const uint8
                                  const uint8_t* BScale, const uint8_t* AFactor,
                                  const uint8_t* BFactor, void* out, int M, int N, int K, int Mpad,
                                  int scaleN_pad, void* stream);
+
+/*
+ * Packed weights (optional, offline): the preshuffled weight and its shuffled
+ * scales rearranged so that every (256-row tile, 256-element K stage) is one
+ * contiguous 34 KB block -- the 32 KB tile in the exact shared-memory order
+ * the tensor-core instruction reads, then its 2 KB of TMEM-ready scale
+ * blocks.  The GEMM then streams each stage with a single bulk copy, which is
+ * what skinny (decode) shapes need to approach HBM bandwidth.  Like the
+ * reference's weight preshuffle this is a one-time step for static weights.
+ * No reference counterpart.
+ *
+ * mbs_packed_weight_bytes: size of the packed buffer for an N x K weight.
+ * mbs_pack_weight: B (flatB [N, K/2]) + BScale (flatS) -> packed.
+ * mbs_gemm_a4w4_packed_launch_ws: as mbs_gemm_a4w4_launch_ws with the packed
+ *   weight in place of B/BScale; workspace size from
+ *   mbs_gemm_a4w4_packed_workspace_size.
+ */
+size_t mbs_packed_weight_bytes(int N, int K);
+int mbs_pack_weight(const uint8_t* B, const uint8_t* BScale, int N, int K, int scaleN_pad,
+                    uint8_t* packed, void* stream);
+size_t mbs_gemm_a4w4_packed_workspace_size(int M, int N, int K);
+int mbs_gemm_a4w4_packed_launch_ws(const uint8_t* A, const uint8_t* packedB, const uint8_t* AScale,
+                                   const uint8_t* AFactor, const uint8_t* BFactor, void* out, int M,
+                                   int N, int K, int Mpad, int scaleN_pad, void* workspace,
+                                   size_t workspace_bytes, void* stream);
 
 /* ---- quantiser and layout kernels ------------------------------------ */
 

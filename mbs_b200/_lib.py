@@ -33,6 +33,11 @@ SIGNATURES = {
     "mbs_shuffle_scales": (_c_int, [_c_void_p, _c_void_p, _c_int, _c_int, _c_void_p]),
     "mbs_device_error": (_c_int, [ctypes.POINTER(_c_int), _c_int]),
     "mbs_set_profile_events": (_c_int, [_c_void_p, _c_void_p]),
+    "mbs_packed_weight_bytes": (_c_size_t, [_c_int, _c_int]),
+    "mbs_pack_weight": (_c_int, [_c_void_p, _c_void_p, _c_int, _c_int, _c_int, _c_void_p, _c_void_p]),
+    "mbs_gemm_a4w4_packed_workspace_size": (_c_size_t, [_c_int] * 3),
+    "mbs_gemm_a4w4_packed_launch_ws": (_c_int, [_c_void_p] * 6 + [_c_int] * 5 + [_c_void_p, _c_size_t,
+                                                                                _c_void_p]),
 }
 
 _lock = threading.Lock()

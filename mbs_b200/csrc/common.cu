@@ -4,6 +4,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 
 namespace mbs {
@@ -80,6 +81,15 @@ int current_device(DeviceInfo* info)
     return MBS_OK;
 }
 
+namespace {
+std::atomic<unsigned long long> g_error_epoch{0};
+}  // namespace
+
+unsigned long long device_error_epoch()
+{
+    return g_error_epoch.load(std::memory_order_acquire);
+}
+
 unsigned* device_error_word(int device)
 {
     static std::mutex mu;
@@ -154,8 +164,9 @@ extern "C" int mbs_device_error(int* code_out, int reset)
     e = cudaMemcpyFromSymbol(&v, mbs::g_device_error, sizeof(v));
     if (e != cudaSuccess) return mbs::cuda_fail(e, "cudaMemcpyFromSymbol");
     *code_out = static_cast<int>(v);
-    if (reset)
+    if (reset && v != 0)
     {
+        mbs::g_error_epoch.fetch_add(1, std::memory_order_acq_rel);
         unsigned z = 0;
         e = cudaMemcpyToSymbol(mbs::g_device_error, &z, sizeof(z));
         if (e != cudaSuccess) return mbs::cuda_fail(e, "cudaMemcpyToSymbol");

@@ -34,6 +34,11 @@ int current_device(DeviceInfo* info);
 // Device-global sticky error word (MBS_ERR_DEVICE_TIMEOUT when a wait ran out).
 unsigned* device_error_word(int device);
 
+// Count of device errors cleared through mbs_device_error(..., reset=1).  A
+// launch that stopped on a device error may leave stream-K flags set, so
+// library-owned workspaces clear their flags when this has moved on.
+unsigned long long device_error_epoch();
+
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
 int encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, void* base,
                 const uint64_t* dims, const uint64_t* strides_bytes /* rank-1 entries */,

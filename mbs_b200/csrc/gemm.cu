@@ -42,6 +42,7 @@
 // ranges start inside the tile) left in the workspace, flagged per CTA.
 #include <cuda_bf16.h>
 
+#include <cstring>
 #include <mutex>
 #include <unordered_map>
 
@@ -72,6 +73,7 @@ struct Params
     float* partials;       // [G][BN][BM] fp32, stream-K only
     unsigned* flags;       // [G], stream-K only; zero between launches
     unsigned* err;         // sticky device error word
+    const uint8_t* packed_b;  // packed weights (C_PACKED configurations)
 };
 
 constexpr int align_up(int x, int a) { return (x + a - 1) / a * a; }
@@ -80,14 +82,22 @@ constexpr int align_up(int x, int a) { return (x + a - 1) / a * a; }
 // Skinny problems load only their M rows (32 or 64); the MMA still reads 128
 // rows, the rest coming from whatever follows in shared memory, which only
 // feeds accumulator rows that are never stored.
-template <int BN_, bool SWAP_, bool W_MACRO_, int STAGES_, int R_ROWS_ = 128>
+// C_PACKED_: the C operand (weights, non-swapped) comes from the packed
+// weight format (pack_weight_kernel): per 256-row tile and K stage one
+// contiguous block = the 32 KB tile in shared-memory order followed by its
+// 2 KB of tcgen05.cp-ready scale blocks, loaded with one bulk copy.
+constexpr int PACK_STAGE_BYTES = 256 * BKB + 4 * 512;
+
+template <int BN_, bool SWAP_, bool W_MACRO_, int STAGES_, int R_ROWS_ = 128, bool C_PACKED_ = false>
 struct Cfg
 {
     static constexpr int BN = BN_;
     static constexpr bool SWAP = SWAP_;
     static constexpr int STAGES = STAGES_;
     static constexpr int R_ROWS = R_ROWS_;
+    static constexpr bool C_PACKED = C_PACKED_;
     static_assert(R_ROWS == 128 || (!SWAP_ && (R_ROWS == 32 || R_ROWS == 64)), "R rows");
+    static_assert(!C_PACKED || (!SWAP_ && !W_MACRO_ && BN_ == 256), "packed weights: non-swapped, BN 256");
     static constexpr bool R_PRESHUF = SWAP;   // weights are the preshuffled operand
     static constexpr bool C_PRESHUF = !SWAP;
     static constexpr bool R_MACRO = SWAP && W_MACRO_;
@@ -97,18 +107,22 @@ struct Cfg
     static constexpr int R_DATA = R_ROWS * BKB;
     static constexpr int C_DATA = BN * BKB;
     static constexpr int R_RAW = R_MACRO ? (R_ROWS / 32) * 16 : (R_ROWS / 32) * 256;
-    static constexpr int C_RAW = C_MACRO ? (BN / 32) * 16 : (BN / 32) * 256;
+    static constexpr int C_RAW = C_PACKED ? 0 : (C_MACRO ? (BN / 32) * 16 : (BN / 32) * 256);
     static constexpr int R_ATOM = 2 * 512;
     static constexpr int C_ATOM = 2 * C_RB * 512;
 
+    // packed: [R data][C data][C atoms][R raw][R atoms] (C data + atoms contiguous)
+    // else:   [R data][C data][R raw][C raw][R atoms][C atoms]
     static constexpr int R_DATA_OFF = 0;
     static constexpr int C_DATA_OFF = R_DATA_OFF + R_DATA;
-    static constexpr int R_RAW_OFF = C_DATA_OFF + C_DATA;
+    static constexpr int R_RAW_OFF = C_PACKED ? C_DATA_OFF + C_DATA + C_ATOM : C_DATA_OFF + C_DATA;
     static constexpr int C_RAW_OFF = R_RAW_OFF + align_up(R_RAW, 128);
     static constexpr int R_ATOM_OFF = C_RAW_OFF + align_up(C_RAW, 128);
-    static constexpr int C_ATOM_OFF = R_ATOM_OFF + R_ATOM;
-    static constexpr int STAGE_BYTES = align_up(C_ATOM_OFF + C_ATOM, 1024);
-    static constexpr uint32_t TX_BYTES = R_DATA + C_DATA + R_RAW + C_RAW;
+    static constexpr int C_ATOM_OFF = C_PACKED ? C_DATA_OFF + C_DATA : R_ATOM_OFF + R_ATOM;
+    static constexpr int STAGE_END = C_PACKED ? R_ATOM_OFF + R_ATOM : C_ATOM_OFF + C_ATOM;
+    static constexpr int STAGE_BYTES = align_up(STAGE_END, 1024);
+    static constexpr uint32_t TX_BYTES = R_DATA + C_DATA + R_RAW + C_RAW + (C_PACKED ? C_ATOM : 0);
+    static_assert(!C_PACKED || C_DATA + C_ATOM == PACK_STAGE_BYTES, "packed stage");
 
     static constexpr int SF_STAGE_COLS = 8 + 8 * C_RB;
     static constexpr int ACC_BUFS = (2 * BN + STAGES * SF_STAGE_COLS <= 512) ? 2 : 1;
@@ -439,9 +453,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         *abort_flag = 0;
         fence_mbar_init();
         prefetch_tmap(&tm_r);
-        prefetch_tmap(&tm_c);
         prefetch_tmap(&tm_rsf);
-        prefetch_tmap(&tm_csf);
+        if (!CF::C_PACKED)
+        {
+            prefetch_tmap(&tm_c);
+            prefetch_tmap(&tm_csf);
+        }
     }
     if (warp == 1)
     {
@@ -487,7 +504,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         tma_load_3d(st + CF::R_DATA_OFF, &tm_r, &full[slot], 0, r0 / 16, ks * 8);
                     else
                         tma_load_2d(st + CF::R_DATA_OFF, &tm_r, &full[slot], ks * BKB, r0);
-                    if (CF::C_PRESHUF)
+                    if (CF::C_PACKED)
+                        bulk_load(st + CF::C_DATA_OFF,
+                                  p.packed_b + ((size_t)tc * p.k_stages + ks) * PACK_STAGE_BYTES,
+                                  PACK_STAGE_BYTES, &full[slot]);
+                    else if (CF::C_PRESHUF)
                         tma_load_3d(st + CF::C_DATA_OFF, &tm_c, &full[slot], 0, c0 / 16, ks * 8);
                     else
                         tma_load_2d(st + CF::C_DATA_OFF, &tm_c, &full[slot], ks * BKB, c0);
@@ -495,7 +516,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         tma_load_2d(st + CF::R_RAW_OFF, &tm_rsf, &full[slot], 16 * (ks >> 1), r0 / 32);
                     else
                         tma_load_3d(st + CF::R_RAW_OFF, &tm_rsf, &full[slot], 0, ks, r0 / 32);
-                    if (CF::C_MACRO)
+                    if (CF::C_PACKED)
+                        ;  // scale blocks arrived with the packed tile
+                    else if (CF::C_MACRO)
                         tma_load_2d(st + CF::C_RAW_OFF, &tm_csf, &full[slot], 16 * (ks >> 1), c0 / 32);
                     else
                         tma_load_3d(st + CF::C_RAW_OFF, &tm_csf, &full[slot], 0, ks, c0 / 32);
@@ -638,7 +661,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 uint8_t* st = smem + slot * CF::STAGE_BYTES;
                 if (r_side)
                     transpose_side<CF::R_ROWS, CF::R_MACRO>(st + CF::R_RAW_OFF, st + CF::R_ATOM_OFF, ks, lane);
-                else
+                else if (!CF::C_PACKED)
                     transpose_side<BN, CF::C_MACRO>(st + CF::C_RAW_OFF, st + CF::C_ATOM_OFF, ks, lane);
                 fence_proxy_async_smem();
                 __syncwarp();
@@ -670,6 +693,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         constexpr int BATCH = NCH < 4 ? NCH : 4;
         // stream-K partial slots hold only the rows that can be valid
         constexpr int PR = CF::SWAP ? BM : CF::R_ROWS;
+        // an owner sums its contributors' partials in the idle pipeline stages when they fit
+        constexpr bool STAGE_PARTIALS = PR * BN * 4 <= STAGES * CF::STAGE_BYTES;
         const bool has_factor = (p.a_factor != nullptr) || (p.b_factor != nullptr);
         // R rows are activations (non-swap) or weights (swap); C columns the other.
         const uint8_t* r_factor = CF::SWAP ? p.b_factor : p.a_factor;
@@ -708,6 +733,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 ok_acc = mbar_wait(&acc_full[acc], acc_phase, abort_flag);
                 MBS_TADD(tacc, 6);
             }
+            // all epilogue warps take the same branch, so none is left behind in a named barrier
+            ok_acc = named_bar_and(1, NUM_EPI_THREADS, ok_acc);
             if (!ok_acc)
             {
                 if (lane == 0) raise_error(p, abort_flag);
@@ -743,6 +770,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             else
             {
                 int c_first = 0, c_last = -1;  // contributing CTAs [c_first, c_last]
+                const float* psum = nullptr;   // their partials summed, [BN][PR] in shared memory
                 if (owner)
                 {
                     const long long tile_end = (long long)(w.tile + 1) * p.k_stages;
@@ -771,6 +799,52 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #endif
                     }
                     named_bar_sync(1, NUM_EPI_THREADS);
+                    // An owner item ends this CTA's range, so it is the CTA's last item: with its
+                    // accumulator full, no load or MMA touches the pipeline stages any more.  The
+                    // contributors' partials are summed there first, every thread keeping eight
+                    // independent 16-byte loads in flight, so the tile costs about one DRAM round
+                    // trip; the drain loop then adds them from shared memory.  (Per-thread loads
+                    // inside the drain loop would pay a round trip per column chunk.)
+                    if constexpr (STAGE_PARTIALS)
+                    {
+                        constexpr int N4 = PR * BN / 4;
+                        constexpr int U = 8;
+                        float4* sum4 = reinterpret_cast<float4*>(smem);
+                        const float4* part4 = reinterpret_cast<const float4*>(p.partials);
+                        for (int base = et; base < N4; base += NUM_EPI_THREADS * U)
+                        {
+                            float4 a[U];
+#pragma unroll
+                            for (int u = 0; u < U; ++u) a[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+                            for (int cc = c_first; cc <= c_last; ++cc)
+                            {
+                                const float4* src = part4 + (size_t)cc * N4;
+                                float4 b[U];
+#pragma unroll
+                                for (int u = 0; u < U; ++u)
+                                {
+                                    const int e4 = base + u * NUM_EPI_THREADS;
+                                    b[u] = e4 < N4 ? __ldcg(src + e4) : make_float4(0.f, 0.f, 0.f, 0.f);
+                                }
+#pragma unroll
+                                for (int u = 0; u < U; ++u)
+                                {
+                                    a[u].x += b[u].x;
+                                    a[u].y += b[u].y;
+                                    a[u].z += b[u].z;
+                                    a[u].w += b[u].w;
+                                }
+                            }
+#pragma unroll
+                            for (int u = 0; u < U; ++u)
+                            {
+                                const int e4 = base + u * NUM_EPI_THREADS;
+                                if (e4 < N4) sum4[e4] = a[u];
+                            }
+                        }
+                        named_bar_sync(1, NUM_EPI_THREADS);
+                        psum = reinterpret_cast<const float*>(smem);
+                    }
                 }
                 uint32_t packed[COLS / 2];
                 const float fr = has_factor ? fr_s[row] : 1.0f;
@@ -788,7 +862,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         float x[16];
 #pragma unroll
                         for (int t = 0; t < 16; ++t) x[t] = __uint_as_float(v[b][t]);
-                        if (row < PR)
+                        if constexpr (STAGE_PARTIALS)
+                        {
+                            if (psum != nullptr && row < PR)
+                            {
+#pragma unroll
+                                for (int t = 0; t < 16; ++t) x[t] += psum[(cb + t) * PR + row];
+                            }
+                        }
+                        else if (row < PR)
                         {
                             for (int cc = c_first; cc <= c_last; ++cc)
                             {
@@ -885,6 +967,61 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #endif
 }
 
+
+// ====================================================================== packing
+// Reference weight layout (flatB + flatS) -> packed format.  Packed block
+// (tile t of 256 rows, K stage ks), PACK_STAGE_BYTES long:
+//   [0, 32 KB)  tile bytes in the shared-memory order the MMA reads:
+//               16-byte row slice (row tile nt, K chunk c) at (c*16 + nt)*256,
+//               i.e. flatB offset (t*16 + nt)*8K + (8ks + c)*256
+//   [32, 34 KB) scale blocks (q, rb) at 32 KB + (2q + rb)*512, row r of the
+//               tile at (r%32)*16 + ((r%128)/32)*4, byte k = scale
+//               (256t + r, 8ks + 4q + k)  (the transpose_side<256> output)
+// Rows past N and K chunks past K/32 are zero.
+__global__ void __launch_bounds__(256) pack_weight_kernel(const uint8_t* __restrict__ B,
+                                                          const uint8_t* __restrict__ BS, int N, int K, int snp,
+                                                          int ks_count, long long nblocks,
+                                                          uint8_t* __restrict__ packed)
+{
+    constexpr int V_PER_BLOCK = (256 * BKB) / 16 + 512;  // 16-byte tile pieces + scale words
+    const long long total = nblocks * V_PER_BLOCK;
+    const int chunks = K / 32;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x)
+    {
+        const long long blk = i / V_PER_BLOCK;
+        const int v = (int)(i - blk * V_PER_BLOCK);
+        const int t = (int)(blk / ks_count), ks = (int)(blk - (long long)t * ks_count);
+        uint8_t* dst = packed + blk * PACK_STAGE_BYTES;
+        if (v < (256 * BKB) / 16)
+        {
+            const int piece = v >> 4, sub = v & 15;  // 256-byte slice, 16-byte part
+            const int c = piece >> 4, nt = piece & 15;
+            const int ntile = t * 16 + nt, chunk = ks * 8 + c;
+            uint4 val = make_uint4(0, 0, 0, 0);
+            if (ntile * 16 < N && chunk < chunks)
+                val = __ldg(reinterpret_cast<const uint4*>(B + (long long)ntile * ((long long)K * 8) +
+                                                           (long long)chunk * 256) + sub);
+            reinterpret_cast<uint4*>(dst)[v] = val;
+        }
+        else
+        {
+            const int wi = v - (256 * BKB) / 16;  // scale word 0..511
+            const int a = wi >> 7, rr = (wi & 127) >> 2, g4 = wi & 3;  // atom, row-in-32, group
+            const int q = a >> 1, rb = a & 1;
+            const int r = 128 * rb + 32 * g4 + rr;
+            const int row = 256 * t + r;
+            uint32_t word = 0;
+            if (row < N)
+            {
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                    word |= (uint32_t)BS[flat_s_offset(row, 8 * ks + 4 * q + k, snp)] << (8 * k);
+            }
+            *reinterpret_cast<uint32_t*>(dst + 256 * BKB + a * 512 + rr * 16 + g4 * 4) = word;
+        }
+    }
+}
 
 // ====================================================================== CTA pair
 // Prefill kernel on CTA pairs (cluster of 2): one tcgen05.mma.cta_group::2
@@ -1364,6 +1501,7 @@ struct Problem
     void* out;
     int M, N, K, Mpad, snp, mb_ld;
     bool macro;
+    bool packed = false;  // B is in the packed format (BS unused)
 };
 
 struct Plan
@@ -1414,12 +1552,18 @@ size_t pair_image_b_bytes(int N, int K)
 struct Plan;
 size_t sk_partial_bytes(const Plan& pl);
 
+// Every workspace starts with the stream-K flag words at a fixed place, so
+// that no schedule's scratch (partials, scale images) ever lands on another
+// schedule's flags when one workspace serves several shapes.
+constexpr size_t kFlagBytes = MBS_GEMM_WS_FLAG_BYTES;
+constexpr int kMaxGrid = (int)(kFlagBytes / sizeof(unsigned));
+
 // Path and schedule choice.  Skinny M (decode) swaps the operands so the
 // weights fill the 128-row MMA dimension; small tile counts use stream-K so
 // every SM streams an equal share of the K work.
 //   MBS_FORCE_SCHEDULE=1 (stream-K) / 2 (data-parallel), MBS_FORCE_GRID=<G>:
 //   debug overrides used by the tests to reach every schedule on small shapes.
-Plan make_plan(int M, int N, int K, int num_sms)
+Plan make_plan(int M, int N, int K, int num_sms, bool packed = false)
 {
     Plan pl{};
     // Skinny M keeps the weights in the N = 256 operand (one 128x256x64 MMA
@@ -1427,7 +1571,7 @@ Plan make_plan(int M, int N, int K, int num_sms)
     // MBS_FORCE_SWAP=1 selects the swapped form (weights as the 128-row operand).
     pl.swap = false;
     const int force_swap = env_int("MBS_FORCE_SWAP", -1);
-    if (force_swap == 1 && M <= 64) pl.swap = true;
+    if (force_swap == 1 && M <= 64 && !packed) pl.swap = true;
     pl.bn = pl.swap ? (M <= 32 ? 32 : 64) : 256;
     pl.r_rows = pl.swap ? 128 : (M <= 32 ? 32 : (M <= 64 ? 64 : 128));
     pl.k_stages = (K + BK - 1) / BK;
@@ -1446,21 +1590,21 @@ Plan make_plan(int M, int N, int K, int num_sms)
     const int force = env_int("MBS_FORCE_SCHEDULE", 0);
     if (force == 1) pl.sk = true;
     if (force == 2) pl.sk = false;
-    int G = num_sms;
+    int G = num_sms < kMaxGrid ? num_sms : kMaxGrid;
     const int fg = env_int("MBS_FORCE_GRID", 0);
     if (fg > 0 && fg < G) G = fg;
     const long long units = pl.sk ? tiles * pl.k_stages : tiles;
     pl.G = (int)(units < G ? units : G);
-    pl.ws_bytes = pl.sk ? sk_partial_bytes(pl) + (size_t)align_up(pl.G * 4, 256) : 0;
+    pl.ws_bytes = pl.sk ? kFlagBytes + sk_partial_bytes(pl) : 0;
     // Large data-parallel problems run on CTA pairs (256 x 256 tiles); their
     // workspace holds the scale images.
-    pl.pair = !pl.swap && !pl.sk && env_int("MBS_FORCE_PAIR", 1) != 0;
+    pl.pair = !packed && !pl.swap && !pl.sk && env_int("MBS_FORCE_PAIR", 1) != 0;
     if (pl.pair)
     {
         const long long t2 = (long long)((M + 2 * BM - 1) / (2 * BM)) * ((N + 255) / 256);
         const int c = G / 2;
         pl.G = 2 * (int)(t2 < c ? t2 : c);
-        pl.ws_bytes = pair_image_a_bytes(M, K) + pair_image_b_bytes(N, K);
+        pl.ws_bytes = kFlagBytes + pair_image_a_bytes(M, K) + pair_image_b_bytes(N, K);
     }
     return pl;
 }
@@ -1475,7 +1619,7 @@ size_t sk_partial_bytes(const Plan& pl)
 
 int validate(const Problem& pb)
 {
-    if (!pb.A || !pb.B || !pb.AS || !pb.BS || !pb.out)
+    if (!pb.A || !pb.B || !pb.AS || (!pb.BS && !pb.packed) || !pb.out)
         return fail(MBS_ERR_INVALID_ARGUMENT, "gemm_a4w4: A, B, scales and out must be non-NULL");
     if (pb.M <= 0 || pb.N <= 0 || pb.K <= 0)
         return fail(MBS_ERR_INVALID_ARGUMENT, "gemm_a4w4: M, N, K must be positive (M=%d N=%d K=%d)",
@@ -1496,7 +1640,7 @@ int validate(const Problem& pb)
     if (pb.macro && (pb.mb_ld % 16 != 0 || pb.mb_ld < pb.K / 32))
         return fail(MBS_ERR_INVALID_ARGUMENT, "gemm_a4w4: mb_ld (%d) must be a multiple of 16 >= K/32",
                     pb.mb_ld);
-    if (!aligned16(pb.A) || !aligned16(pb.B) || !aligned16(pb.AS) || !aligned16(pb.BS) ||
+    if (!aligned16(pb.A) || !aligned16(pb.B) || !aligned16(pb.AS) || (!pb.packed && !aligned16(pb.BS)) ||
         !aligned16(pb.out))
         return fail(MBS_ERR_MISALIGNED, "gemm_a4w4: A, B, scales and out must be 16-byte aligned");
     return MBS_OK;
@@ -1523,6 +1667,12 @@ int make_maps(const Problem& pb, const Plan& pl, CUtensorMap* tm_r, CUtensorMap*
                          CU_TENSOR_MAP_SWIZZLE_128B);
         if (st) return st;
     }
+    if (pb.packed)
+    {  // weights and their scales come from the packed buffer by bulk copies
+        memset(w_map, 0, sizeof(CUtensorMap));
+        memset(w_sf, 0, sizeof(CUtensorMap));
+    }
+    if (!pb.packed)
     {  // weights: flatB as {256 B block, row tile (16 rows), K chunk (16 B)}
         const uint64_t dims[3] = {256, (uint64_t)pb.N / 16, (uint64_t)pb.K / 32};
         const uint64_t strides[2] = {(uint64_t)pb.K * 8, 256};
@@ -1539,7 +1689,10 @@ int make_maps(const Problem& pb, const Plan& pl, CUtensorMap* tm_r, CUtensorMap*
                          CU_TENSOR_MAP_SWIZZLE_NONE);
         if (st) return st;
     }
-    if (!pb.macro)
+    if (pb.packed)
+    {
+    }
+    else if (!pb.macro)
     {  // weight scales: flatS, roundup(N,32) rows
         const uint64_t dims[3] = {256, (uint64_t)pb.snp / 8, (uint64_t)(pb.N + 31) / 32};
         const uint64_t strides[2] = {256, (uint64_t)pb.snp * 32};
@@ -1617,7 +1770,7 @@ int launch_pair(const Problem& pb, const Plan& pl, const DeviceInfo& dev, void* 
     }
     const size_t ia = pair_image_a_bytes(pb.M, pb.K);
     const size_t ib = pair_image_b_bytes(pb.N, pb.K);
-    uint8_t* img_a = static_cast<uint8_t*>(ws);
+    uint8_t* img_a = static_cast<uint8_t*>(ws) + kFlagBytes;
     uint8_t* img_b = img_a + ia;
     CUtensorMap tm_a, tm_b, tm_ia, tm_ib;
     int st = make_maps_pair(pb, img_a, ia, img_b, ib, &tm_a, &tm_b, &tm_ia, &tm_ib);
@@ -1694,11 +1847,12 @@ int launch_cfg(const Problem& pb, const Plan& pl, const DeviceInfo& dev, void* w
     p.out = static_cast<__nv_bfloat16*>(pb.out);
     if (pl.sk)
     {
-        p.partials = static_cast<float*>(ws);
-        p.flags = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(ws) + sk_partial_bytes(pl));
+        p.flags = static_cast<unsigned*>(ws);
+        p.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + kFlagBytes);
     }
     p.err = device_error_word(dev.device);
     if (p.err == nullptr) return fail(MBS_ERR_CUDA, "device error word unavailable");
+    p.packed_b = pb.packed ? pb.B : nullptr;
 
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(pl.G);
@@ -1719,6 +1873,12 @@ int launch_cfg(const Problem& pb, const Plan& pl, const DeviceInfo& dev, void* w
 
 int dispatch(const Problem& pb, const Plan& pl, const DeviceInfo& dev, void* ws, cudaStream_t s)
 {
+    if (pb.packed)
+    {
+        if (pl.r_rows == 32) return launch_cfg<Cfg<256, false, false, 5, 32, true>>(pb, pl, dev, ws, s);
+        if (pl.r_rows == 64) return launch_cfg<Cfg<256, false, false, 5, 64, true>>(pb, pl, dev, ws, s);
+        return launch_cfg<Cfg<256, false, false, 4, 128, true>>(pb, pl, dev, ws, s);
+    }
     if (pl.pair) return launch_pair<CfgPair<4>>(pb, pl, dev, ws, s);
     if (pl.swap)
     {
@@ -1745,14 +1905,30 @@ void* internal_workspace(int device, cudaStream_t stream, size_t bytes, int* sta
     {
         void* ptr;
         size_t bytes;
+        unsigned long long epoch;  // device_error_epoch() when the flags were last known zero
     };
     static std::mutex mu;
     static std::unordered_map<unsigned long long, Buf> bufs;
     std::lock_guard<std::mutex> lk(mu);
     const unsigned long long key = (reinterpret_cast<uintptr_t>(stream) << 8) ^ (unsigned)device;
     Buf& b = bufs[key];
-    if (b.bytes >= bytes && b.ptr != nullptr) return b.ptr;
     cudaError_t e;
+    if (b.bytes >= bytes && b.ptr != nullptr)
+    {
+        const unsigned long long ep = device_error_epoch();
+        if (b.epoch != ep)
+        {
+            // a launch may have stopped on a device error since: clear its flags
+            e = cudaMemsetAsync(b.ptr, 0, kFlagBytes, stream);
+            if (e != cudaSuccess)
+            {
+                *status = cuda_fail(e, "cudaMemsetAsync (gemm workspace flags)");
+                return nullptr;
+            }
+            b.epoch = ep;
+        }
+        return b.ptr;
+    }
     if (b.ptr != nullptr)
     {
         e = cudaStreamSynchronize(stream);
@@ -1780,6 +1956,7 @@ void* internal_workspace(int device, cudaStream_t stream, size_t bytes, int* sta
         return nullptr;
     }
     b.bytes = want;
+    b.epoch = device_error_epoch();
     return b.ptr;
 }
 
@@ -1790,7 +1967,7 @@ int run(const Problem& pb, void* ws, size_t ws_bytes, bool internal_ws, cudaStre
     DeviceInfo dev;
     st = current_device(&dev);
     if (st) return st;
-    const Plan pl = make_plan(pb.M, pb.N, pb.K, dev.num_sms);
+    const Plan pl = make_plan(pb.M, pb.N, pb.K, dev.num_sms, pb.packed);
     if (pl.ws_bytes > 0)
     {
         if (internal_ws)
@@ -1874,6 +2051,68 @@ extern "C" int mbs_gemm_a4w4_launch_ws(const uint8_t* A, const uint8_t* B, const
 {
     mbs::clear_error();
     Problem pb{A, B, AScale, BScale, AFactor, BFactor, out, M, N, K, Mpad, scaleN_pad, 0, false};
+    return mbs::gemm::run(pb, workspace, workspace_bytes, false, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" size_t mbs_packed_weight_bytes(int N, int K)
+{
+    if (N <= 0 || K <= 0) return 0;
+    return (size_t)((N + 255) / 256) * ((K + mbs::gemm::BK - 1) / mbs::gemm::BK) * mbs::gemm::PACK_STAGE_BYTES;
+}
+
+extern "C" int mbs_pack_weight(const uint8_t* B, const uint8_t* BScale, int N, int K, int scaleN_pad,
+                               uint8_t* packed, void* stream)
+{
+    using namespace mbs::gemm;
+    mbs::clear_error();
+    if (!B || !BScale || !packed) return mbs::fail(MBS_ERR_INVALID_ARGUMENT, "mbs_pack_weight: null pointer");
+    if (N <= 0 || K <= 0) return mbs::fail(MBS_ERR_INVALID_ARGUMENT, "mbs_pack_weight: N, K must be positive");
+    if (N % 16 != 0 || K % 64 != 0)
+        return mbs::fail(MBS_ERR_UNSUPPORTED_SHAPE, "mbs_pack_weight: needs N %% 16 == 0 and K %% 64 == 0");
+    if (scaleN_pad % 8 != 0 || scaleN_pad < K / 32)
+        return mbs::fail(MBS_ERR_INVALID_ARGUMENT, "mbs_pack_weight: bad scaleN_pad %d", scaleN_pad);
+    if (!mbs::aligned16(B) || !mbs::aligned16(packed))
+        return mbs::fail(MBS_ERR_MISALIGNED, "mbs_pack_weight: B and packed must be 16-byte aligned");
+    mbs::DeviceInfo dev;
+    int st = mbs::current_device(&dev);
+    if (st) return st;
+    const int ks_count = (K + BK - 1) / BK;
+    const long long nblocks = (long long)((N + 255) / 256) * ks_count;
+    const long long work = nblocks * ((256 * BKB) / 16 + 512);
+    long long blocks = (work + 255) / 256;
+    if (blocks > (long long)dev.num_sms * 16) blocks = (long long)dev.num_sms * 16;
+    pack_weight_kernel<<<(int)blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        B, BScale, N, K, scaleN_pad, ks_count, nblocks, packed);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? MBS_OK : mbs::cuda_fail(e, "pack_weight launch");
+}
+
+extern "C" size_t mbs_gemm_a4w4_packed_workspace_size(int M, int N, int K)
+{
+    int num_sms = 148;
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess)
+    {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && n > 0)
+            num_sms = n;
+    }
+    else
+    {
+        cudaGetLastError();
+    }
+    if (M <= 0 || N <= 0 || K <= 0) return 0;
+    return mbs::gemm::make_plan(M, N, K, num_sms, true).ws_bytes;
+}
+
+extern "C" int mbs_gemm_a4w4_packed_launch_ws(const uint8_t* A, const uint8_t* packedB, const uint8_t* AScale,
+                                              const uint8_t* AFactor, const uint8_t* BFactor, void* out, int M,
+                                              int N, int K, int Mpad, int scaleN_pad, void* workspace,
+                                              size_t workspace_bytes, void* stream)
+{
+    mbs::clear_error();
+    Problem pb{A, packedB, AScale, nullptr, AFactor, BFactor, out, M, N, K, Mpad, scaleN_pad, 0, false};
+    pb.packed = true;
     return mbs::gemm::run(pb, workspace, workspace_bytes, false, reinterpret_cast<cudaStream_t>(stream));
 }
 
@@ -1964,9 +2203,7 @@ extern "C" int mbs_gemm_a4w4_launch_noalloc(const uint8_t* A, const uint8_t* B,
     {
         // The stream-K flags must start at zero.  A completed launch leaves
         // them zero, but one that stopped early may not have, so clear them.
-        const size_t flags_off = sk_partial_bytes(pl);
-        cudaError_t e = cudaMemsetAsync(static_cast<uint8_t*>(ws) + flags_off, 0,
-                                        (size_t)pl.G * sizeof(unsigned), s);
+        cudaError_t e = cudaMemsetAsync(ws, 0, (size_t)pl.G * sizeof(unsigned), s);
         if (e != cudaSuccess) return mbs::cuda_fail(e, "cudaMemsetAsync (no-alloc flags)");
     }
     return dispatch(pb, pl, dev, ws, s);

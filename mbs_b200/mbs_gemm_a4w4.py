@@ -16,13 +16,18 @@ Launches go to the current torch CUDA stream of A's device, asynchronously.
 
 from __future__ import annotations
 
+import ctypes
 import threading
 
 import torch
 
 from . import _lib
 
-__all__ = ["gemm_a4w4", "gemm_a4w4_macro", "workspace_for"]
+__all__ = ["gemm_a4w4", "gemm_a4w4_macro", "workspace_for", "device_error"]
+
+# Workspace layout of include/mbs_gemm_a4w4.h: the first WS_FLAG_BYTES bytes
+# are the stream-K flag words (zero between launches), the rest is scratch.
+WS_FLAG_BYTES = 4096
 
 _ws_lock = threading.Lock()
 _ws_cache: dict = {}
@@ -42,13 +47,12 @@ def _bytes(t: torch.Tensor) -> torch.Tensor:
     return t.view(torch.uint8).contiguous()
 
 
-def workspace_for(M: int, N: int, K: int, device: torch.device) -> torch.Tensor | None:
-    """Zero-initialised stream-K scratch for this shape on the current stream.
+def cached_workspace(need: int, device: torch.device) -> torch.Tensor | None:
+    """The (device, current stream) workspace, grown to at least `need` bytes.
 
-    One buffer per (device, stream), grown on demand.  The kernels leave it
-    zeroed after every launch, so it is reused without clearing.
+    Zero-filled when allocated; every completed launch leaves its flag words
+    zero again, so one buffer serves every shape and schedule on that stream.
     """
-    need = int(_lib.lib().mbs_gemm_a4w4_workspace_size(M, N, K))
     if need == 0:
         return None
     stream = torch.cuda.current_stream(device)
@@ -59,6 +63,28 @@ def workspace_for(M: int, N: int, K: int, device: torch.device) -> torch.Tensor 
             buf = torch.zeros(max(need, 1 << 22), dtype=torch.uint8, device=device)
             _ws_cache[key] = buf
     return buf
+
+
+def workspace_for(M: int, N: int, K: int, device: torch.device) -> torch.Tensor | None:
+    """Workspace for a drop-in launch of this shape on the current stream."""
+    return cached_workspace(int(_lib.lib().mbs_gemm_a4w4_workspace_size(M, N, K)), device)
+
+
+def device_error(reset: bool = False) -> int:
+    """Sticky device error code of the current device (0 = none; synchronises).
+
+    With reset=True the code is cleared, and so are the flag words of this
+    module's cached workspaces: a launch that stopped on a device error may
+    have left some set.
+    """
+    code = ctypes.c_int(0)
+    _lib.call("mbs_device_error", ctypes.byref(code), 1 if reset else 0)
+    if reset and code.value != 0:
+        with _ws_lock:
+            for buf in _ws_cache.values():
+                buf[:WS_FLAG_BYTES].zero_()
+        torch.cuda.synchronize()  # cleared before any stream's next launch
+    return code.value
 
 
 def _check_inputs(A, B, A_scale, B_scale, A_factor, B_factor):

@@ -84,8 +84,21 @@ def test_workspace_size_is_host_only(lib):
     # whose workspace holds the scale images (4 KB per 128 rows of A and 8 KB
     # per 256 rows of B, per 256-element K stage)
     assert lib.mbs_gemm_a4w4_workspace_size(16, 57344, 8192) > 0
-    assert lib.mbs_gemm_a4w4_workspace_size(8192, 8192, 8192) == 64 * 32 * 4096 + 32 * 32 * 8192
+    # flag words first, then the pair path's A and B scale images
+    assert lib.mbs_gemm_a4w4_workspace_size(8192, 8192, 8192) == 4096 + 64 * 32 * 4096 + 32 * 32 * 8192
+    # stream-K: flag words, then one [BN=256][32 rows] fp32 partial slot per CTA (G = 148 SMs
+    # is not known without a device, so only the layout's lower bound is checked)
+    for shape in [(16, 57344, 8192), (1, 16, 64), (300, 272, 1088)]:
+        ws = lib.mbs_gemm_a4w4_workspace_size(*shape)
+        assert ws == 0 or ws >= 4096
     assert lib.mbs_gemm_a4w4_workspace_size(0, 16, 64) == 0
+
+
+def test_workspace_flag_region_matches_header():
+    from mbs_b200 import mbs_gemm_a4w4
+    hdr = open(os.path.join(REPO, "include", "mbs_gemm_a4w4.h")).read()
+    m = re.search(r"#define MBS_GEMM_WS_FLAG_BYTES (\d+)", hdr)
+    assert m and int(m.group(1)) == mbs_gemm_a4w4.WS_FLAG_BYTES
 
 
 def test_python_layer_fails_loudly_without_library(monkeypatch, tmp_path):

@@ -77,6 +77,28 @@ def test_stream_k_splits(force_env, M, N, K, grid):
     assert torch.equal(out, out2)
 
 
+def test_one_workspace_serves_every_schedule(force_env):
+    """Shapes and schedules in sequence on one stream share the cached
+    workspace: scale images and wide stream-K partial slots written by one
+    launch must never read as another schedule's completion flags."""
+    seq = [
+        (dict(), (512, 512, 1024)),                                         # CTA pairs: scale images
+        (dict(MBS_FORCE_SCHEDULE=1), (300, 1024, 2048)),                    # stream-K, 128-row slots
+        (dict(MBS_FORCE_SCHEDULE=1, MBS_FORCE_GRID=17), (2, 2048, 4096)),   # 3 CTAs per tile
+        (dict(MBS_FORCE_SCHEDULE=1, MBS_FORCE_GRID=29), (48, 1024, 4096)),  # 64-row slots
+        (dict(MBS_FORCE_SCHEDULE=1, MBS_FORCE_GRID=17), (2, 2048, 4096)),
+    ]
+    for i, (env, (M, N, K)) in enumerate(seq):
+        os.environ.pop("MBS_FORCE_SCHEDULE", None)
+        os.environ.pop("MBS_FORCE_GRID", None)
+        force_env(**env)
+        c = Case(M, N, K, seed=100 + i, factors=True)
+        out = _gemm(c)
+        torch.cuda.synchronize()
+        ref, bound = c.reference()
+        assert_gemm_close(out, ref, bound, f"step {i} {M}x{N}x{K} {env}")
+
+
 @pytest.mark.parametrize("M,N,K", [(384, 1024, 512), (1000, 2048, 256)])
 def test_data_parallel_schedule(force_env, M, N, K):
     force_env(MBS_FORCE_SCHEDULE=2, MBS_FORCE_GRID=7)
