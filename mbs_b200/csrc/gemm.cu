@@ -74,6 +74,7 @@ struct Params
     unsigned* flags;       // [G], stream-K only; zero between launches
     unsigned* err;         // sticky device error word
     const uint8_t* packed_b;  // packed weights (C_PACKED configurations)
+    int act_rows;          // rows per activation TMA box (the activation operand's tile rows, or M)
 };
 
 constexpr int align_up(int x, int a) { return (x + a - 1) / a * a; }
@@ -477,6 +478,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         {
             int slot = 0;
             uint32_t phase = 0;
+            // The weights (C, or R when swapped) are read exactly once when the
+            // other operand is a single tile: stream them evict-first.
+            const bool w_once = CF::SWAP ? p.tiles_c == 1 : p.tiles_r == 1;
+            const uint64_t pol_w = w_once ? l2_policy_evict_first() : l2_policy_evict_normal();
+            const uint64_t pol_r = CF::SWAP ? pol_w : l2_policy_evict_normal();
+            const uint64_t pol_c = CF::SWAP ? l2_policy_evict_normal() : pol_w;
+            // A box of activation rows stops at M when one tile covers them all, so no
+            // stage pays for out-of-bounds fill; expect only the bytes it brings.
+            const uint32_t tx_bytes = CF::TX_BYTES - (uint32_t)((CF::SWAP ? BN : CF::R_ROWS) - p.act_rows) * BKB;
             Work w;
             for (int i = 0; get_work(p, i, w); ++i)
             {
@@ -499,29 +509,29 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     tacc[10] += 1;
 #endif
                     uint8_t* st = smem + slot * CF::STAGE_BYTES;
-                    mbar_arrive_expect_tx(&full[slot], CF::TX_BYTES);
+                    mbar_arrive_expect_tx(&full[slot], tx_bytes);
                     if (CF::R_PRESHUF)
-                        tma_load_3d(st + CF::R_DATA_OFF, &tm_r, &full[slot], 0, r0 / 16, ks * 8);
+                        tma_load_3d_hint(st + CF::R_DATA_OFF, &tm_r, &full[slot], 0, r0 / 16, ks * 8, pol_r);
                     else
-                        tma_load_2d(st + CF::R_DATA_OFF, &tm_r, &full[slot], ks * BKB, r0);
+                        tma_load_2d_hint(st + CF::R_DATA_OFF, &tm_r, &full[slot], ks * BKB, r0, pol_r);
                     if (CF::C_PACKED)
-                        bulk_load(st + CF::C_DATA_OFF,
-                                  p.packed_b + ((size_t)tc * p.k_stages + ks) * PACK_STAGE_BYTES,
-                                  PACK_STAGE_BYTES, &full[slot]);
+                        bulk_load_hint(st + CF::C_DATA_OFF,
+                                       p.packed_b + ((size_t)tc * p.k_stages + ks) * PACK_STAGE_BYTES,
+                                       PACK_STAGE_BYTES, &full[slot], pol_c);
                     else if (CF::C_PRESHUF)
-                        tma_load_3d(st + CF::C_DATA_OFF, &tm_c, &full[slot], 0, c0 / 16, ks * 8);
+                        tma_load_3d_hint(st + CF::C_DATA_OFF, &tm_c, &full[slot], 0, c0 / 16, ks * 8, pol_c);
                     else
-                        tma_load_2d(st + CF::C_DATA_OFF, &tm_c, &full[slot], ks * BKB, c0);
+                        tma_load_2d_hint(st + CF::C_DATA_OFF, &tm_c, &full[slot], ks * BKB, c0, pol_c);
                     if (CF::R_MACRO)
-                        tma_load_2d(st + CF::R_RAW_OFF, &tm_rsf, &full[slot], 16 * (ks >> 1), r0 / 32);
+                        tma_load_2d_hint(st + CF::R_RAW_OFF, &tm_rsf, &full[slot], 16 * (ks >> 1), r0 / 32, pol_r);
                     else
-                        tma_load_3d(st + CF::R_RAW_OFF, &tm_rsf, &full[slot], 0, ks, r0 / 32);
+                        tma_load_3d_hint(st + CF::R_RAW_OFF, &tm_rsf, &full[slot], 0, ks, r0 / 32, pol_r);
                     if (CF::C_PACKED)
                         ;  // scale blocks arrived with the packed tile
                     else if (CF::C_MACRO)
-                        tma_load_2d(st + CF::C_RAW_OFF, &tm_csf, &full[slot], 16 * (ks >> 1), c0 / 32);
+                        tma_load_2d_hint(st + CF::C_RAW_OFF, &tm_csf, &full[slot], 16 * (ks >> 1), c0 / 32, pol_c);
                     else
-                        tma_load_3d(st + CF::C_RAW_OFF, &tm_csf, &full[slot], 0, ks, c0 / 32);
+                        tma_load_3d_hint(st + CF::C_RAW_OFF, &tm_csf, &full[slot], 0, ks, c0 / 32, pol_c);
                     if (++slot == STAGES)
                     {
                         slot = 0;
@@ -1647,6 +1657,16 @@ int validate(const Problem& pb)
 }
 
 // TMA descriptors for the four operands of one launch.
+// Rows per activation TMA box: the activation operand's rows per tile, cut to
+// M when a single tile holds them all (TMA zero-fill of the rows past M costs
+// stream time; those shared-memory rows only feed accumulator rows that are
+// never stored).
+int act_box_rows(const Problem& pb, const Plan& pl)
+{
+    const int tile_rows = pl.swap ? pl.bn : pl.r_rows;
+    return pb.M < tile_rows ? pb.M : tile_rows;
+}
+
 int make_maps(const Problem& pb, const Plan& pl, CUtensorMap* tm_r, CUtensorMap* tm_c,
               CUtensorMap* tm_rsf, CUtensorMap* tm_csf)
 {
@@ -1662,7 +1682,7 @@ int make_maps(const Problem& pb, const Plan& pl, CUtensorMap* tm_r, CUtensorMap*
     {  // activations: plain [M, K/2], 128-byte swizzled boxes of {128 B, rows}
         const uint64_t dims[2] = {Kp, (uint64_t)pb.M};
         const uint64_t strides[1] = {Kp};
-        const uint32_t box[2] = {BKB, (uint32_t)act_rows};
+        const uint32_t box[2] = {BKB, (uint32_t)act_box_rows(pb, pl)};
         st = encode_tmap(act_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, (void*)pb.A, dims, strides, box,
                          CU_TENSOR_MAP_SWIZZLE_128B);
         if (st) return st;
@@ -1853,6 +1873,7 @@ int launch_cfg(const Problem& pb, const Plan& pl, const DeviceInfo& dev, void* w
     p.err = device_error_word(dev.device);
     if (p.err == nullptr) return fail(MBS_ERR_CUDA, "device error word unavailable");
     p.packed_b = pb.packed ? pb.B : nullptr;
+    p.act_rows = act_box_rows(pb, pl);
 
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(pl.G);
