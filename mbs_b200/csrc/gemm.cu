@@ -147,9 +147,27 @@ struct Work
     int tile, k0, k1;
 };
 
+// floor(a * b / c) for non-negative operands; 32-bit division when the
+// product fits (the common case), which costs far less than the 64-bit one.
+__device__ __forceinline__ long long muldiv(long long a, long long b, long long c)
+{
+    const unsigned long long prod = (unsigned long long)a * (unsigned long long)b;
+    if (prod <= 0xFFFFFFFFull && (unsigned long long)c <= 0xFFFFFFFFull)
+        return (long long)((unsigned)prod / (unsigned)c);
+    return (long long)(prod / (unsigned long long)c);
+}
+
 __device__ __forceinline__ long long sk_start(const Params& p, int c)
 {
-    return (long long)c * p.sk_units / gridDim.x;
+    return muldiv(c, p.sk_units, gridDim.x);
+}
+
+// Last CTA whose stream-K range starts before unit `tile_end`: sk_start(c) <
+// tile_end  <=>  c * units < tile_end * G.
+__device__ __forceinline__ int sk_last_starting_before(const Params& p, long long tile_end)
+{
+    const long long last = muldiv(tile_end * gridDim.x - 1, 1, p.sk_units);
+    return last < (long long)gridDim.x - 1 ? (int)last : (int)gridDim.x - 1;
 }
 
 // idx-th work item of this CTA; false when exhausted.
@@ -167,7 +185,7 @@ __device__ __forceinline__ bool get_work(const Params& p, int idx, Work& w)
     const long long s = sk_start(p, blockIdx.x);
     const long long e = sk_start(p, blockIdx.x + 1);
     const int ks = p.k_stages;
-    const long long t0 = s / ks;
+    const long long t0 = muldiv(s, 1, ks);
     if (idx == 0)
     {
         if (s >= e) return false;
@@ -785,8 +803,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 {
                     const long long tile_end = (long long)(w.tile + 1) * p.k_stages;
                     c_first = blockIdx.x + 1;
-                    c_last = blockIdx.x;
-                    while (c_last + 1 < (int)gridDim.x && sk_start(p, c_last + 1) < tile_end) ++c_last;
+                    c_last = sk_last_starting_before(p, tile_end);
                     if (et == 0)
                     {
 #if MBS_TIMING
