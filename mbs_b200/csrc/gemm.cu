@@ -1069,9 +1069,14 @@ __global__ void __launch_bounds__(256) pack_weight_kernel(const uint8_t* __restr
 //     multicasts to both), then TMA their A tile, B half, A-scale image and
 //     the pair's B-scale image with .cta_group::2, completing on the LEADER's
 //     `full` barrier, which the leader's producer arms with both CTAs' bytes;
-//   * the leader's MMA thread issues tcgen05.cp.cta_group::2 (each CTA's
-//     shared memory -> its own TMEM) and the pair MMAs, and multicasts its
-//     commits to both CTAs' `empty` / `acc_full`;
+//   * the leader's scale-copy thread (warp 2) waits on `full`, issues
+//     tcgen05.cp.cta_group::2 (each CTA's shared memory -> its own TMEM) into
+//     the slot's scale columns and commits to the leader's `sfready`;
+//   * the leader's MMA thread waits on `full` and `sfready`, issues the pair
+//     MMAs and multicasts its commits to both CTAs' `empty` / `acc_full`.
+//     (Keeping tcgen05.cp out of the MMA thread matters: a thread that issues
+//     copies right after an mbarrier wait stalls ~120 cycles per stage, one
+//     that issues only MMAs does not.)
 //   * each CTA's epilogue drains its own TMEM and arrives on the leader's
 //     `acc_empty` (16 warps).
 
@@ -1188,8 +1193,8 @@ struct CfgPair
     static constexpr int SF_BASE = BN;  // one accumulator buffer
     static constexpr int TMEM_COLS = 512;
     static_assert(SF_BASE + STAGES * SF_STAGE_COLS <= 512, "TMEM budget");
-    // full, empty [STAGES]; acc_full, acc_empty; tmem slot; abort
-    static constexpr int BAR_BYTES = (2 * STAGES + 2) * 8 + 16;
+    // full, sfready, empty [STAGES]; acc_full, acc_empty; tmem slot; abort
+    static constexpr int BAR_BYTES = (3 * STAGES + 2) * 8 + 16;
     static constexpr int EPI_BYTES = (BM + BN) * 4;
     static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + EPI_BYTES + 1024;
     static_assert(SMEM_BYTES <= 232448, "shared memory budget");
@@ -1207,7 +1212,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) __cluster_dims__(2, 1, 1)
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~static_cast<uintptr_t>(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * CF::STAGE_BYTES);
-    uint64_t* empty = full + STAGES;
+    uint64_t* sfready = full + STAGES;  // leader: a stage's scales are in TMEM
+    uint64_t* empty = sfready + STAGES;
     uint64_t* acc_full = empty + STAGES;
     uint64_t* acc_empty = acc_full + 1;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 1);
@@ -1230,6 +1236,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) __cluster_dims__(2, 1, 1)
         for (int s = 0; s < STAGES; ++s)
         {
             mbar_init(&full[s], 1);
+            mbar_init(&sfready[s], 1);
             mbar_init(&empty[s], 1);
         }
         mbar_init(acc_full, 1);
@@ -1335,6 +1342,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) __cluster_dims__(2, 1, 1)
                         ok_in = mbar_wait(&full[slot], phase, abort_flag);
                         MBS_TADD(tacc, 2);
                     }
+                    {
+                        MBS_TSTART();
+                        ok_in = ok_in && mbar_wait(&sfready[slot], phase, abort_flag);
+                        MBS_TADD(tacc, 3);
+                    }
                     if (!ok_in)
                     {
                         raise_error(p, abort_flag);
@@ -1346,12 +1358,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) __cluster_dims__(2, 1, 1)
                     const uint8_t* st = smem + slot * CF::STAGE_BYTES;
                     const uint32_t sf_a = tmem_base + CF::SF_BASE + slot * CF::SF_STAGE_COLS;
                     const uint32_t sf_b = sf_a + 8;
-                    // 3 copies of 128 rows x 32 B: SFA both K-group sets, SFB one set each
-                    tc_cp_128x256b_pair(sf_a, make_smem_desc(smem_u32(st + CF::A_IMG_OFF), 2048, 128, 0));
-#pragma unroll
-                    for (int q = 0; q < 2; ++q)
-                        tc_cp_128x256b_pair(sf_b + 8 * q,
-                                            make_smem_desc(smem_u32(st + CF::B_IMG_OFF + q * 4096), 2048, 128, 0));
                     const uint32_t a_base = smem_u32(st + CF::A_DATA_OFF);
                     const uint32_t b_base = smem_u32(st + CF::B_DATA_OFF);
 #pragma unroll
@@ -1387,6 +1393,49 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) __cluster_dims__(2, 1, 1)
             tacc[13] = (unsigned long long)clock64();  // last issue time, turned into a tail below
             tacc[15] = tacc[13] - (unsigned long long)t_loop0;
 #endif
+        }
+    }
+    else if (warp == 2)
+    {
+        // ------------------------------------------------ scale copies (leader)
+        // A thread that issues tcgen05.cp right after observing an mbarrier
+        // stalls far longer than one that only issues MMAs, so the scale
+        // images go to TMEM from here, one stage ahead of the MMA thread,
+        // which then waits on sfready (cheap) instead.
+        if (lane == 0 && leader)
+        {
+            int slot = 0;
+            uint32_t phase = 0;
+            for (int t = cluster; t < ntiles; t += nclusters)
+            {
+                bool ok = true;
+                for (int ks = 0; ks < p.k_stages; ++ks)
+                {
+                    if (!mbar_wait(&full[slot], phase, abort_flag))
+                    {
+                        raise_error(p, abort_flag);
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint8_t* st = smem + slot * CF::STAGE_BYTES;
+                    const uint32_t sf_a = tmem_base + CF::SF_BASE + slot * CF::SF_STAGE_COLS;
+                    const uint32_t sf_b = sf_a + 8;
+                    // 3 copies of 128 rows x 32 B: SFA both K-group sets, SFB one set each
+                    tc_cp_128x256b_pair(sf_a, make_smem_desc(smem_u32(st + CF::A_IMG_OFF), 2048, 128, 0));
+#pragma unroll
+                    for (int q = 0; q < 2; ++q)
+                        tc_cp_128x256b_pair(sf_b + 8 * q,
+                                            make_smem_desc(smem_u32(st + CF::B_IMG_OFF + q * 4096), 2048, 128, 0));
+                    tc_commit_pair_mc(&sfready[slot], 0x1);
+                    if (++slot == STAGES)
+                    {
+                        slot = 0;
+                        phase ^= 1;
+                    }
+                }
+                if (!ok) break;
+            }
         }
     }
     else if (warp >= EPI_WARP0)
