@@ -317,116 +317,6 @@ __device__ __forceinline__ void transpose_side(const uint8_t* raw, uint8_t* atom
     }
 }
 
-// flatS groups [0, G_TOTAL) of two operands handled by LANES threads: groups
-// below G_A belong to operand A (raw_a/atoms_a, RB_A 128-row blocks), the
-// rest to operand B.  Same per-group transform as transpose_side.
-template <int G_A, int RB_A, int G_TOTAL, int RB_B, int LANES>
-__device__ __forceinline__ void transpose_groups(const uint8_t* raw_a, uint8_t* atoms_a, const uint8_t* raw_b,
-                                                 uint8_t* atoms_b, int t)
-{
-    constexpr int OPS = G_TOTAL * 16;
-#pragma unroll
-    for (int op = t; op < OPS; op += LANES)
-    {
-        const int gg = op >> 4, rho = op & 15;
-        const bool is_a = gg < G_A;
-        const int g = is_a ? gg : gg - G_A;
-        const uint32_t* raw32 = reinterpret_cast<const uint32_t*>(is_a ? raw_a : raw_b);
-        uint8_t* atoms = is_a ? atoms_a : atoms_b;
-        const int RB = is_a ? RB_A : RB_B;
-        const uint32_t w0 = raw32[g * 64 + rho];
-        const uint32_t w1 = raw32[g * 64 + 16 + rho];
-        const uint32_t w2 = raw32[g * 64 + 32 + rho];
-        const uint32_t w3 = raw32[g * 64 + 48 + rho];
-        const uint32_t t0 = __byte_perm(w0, w1, 0x5140);
-        const uint32_t t1 = __byte_perm(w2, w3, 0x5140);
-        const uint32_t t2 = __byte_perm(w0, w1, 0x7362);
-        const uint32_t t3 = __byte_perm(w2, w3, 0x7362);
-        const uint32_t o[4] = {__byte_perm(t0, t1, 0x5410), __byte_perm(t0, t1, 0x7632),
-                               __byte_perm(t2, t3, 0x5410), __byte_perm(t2, t3, 0x7632)};
-#pragma unroll
-        for (int pp = 0; pp < 4; ++pp)
-        {
-            const int r = 32 * g + 16 * (pp & 1) + rho;
-            const int q = pp >> 1;
-            *reinterpret_cast<uint32_t*>(atoms + (q * RB + (r >> 7)) * 512 + (r & 31) * 16 +
-                                         ((r >> 5) & 3) * 4) = o[pp];
-        }
-    }
-}
-
-// Raw scales -> "replicated" blocks for tcgen05.cp.128x256b.  A replicated
-// block is the 512-byte 32x16B block above repeated at +0/+512/+1024/+1536
-// (2 KB = 128 rows x 16 B), so that a 128x256b copy of two such blocks
-// (LBO 2048 B, SBO 128 B) writes exactly what two 32x128b.warpx4 copies would
-// write: lane 32s + l, column c of block j <- row l, bytes 4c..4c+3.
-//   SFA (128 rows): block j = K-group set q   (base + q*2048)
-//   SFB (256 rows): block j = 128-row block b, one 4 KB buffer per q
-// One lane-op = (128-row block b, row-in-16 rho): the four 32-row groups of
-// the block at that rho are transposed together and each (h, q) result row
-// (16 B) is stored to the four replicas.
-template <int G_A, int G_B, int LANES>
-__device__ __forceinline__ void transpose_rep(const uint8_t* raw_a, uint8_t* rep_a, const uint8_t* raw_b,
-                                              uint8_t* rep_b, int t)
-{
-    constexpr int BLK_A = G_A / 4, BLK_B = G_B / 4;
-    constexpr int OPS = (BLK_A + BLK_B) * 16;
-#pragma unroll
-    for (int op = t; op < OPS; op += LANES)
-    {
-        const int blk = op >> 4, rho = op & 15;
-        const bool is_a = blk < BLK_A;
-        const int b = is_a ? blk : blk - BLK_A;
-        const uint32_t* raw32 = reinterpret_cast<const uint32_t*>(is_a ? raw_a : raw_b) + b * 4 * 64;
-        uint32_t o[4][4];  // [group in block][p]
-#pragma unroll
-        for (int gg = 0; gg < 4; ++gg)
-        {
-            const uint32_t w0 = raw32[gg * 64 + rho];
-            const uint32_t w1 = raw32[gg * 64 + 16 + rho];
-            const uint32_t w2 = raw32[gg * 64 + 32 + rho];
-            const uint32_t w3 = raw32[gg * 64 + 48 + rho];
-            const uint32_t t0 = __byte_perm(w0, w1, 0x5140);
-            const uint32_t t1 = __byte_perm(w2, w3, 0x5140);
-            const uint32_t t2 = __byte_perm(w0, w1, 0x7362);
-            const uint32_t t3 = __byte_perm(w2, w3, 0x7362);
-            o[gg][0] = __byte_perm(t0, t1, 0x5410);
-            o[gg][1] = __byte_perm(t0, t1, 0x7632);
-            o[gg][2] = __byte_perm(t2, t3, 0x5410);
-            o[gg][3] = __byte_perm(t2, t3, 0x7632);
-        }
-#pragma unroll
-        for (int pp = 0; pp < 4; ++pp)
-        {
-            const int h = pp & 1, q = pp >> 1;
-            const uint4 v = make_uint4(o[0][pp], o[1][pp], o[2][pp], o[3][pp]);
-            uint8_t* blkp = is_a ? rep_a + q * 2048 : rep_b + q * 4096 + b * 2048;
-            uint8_t* dst = blkp + (16 * h + rho) * 16;
-#pragma unroll
-            for (int s = 0; s < 4; ++s) *reinterpret_cast<uint4*>(dst + s * 512) = v;
-        }
-    }
-}
-
-// Macro-block B scales -> replicated SFB blocks: every row of a 32-row group
-// shares the group's bytes, so each block row is the same 16 bytes.
-template <int LANES>
-__device__ __forceinline__ void transpose_rep_macro_b(const uint8_t* raw, uint8_t* rep_b, int ks, int t)
-{
-    // 2 groups-of-4 x 2 row blocks x 128 rows, 16 B each
-    constexpr int OPS = 2 * 2 * 128;
-#pragma unroll 4
-    for (int op = t; op < OPS; op += LANES)
-    {
-        const int q = op >> 8, b = (op >> 7) & 1, i = op & 127;
-        const uint8_t* src = raw + 8 * (ks & 1) + 4 * q;
-        const uint4 v = make_uint4(*reinterpret_cast<const uint32_t*>(src + (4 * b + 0) * 16),
-                                   *reinterpret_cast<const uint32_t*>(src + (4 * b + 1) * 16),
-                                   *reinterpret_cast<const uint32_t*>(src + (4 * b + 2) * 16),
-                                   *reinterpret_cast<const uint32_t*>(src + (4 * b + 3) * 16));
-        *reinterpret_cast<uint4*>(rep_b + q * 4096 + b * 2048 + i * 16) = v;
-    }
-}
 
 // ------------------------------------------------------------------ kernel
 template <class CF>
@@ -1059,10 +949,11 @@ __global__ void __launch_bounds__(256) pack_weight_kernel(const uint8_t* __restr
 // single-CTA 128 x 256 tile.
 //
 // Scales reach it as "scale images" written by scale_image_kernel: per
-// 128-row block of A and per 256-row tile of B, per K stage, the exact bytes
-// tcgen05.cp.128x256b moves into TMEM (see transpose_rep).  Every image is
-// reused by all tiles of its row / column, so building them once per call
-// costs a few microseconds and removes all scale work from the GEMM.
+// 128-row block of A and per 256-row tile of B, per K stage, the 512-byte
+// 32x16B blocks tcgen05.cp.32x128b.warpx4 copies into TMEM (the copy
+// replicates them to all four lane quarters).  Every image is reused by all
+// tiles of its row / column, so building them once per call costs a few
+// microseconds and removes all scale work from the GEMM.
 //
 // Protocol (leader = cluster rank 0):
 //   * both producers wait on their own `empty` slot (the leader's commit
@@ -1080,19 +971,21 @@ __global__ void __launch_bounds__(256) pack_weight_kernel(const uint8_t* __restr
 //   * each CTA's epilogue drains its own TMEM and arrives on the leader's
 //     `acc_empty` (16 warps).
 
-constexpr int IMG_A_BYTES = 2 * 2048;      // per 128 A rows per K stage
-constexpr int IMG_B_BYTES = 2 * 2 * 2048;  // per 256 B rows per K stage
+constexpr int IMG_A_BYTES = 2 * 512;      // per 128 A rows per K stage: [q] blocks
+constexpr int IMG_B_BYTES = 2 * 2 * 512;  // per 256 B rows per K stage: [q][128-row half] blocks
 
 // flatS scales (or macro-block B scales) -> scale images.
-//   A image [rb128][ks][q][s][l][16 B]: word w = SF(128rb + 32w + l, 8ks+4q+k)
-//   B image [tb256][ks][q][b][s][l][16 B]: word w = SF(256tb + 128b + 32w + l, ...)
-// for replicas s = 0..3 (identical).  Rows outside the scale buffer give 0.
+//   A image [rb128][ks][q][l][16 B]: word w of row l, byte k = SF(128rb + 32w + l, 8ks + 4q + k)
+//   B image [tb256][ks][q][b][l][16 B]: word w = SF(256tb + 128b + 32w + l, ...)
+// i.e. per (block, K stage, K-group set q) the 32x16B block tcgen05.cp
+// .32x128b.warpx4 takes.  Rows outside the scale buffer give 0.
 // One thread per (128-row block, K stage, row-in-16 rho): it loads the 16
 // flatS words of the block's four 32-row groups at that rho (word k*16 + rho
 // of each group's 256-byte chunk holds the scales of rows rho and rho + 16
-// for the K-group k of both sets of 4), transposes them as transpose_rep does
-// and writes four 16-byte rows to each replica.  Macro-block B scales are
-// shared by all rows of a 32-row group, so their image rows are copies.
+// for the K-group k of both sets of 4), transposes them with byte
+// permutes and writes the four 16-byte rows (rho and rho + 16, both q).
+// Macro-block B scales are shared by all rows of a 32-row group, so their
+// image rows are copies.
 __global__ void __launch_bounds__(256) scale_image_kernel(const uint8_t* __restrict__ sa, int a_rows_buf,
                                                           int a_blocks, const uint8_t* __restrict__ sb,
                                                           int b_rows_buf, int b_tiles, int snp, int ks_count,
@@ -1166,11 +1059,9 @@ __global__ void __launch_bounds__(256) scale_image_kernel(const uint8_t* __restr
         {
             const int h = pp & 1, q = pp >> 1;
             const uint4 v4 = make_uint4(o[0][pp], o[1][pp], o[2][pp], o[3][pp]);
-            uint8_t* dst = is_a ? img_a + (blk * ks_count + ks) * IMG_A_BYTES + q * 2048
-                                : img_b + (blk * ks_count + ks) * IMG_B_BYTES + q * 4096 + b * 2048;
-            dst += (16 * h + rho) * 16;
-#pragma unroll
-            for (int s = 0; s < 4; ++s) *reinterpret_cast<uint4*>(dst + s * 512) = v4;
+            uint8_t* dst = is_a ? img_a + (blk * ks_count + ks) * IMG_A_BYTES + q * 512
+                                : img_b + (blk * ks_count + ks) * IMG_B_BYTES + q * 1024 + b * 512;
+            *reinterpret_cast<uint4*>(dst + (16 * h + rho) * 16) = v4;
         }
     }
 }
@@ -1421,12 +1312,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) __cluster_dims__(2, 1, 1)
                     const uint8_t* st = smem + slot * CF::STAGE_BYTES;
                     const uint32_t sf_a = tmem_base + CF::SF_BASE + slot * CF::SF_STAGE_COLS;
                     const uint32_t sf_b = sf_a + 8;
-                    // 3 copies of 128 rows x 32 B: SFA both K-group sets, SFB one set each
-                    tc_cp_128x256b_pair(sf_a, make_smem_desc(smem_u32(st + CF::A_IMG_OFF), 2048, 128, 0));
+                    // SFA: one 32x16B block per K-group set q; SFB: per q, one per 128-row half
 #pragma unroll
                     for (int q = 0; q < 2; ++q)
-                        tc_cp_128x256b_pair(sf_b + 8 * q,
-                                            make_smem_desc(smem_u32(st + CF::B_IMG_OFF + q * 4096), 2048, 128, 0));
+                        tc_cp_32x128b_warpx4_pair(sf_a + 4 * q,
+                                                  make_smem_desc(smem_u32(st + CF::A_IMG_OFF + q * 512), 0, 128, 0));
+#pragma unroll
+                    for (int a = 0; a < 4; ++a)
+                        tc_cp_32x128b_warpx4_pair(sf_b + 4 * a,
+                                                  make_smem_desc(smem_u32(st + CF::B_IMG_OFF + a * 512), 0, 128, 0));
                     tc_commit_pair_mc(&sfready[slot], 0x1);
                     if (++slot == STAGES)
                     {
@@ -1966,7 +1860,7 @@ int dispatch(const Problem& pb, const Plan& pl, const DeviceInfo& dev, void* ws,
         if (pl.r_rows == 64) return launch_cfg<Cfg<256, false, false, 5, 64, true>>(pb, pl, dev, ws, s);
         return launch_cfg<Cfg<256, false, false, 4, 128, true>>(pb, pl, dev, ws, s);
     }
-    if (pl.pair) return launch_pair<CfgPair<4>>(pb, pl, dev, ws, s);
+    if (pl.pair) return launch_pair<CfgPair<6>>(pb, pl, dev, ws, s);
     if (pl.swap)
     {
         if (pl.bn == 32)

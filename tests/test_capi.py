@@ -81,11 +81,11 @@ def test_quant_and_shuffle_validation_without_device(lib):
 def test_workspace_size_is_host_only(lib):
     lib.mbs_gemm_a4w4_workspace_size.restype = ctypes.c_size_t
     # decode shapes use stream-K partials; a large prefill runs on CTA pairs
-    # whose workspace holds the scale images (4 KB per 128 rows of A and 8 KB
+    # whose workspace holds the scale images (1 KB per 128 rows of A and 2 KB
     # per 256 rows of B, per 256-element K stage)
     assert lib.mbs_gemm_a4w4_workspace_size(16, 57344, 8192) > 0
     # flag words first, then the pair path's A and B scale images
-    assert lib.mbs_gemm_a4w4_workspace_size(8192, 8192, 8192) == 4096 + 64 * 32 * 4096 + 32 * 32 * 8192
+    assert lib.mbs_gemm_a4w4_workspace_size(8192, 8192, 8192) == 4096 + 64 * 32 * 1024 + 32 * 32 * 2048
     # stream-K: flag words, then one [BN=256][32 rows] fp32 partial slot per CTA (G = 148 SMs
     # is not known without a device, so only the layout's lower bound is checked)
     for shape in [(16, 57344, 8192), (1, 16, 64), (300, 272, 1088)]:
