@@ -293,6 +293,14 @@ def run_mbs(args):
                 "unit": "TFLOP/s", "frac": round(kernel_tflops / peak, 4), "traffic": traffic,
                 "peak_source": f"4 x bf16_tflops of {src} (dense FP4:BF16 = 4:1)",
                 "kernel_ms": round(kernel_ms, 5)}
+        # the measured mxf4 tensor-pipe peak of this GPU (MMA-only probe), beside the derived one
+        from mbs_b200.probe import mxf4_peak_probe
+        pr = mxf4_peak_probe(groups=20000, device=dev)
+        roof["peak_probe"] = {"tflops": round(pr["tflops"], 1), "sm_mhz": round(pr["sm_mhz"], 1),
+                              "cycles_per_mma": round(pr["cycles_per_mma"], 2),
+                              "frac": round(kernel_tflops / pr["tflops"], 4),
+                              "what": "mbs_mxf4_peak_probe: back-to-back 256x256x64 pair MMAs, "
+                                      "operands resident in shared memory, no memory traffic"}
     else:
         nbytes = N * K // 2 + N * K // 32 + M * K // 2 + M * K // 32 + M * N * 2
         gbs = nbytes / (kernel_ms * 1e-3) / 1e9

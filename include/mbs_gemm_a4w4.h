@@ -212,6 +212,19 @@ int mbs_set_profile_events(void* before_main, void* after_main);
  */
 int mbs_device_error(int* code_out, int reset);
 
+/*
+ * Diagnostic: the tensor-pipe peak of tcgen05.mma kind::mxf4 on the current
+ * device, measured with every CTA pair issuing `groups` x 4 back-to-back
+ * 256x256x64 pair MMAs (the prefill kernel's instruction) on operands
+ * resident in shared memory and scales resident in TMEM.  Writes the
+ * grid's TFLOP/s (CUDA events), cycles per MMA and the SM clock seen (MHz).
+ * Blocks until done (synchronises `stream`).  groups in [16, 2^24].  This is
+ * the roofline denominator a compute-bound GEMM is quoted against; the
+ * reference has no counterpart (its MFMA probe, kernel/mfma_probe.hip, only
+ * checks numerics).
+ */
+int mbs_mxf4_peak_probe(int groups, double* tflops, double* cycles_per_mma, double* sm_mhz, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -38,6 +38,7 @@ SIGNATURES = {
     "mbs_gemm_a4w4_packed_workspace_size": (_c_size_t, [_c_int] * 3),
     "mbs_gemm_a4w4_packed_launch_ws": (_c_int, [_c_void_p] * 6 + [_c_int] * 5 + [_c_void_p, _c_size_t,
                                                                                 _c_void_p]),
+    "mbs_mxf4_peak_probe": (_c_int, [_c_int] + [ctypes.POINTER(ctypes.c_double)] * 3 + [_c_void_p]),
 }
 
 _lock = threading.Lock()
