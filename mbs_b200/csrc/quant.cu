@@ -1,6 +1,8 @@
 // bf16 -> MXFP4 quantisers and the two layout kernels (weight preshuffle,
 // scale shuffle).  All are HBM-bound byte work: 16-byte vector loads/stores,
-// integer arithmetic for the scale, warp shuffles for the block amax.
+// integer arithmetic for the scale, warp shuffles for the block amax, and the
+// hardware e2m1 conversion for the codes (a bit-level software encoding cost
+// ~20 instructions per element and made the quantiser issue-bound).
 //
 // Quantiser arithmetic (OCP MX per-1x32, the task's spec for aiter's
 // per_1x32 quantiser called at test_gemm_a4w4.py:134-140):
@@ -17,21 +19,34 @@
 namespace mbs {
 namespace {
 
-// e2m1 magnitude code of q in [0, 8) with round-to-nearest-even, saturating
-// at 6 (code 7).  The grid {0, .5, 1, 1.5, 2, 3, 4, 6} is one mantissa bit
-// above 1 and a fixed 0.5 step below it:
-//   q <  1: code = rint(2q)  (ties 0.25 -> 0 and 0.75 -> 2 go to even)
-//   q >= 1: round the fp32 significand to 1 bit, RNE (add 2^21 - 1 plus the
-//           kept bit, so a carry happens above half and at half only when
-//           the kept bit is 1); bits [30:22] are then 2*E + m with E the
-//           biased exponent, and the code is 2*(E-126) + m = (bits>>22) - 252.
-//           Rounding 7.x up gives 8 (code 8), clamped to 6 (code 7).
-__device__ __forceinline__ uint32_t e2m1_code(float q)
+// Eight fp32 values -> eight e2m1 codes packed low nibble first, with the
+// sm_100a conversion cvt.rn.satfinite.e2m1x2.f32: IEEE round-to-nearest-even
+// onto {0,.5,1,1.5,2,3,4,6}, saturating at +-6, the sign kept (so a value
+// that rounds to zero keeps its sign bit, -0 -> 0x8).  The inputs are
+// x * 2^(127 - scale) for bf16 x, exact products (a power of two), so this
+// is the spec's code for every finite x.  The instruction writes its first
+// source to the high nibble, hence the (odd, even) operand order.
+__device__ __forceinline__ uint32_t cvt_e2m1x8(const float (&f)[8])
 {
-    if (q < 1.0f) return (uint32_t)__float2int_rn(q * 2.0f);
-    const uint32_t b = __float_as_uint(q);
-    const uint32_t c = ((b + 0x1FFFFFu + ((b >> 22) & 1u)) >> 22) - 252u;
-    return c < 7u ? c : 7u;
+    uint32_t out;
+    asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+        "cvt.rn.satfinite.e2m1x2.f32 b0, %2, %1;\n\t"
+        "cvt.rn.satfinite.e2m1x2.f32 b1, %4, %3;\n\t"
+        "cvt.rn.satfinite.e2m1x2.f32 b2, %6, %5;\n\t"
+        "cvt.rn.satfinite.e2m1x2.f32 b3, %8, %7;\n\t"
+        "mov.b32 %0, {b0, b1, b2, b3};\n\t}"
+        : "=r"(out)
+        : "f"(f[0]), "f"(f[1]), "f"(f[2]), "f"(f[3]), "f"(f[4]), "f"(f[5]), "f"(f[6]), "f"(f[7]));
+    return out;
+}
+
+// max |x| bit pattern over the 8 bf16 of four 32-bit words (|x| bits =
+// bits & 0x7FFF order like the magnitudes); two halfword maxes per step.
+__device__ __forceinline__ uint32_t amax_bits8(const uint32_t (&w)[4])
+{
+    const uint32_t m = __vmaxu2(__vmaxu2(w[0] & 0x7FFF7FFFu, w[1] & 0x7FFF7FFFu),
+                                __vmaxu2(w[2] & 0x7FFF7FFFu, w[3] & 0x7FFF7FFFu));
+    return max(m & 0xFFFFu, m >> 16);
 }
 
 __device__ __forceinline__ uint32_t scale_from_amax_bits(uint32_t amax_bits)
@@ -41,14 +56,20 @@ __device__ __forceinline__ uint32_t scale_from_amax_bits(uint32_t amax_bits)
     return (uint32_t)max(e - 2, 0);
 }
 
-// Encode 2 bf16 (one 32-bit word) with multiplier `inv` = 2^(127 - scale).
-__device__ __forceinline__ uint32_t encode_pair(uint32_t w, float inv, bool nan_block)
+// Encode 8 bf16 (four 32-bit words, element 0 in the low half of w[0]) with
+// multiplier `inv` = 2^(127 - scale): 32 bits of packed codes.  Blocks that
+// hold an Inf or NaN get all-zero codes.
+__device__ __forceinline__ uint32_t encode8(const uint32_t (&w)[4], float inv, bool nan_block)
 {
-    const uint32_t lo = w & 0xFFFFu, hi = w >> 16;
-    uint32_t c0 = e2m1_code(__uint_as_float((lo & 0x7FFFu) << 16) * inv) | ((lo >> 15) << 3);
-    uint32_t c1 = e2m1_code(__uint_as_float((hi & 0x7FFFu) << 16) * inv) | ((hi >> 15) << 3);
-    if (nan_block) c0 = c1 = 0;
-    return c0 | (c1 << 4);
+    float f[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+    {
+        f[2 * i] = __uint_as_float(w[i] << 16) * inv;
+        f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u) * inv;
+    }
+    const uint32_t packed = cvt_e2m1x8(f);
+    return nan_block ? 0u : packed;
 }
 
 __device__ __forceinline__ int64_t flat_s(int r, int b, int snp)
@@ -94,20 +115,14 @@ __global__ void __launch_bounds__(QUANT_THREADS) quantize_1x32_kernel(const uint
                 const int j = j0 + u * QUANT_THREADS;
                 if (j - (int)(threadIdx.x & 31) >= limit) break;  // whole warp past the row end
                 const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
-                uint32_t am = 0;
-#pragma unroll
-                for (int i = 0; i < 4; ++i)
-                    am = max(am, max(w[i] & 0x7FFFu, (w[i] >> 16) & 0x7FFFu));
+                uint32_t am = amax_bits8(w);
                 am = max(am, __shfl_xor_sync(0xffffffffu, am, 1));
                 am = max(am, __shfl_xor_sync(0xffffffffu, am, 2));
                 if (j >= oct) continue;
                 const uint32_t s = scale_from_amax_bits(am);
                 const bool nan_block = s == 0xFFu;
                 const float inv = __uint_as_float((254u - (nan_block ? 254u : s)) << 23);
-                uint32_t packed = 0;
-#pragma unroll
-                for (int i = 0; i < 4; ++i) packed |= encode_pair(w[i], inv, nan_block) << (8 * i);
-                qr[j] = packed;
+                qr[j] = encode8(w, inv, nan_block);
                 if ((j & 3) == 0)
                 {
                     const int b = j >> 2;
@@ -180,7 +195,11 @@ __global__ void __launch_bounds__(256) quantize_macro_kernel(const uint16_t* __r
         }
         uint32_t am = 0;
 #pragma unroll
-        for (int i = 0; i < 16; ++i) am = max(am, max(w[i] & 0x7FFFu, (w[i] >> 16) & 0x7FFFu));
+        for (int i = 0; i < 4; ++i)
+        {
+            const uint32_t wi[4] = {w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]};
+            am = max(am, amax_bits8(wi));
+        }
 #pragma unroll
         for (int m = 1; m < 32; m <<= 1) am = max(am, __shfl_xor_sync(0xffffffffu, am, m));
         const uint32_t s = scale_from_amax_bits(am);
@@ -192,10 +211,8 @@ __global__ void __launch_bounds__(256) quantize_macro_kernel(const uint16_t* __r
 #pragma unroll
             for (int i = 0; i < 4; ++i)
             {
-                uint32_t p = 0;
-#pragma unroll
-                for (int t = 0; t < 4; ++t) p |= encode_pair(w[4 * i + t], inv, nan_block) << (8 * t);
-                out[i] = p;
+                const uint32_t wi[4] = {w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]};
+                out[i] = encode8(wi, inv, nan_block);
             }
             *reinterpret_cast<uint4*>(q + (int64_t)r * (K >> 1) + kb * 16) =
                 make_uint4(out[0], out[1], out[2], out[3]);

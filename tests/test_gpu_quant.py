@@ -47,6 +47,52 @@ def test_quantize_bit_exact(R, K, shuffle):
         assert np.array_equal(s.cpu().numpy(), s_ref)
 
 
+def _from_bits(bits: np.ndarray) -> torch.Tensor:
+    return torch.from_numpy(bits.astype(np.uint16).view(np.int16)).view(torch.bfloat16)
+
+
+@pytest.mark.parametrize("macro", [False, True])
+def test_quantize_every_bf16_pattern(macro):
+    """All 65536 bf16 bit patterns (in order, 32 per block: zero, subnormal,
+    normal, Inf and NaN blocks of both signs) against the oracle."""
+    import mbs_b200
+    bits = np.arange(65536, dtype=np.uint32).astype(np.uint16).reshape(64, 1024)
+    x = _from_bits(bits)
+    if macro:
+        q, s = mbs_b200.quantize_mxfp4_macro(x.cuda())
+        q_ref, s_ref = O.quantize_mxfp4_macro(bits)
+    else:
+        q, s = mbs_b200.quantize_mxfp4(x.cuda(), shuffle=False)
+        q_ref, s_ref = O.quantize_mxfp4(bits)
+    torch.cuda.synchronize()
+    assert np.array_equal(q.cpu().numpy(), q_ref)
+    assert np.array_equal(s.cpu().numpy(), s_ref)
+
+
+def test_quantize_ties_and_saturation_at_every_scale():
+    """Blocks whose amax is 4 * 2^k hold every rounding midpoint of the e2m1
+    grid (ties to even), values just off the midpoints, values that saturate
+    and values that round to zero, at scales k = -126..126, both signs."""
+    import mbs_b200
+    mids = [0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0, 7.0, 0.125, 0.2, 0.3, 6.5, 5.5, 4.5, 2.75]
+    rows = []
+    for k in range(-126, 127):
+        blk = np.zeros(32, dtype=np.float32)
+        blk[0] = 4.0
+        blk[1:1 + len(mids)] = mids
+        blk[16:16 + len(mids)] = [-m for m in mids]
+        blk[31] = -7.9
+        rows.append(np.ldexp(blk, k))
+    xf = torch.from_numpy(np.stack(rows)).to(torch.bfloat16)   # [253, 32] rows of one block each
+    x = xf.repeat(1, 2)                                         # K = 64
+    bits = x.view(torch.int16).numpy().view(np.uint16)
+    q, s = mbs_b200.quantize_mxfp4(x.cuda(), shuffle=False)
+    q_ref, s_ref = O.quantize_mxfp4(bits)
+    torch.cuda.synchronize()
+    assert np.array_equal(s.cpu().numpy(), s_ref)
+    assert np.array_equal(q.cpu().numpy(), q_ref)
+
+
 def test_quantize_strided_rows():
     import mbs_b200
     big = seeded_bf16(40, 512, seed=5)
