@@ -175,6 +175,18 @@ int mbs_quantize_mxfp4(const void* x_bf16, int rows, int K, int ld_x, uint8_t* f
                        uint8_t* scale_out, int shuffled, void* stream);
 
 /*
+ * As mbs_quantize_mxfp4, fused with the MBS factor producer the reference
+ * describes but does not ship (docs/kernel_advanced.md:120-129): per row,
+ * factor_out[r] = b = the top 8 mantissa bits of 6.0 / max|x[r,:]| (IEEE
+ * division, bits truncated; 0 for a zero, Inf or NaN max), and the row is
+ * quantised as x * (1 + b/256) (exact in fp32; block scales from the fp32
+ * amax).  Passing b as A_factor (or B_factor for weight rows) to the GEMM
+ * multiplies the result by 1 / (1 + b/256), which undoes the scaling.
+ */
+int mbs_quantize_mxfp4_mbs(const void* x_bf16, int rows, int K, int ld_x, uint8_t* fp4_out,
+                           uint8_t* scale_out, uint8_t* factor_out, int shuffled, void* stream);
+
+/*
  * Macro-block quantiser: one scale per 32-row x 32-K block of x, written as
  * scale_out[ceil(rows/32)][roundup(K/32,16)] (padding 127).  No reference
  * counterpart (spec-defined).

@@ -27,6 +27,8 @@ SIGNATURES = {
                                       + [_c_void_p, _c_size_t, _c_void_p]),
     "mbs_quantize_mxfp4": (_c_int, [_c_void_p, _c_int, _c_int, _c_int, _c_void_p, _c_void_p, _c_int,
                                     _c_void_p]),
+    "mbs_quantize_mxfp4_mbs": (_c_int, [_c_void_p, _c_int, _c_int, _c_int, _c_void_p, _c_void_p, _c_void_p,
+                                        _c_int, _c_void_p]),
     "mbs_quantize_mxfp4_macro": (_c_int, [_c_void_p, _c_int, _c_int, _c_int, _c_void_p, _c_void_p,
                                           _c_void_p]),
     "mbs_shuffle_weight": (_c_int, [_c_void_p, _c_void_p, _c_int, _c_int, _c_void_p]),

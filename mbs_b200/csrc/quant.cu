@@ -72,6 +72,38 @@ __device__ __forceinline__ uint32_t encode8(const uint32_t (&w)[4], float inv, b
     return nan_block ? 0u : packed;
 }
 
+// As encode8 for MBS rows: the values are (x * m) * inv, both products exact
+// (m = 1 + b/256 has 9 significant bits; inv is a power of two; m * inv alone
+// could overflow when the block scale is 0).
+__device__ __forceinline__ uint32_t encode8_mbs(const uint32_t (&w)[4], float m, float inv, bool nan_block)
+{
+    float f[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+    {
+        f[2 * i] = (__uint_as_float(w[i] << 16) * m) * inv;
+        f[2 * i + 1] = (__uint_as_float(w[i] & 0xFFFF0000u) * m) * inv;
+    }
+    const uint32_t packed = cvt_e2m1x8(f);
+    return nan_block ? 0u : packed;
+}
+
+// MBS factor byte of a row whose max |x| has bf16 bit pattern `amax_bits`:
+// the top 8 mantissa bits of 6.0 / max (IEEE division, bits truncated;
+// docs/kernel_advanced.md:122-125 of the reference); 0 for a zero, Inf or
+// NaN max, and for a max so close to the top of the fp32 range that max * m
+// would overflow (finite rows never become Inf blocks).  The row is then
+// scaled by m = 1 + b/256, undone by the GEMM's factor 1/m.
+__device__ __forceinline__ uint32_t mbs_factor_byte(uint32_t amax_bits)
+{
+    if (amax_bits == 0u || amax_bits >= 0x7F80u) return 0u;
+    const float amax = __uint_as_float(amax_bits << 16);
+    const float sc = __fdiv_rn(6.0f, amax);
+    const uint32_t b = (__float_as_uint(sc) >> 15) & 0xFFu;
+    const float scaled = amax * __uint_as_float(0x3F800000u | (b << 15));
+    return (__float_as_uint(scaled) & 0x7F800000u) == 0x7F800000u ? 0u : b;
+}
+
 __device__ __forceinline__ int64_t flat_s(int r, int b, int snp)
 {
     const int r32 = r & 31, b8 = b & 7;
@@ -88,50 +120,144 @@ __device__ __forceinline__ int64_t flat_s(int r, int b, int snp)
 constexpr int QUANT_UNROLL = 4;
 constexpr int QUANT_THREADS = 256;
 
+// MBS = true: each row is first reduced to its max |x| (one read of the row,
+// kept in L2 for the second), its factor byte b is written to `factors`, and
+// the row is quantised as x * (1 + b/256).
+// Codes and scales of one group of QUANT_UNROLL octets per thread (octet j =
+// j0 + u * QUANT_THREADS of row r), the row already multiplied by m when MBS.
+template <bool MBS>
+__device__ __forceinline__ void quantize_group(const uint4 (&v)[QUANT_UNROLL], int j0, int oct, int limit,
+                                               float m, int r, int K, uint32_t* __restrict__ qr,
+                                               uint8_t* __restrict__ sc, int shuffled, int snp)
+{
+#pragma unroll
+    for (int u = 0; u < QUANT_UNROLL; ++u)
+    {
+        const int j = j0 + u * QUANT_THREADS;
+        if (j - (int)(threadIdx.x & 31) >= limit) break;  // whole warp past the row end
+        const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+        uint32_t am = amax_bits8(w);
+        am = max(am, __shfl_xor_sync(0xffffffffu, am, 1));
+        am = max(am, __shfl_xor_sync(0xffffffffu, am, 2));
+        if (j >= oct) continue;
+        uint32_t s;
+        if constexpr (MBS)
+        {
+            // block amax of x * m is m * amax (exact): scale from its fp32 exponent
+            const uint32_t e = (__float_as_uint(__uint_as_float(am << 16) * m) >> 23) & 0xFFu;
+            s = am >= 0x7F80u ? 0xFFu : (e > 2u ? e - 2u : 0u);
+        }
+        else
+        {
+            s = scale_from_amax_bits(am);
+        }
+        const bool nan_block = s == 0xFFu;
+        const float inv = __uint_as_float((254u - (nan_block ? 254u : s)) << 23);
+        qr[j] = MBS ? encode8_mbs(w, m, inv, nan_block) : encode8(w, inv, nan_block);
+        if ((j & 3) == 0)
+        {
+            const int b = j >> 2;
+            if (shuffled)
+                sc[flat_s(r, b, snp)] = (uint8_t)s;
+            else
+                sc[(int64_t)r * (K >> 5) + b] = (uint8_t)s;
+        }
+    }
+}
+
+template <int UNROLL>
+__device__ __forceinline__ void load_group(const uint4* __restrict__ xr, int j0, int oct, uint4 (&v)[UNROLL],
+                                           bool last_use)
+{
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u)
+    {
+        const int j = j0 + u * QUANT_THREADS;
+        v[u] = j < oct ? (last_use ? __ldcs(xr + j) : __ldcg(xr + j)) : make_uint4(0, 0, 0, 0);
+    }
+}
+
+// MBS row factor: CTA-wide max of the threads' `am`, factor byte to
+// factors[r], returns the row multiplier m = 1 + b/256.
+__device__ __forceinline__ float mbs_row_multiplier(uint32_t am, int r, uint8_t* __restrict__ factors,
+                                                    uint32_t* red)
+{
+    am = __reduce_max_sync(0xffffffffu, am);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = am;
+    __syncthreads();
+    if (threadIdx.x < 32)
+    {
+        uint32_t a = threadIdx.x < QUANT_THREADS / 32 ? red[threadIdx.x] : 0u;
+        a = __reduce_max_sync(0xffffffffu, a);
+        if (threadIdx.x == 0)
+        {
+            const uint32_t b = mbs_factor_byte(a);
+            factors[r] = (uint8_t)b;
+            red[0] = b;
+        }
+    }
+    __syncthreads();
+    const float m = __uint_as_float(0x3F800000u | (red[0] << 15));
+    __syncthreads();  // red is rewritten by the next row
+    return m;
+}
+
+// MBS = true: each row is first reduced to its max |x|, its factor byte b is
+// written to `factors`, and the row is quantised as x * (1 + b/256).  A row
+// of up to QUANT_THREADS * QUANT_UNROLL octets (K <= 8192) stays in registers
+// between the two steps; longer rows are read twice (the second read from L2).
+template <bool MBS>
 __global__ void __launch_bounds__(QUANT_THREADS) quantize_1x32_kernel(const uint16_t* __restrict__ x,
                                                                       int rows, int K, int ld_x,
                                                                       uint8_t* __restrict__ q,
                                                                       uint8_t* __restrict__ sc, int shuffled,
-                                                                      int snp)
+                                                                      int snp, uint8_t* __restrict__ factors)
 {
+    __shared__ uint32_t red[QUANT_THREADS / 32];
     const int oct = K >> 3;                 // octets in a row (multiple of 4)
     const int limit = (oct + 31) & ~31;     // whole warps
+    const bool one_pass = oct <= QUANT_THREADS * QUANT_UNROLL;
     for (int r = blockIdx.x; r < rows; r += gridDim.x)
     {
         const uint4* xr = reinterpret_cast<const uint4*>(x + (int64_t)r * ld_x);
         uint32_t* qr = reinterpret_cast<uint32_t*>(q + (int64_t)r * (K >> 1));
+        if (MBS && one_pass)
+        {
+            uint4 v[QUANT_UNROLL];
+            load_group<QUANT_UNROLL>(xr, threadIdx.x, oct, v, true);
+            uint32_t am = 0;
+#pragma unroll
+            for (int u = 0; u < QUANT_UNROLL; ++u)
+            {
+                const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+                am = max(am, amax_bits8(w));
+            }
+            const float m = mbs_row_multiplier(am, r, factors, red);
+            quantize_group<MBS>(v, threadIdx.x, oct, limit, m, r, K, qr, sc, shuffled, snp);
+            continue;
+        }
+        float m = 1.0f;
+        if constexpr (MBS)
+        {
+            uint32_t am = 0;
+            for (int j0 = threadIdx.x; j0 < oct; j0 += QUANT_THREADS * QUANT_UNROLL)
+            {
+                uint4 v[QUANT_UNROLL];
+                load_group<QUANT_UNROLL>(xr, j0, oct, v, false);
+#pragma unroll
+                for (int u = 0; u < QUANT_UNROLL; ++u)
+                {
+                    const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+                    am = max(am, amax_bits8(w));
+                }
+            }
+            m = mbs_row_multiplier(am, r, factors, red);
+        }
         for (int j0 = threadIdx.x; j0 < limit; j0 += QUANT_THREADS * QUANT_UNROLL)
         {
             uint4 v[QUANT_UNROLL];
-#pragma unroll
-            for (int u = 0; u < QUANT_UNROLL; ++u)
-            {
-                const int j = j0 + u * QUANT_THREADS;
-                v[u] = j < oct ? __ldcs(xr + j) : make_uint4(0, 0, 0, 0);
-            }
-#pragma unroll
-            for (int u = 0; u < QUANT_UNROLL; ++u)
-            {
-                const int j = j0 + u * QUANT_THREADS;
-                if (j - (int)(threadIdx.x & 31) >= limit) break;  // whole warp past the row end
-                const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
-                uint32_t am = amax_bits8(w);
-                am = max(am, __shfl_xor_sync(0xffffffffu, am, 1));
-                am = max(am, __shfl_xor_sync(0xffffffffu, am, 2));
-                if (j >= oct) continue;
-                const uint32_t s = scale_from_amax_bits(am);
-                const bool nan_block = s == 0xFFu;
-                const float inv = __uint_as_float((254u - (nan_block ? 254u : s)) << 23);
-                qr[j] = encode8(w, inv, nan_block);
-                if ((j & 3) == 0)
-                {
-                    const int b = j >> 2;
-                    if (shuffled)
-                        sc[flat_s(r, b, snp)] = (uint8_t)s;
-                    else
-                        sc[(int64_t)r * (K >> 5) + b] = (uint8_t)s;
-                }
-            }
+            load_group<QUANT_UNROLL>(xr, j0, oct, v, true);
+            quantize_group<MBS>(v, j0, oct, limit, m, r, K, qr, sc, shuffled, snp);
         }
     }
 }
@@ -270,12 +396,15 @@ int grid_for(int64_t work, int threads, int num_sms)
 
 using namespace mbs;
 
-extern "C" int mbs_quantize_mxfp4(const void* x_bf16, int rows, int K, int ld_x, uint8_t* fp4_out,
-                                  uint8_t* scale_out, int shuffled, void* stream)
+namespace mbs {
+namespace {
+
+int quantize_1x32(const char* fn, const void* x_bf16, int rows, int K, int ld_x, uint8_t* fp4_out,
+                  uint8_t* scale_out, uint8_t* factors, int shuffled, void* stream)
 {
     clear_error();
     if (!x_bf16 || !fp4_out || !scale_out)
-        return fail(MBS_ERR_INVALID_ARGUMENT, "mbs_quantize_mxfp4: null pointer");
+        return fail(MBS_ERR_INVALID_ARGUMENT, "%s: null pointer", fn);
     if (rows <= 0 || K <= 0) return fail(MBS_ERR_INVALID_ARGUMENT, "rows and K must be positive");
     if (K % 32 != 0) return fail(MBS_ERR_UNSUPPORTED_SHAPE, "K must be a multiple of 32, got %d", K);
     if (ld_x < K) return fail(MBS_ERR_INVALID_ARGUMENT, "ld_x (%d) < K (%d)", ld_x, K);
@@ -288,9 +417,14 @@ extern "C" int mbs_quantize_mxfp4(const void* x_bf16, int rows, int K, int ld_x,
     const int snp = scale_n_pad(K);
     // one CTA per row (grid-stride over rows beyond the cap)
     const int qgrid = rows < dev.num_sms * 64 ? rows : dev.num_sms * 64;
-    quantize_1x32_kernel<<<qgrid, QUANT_THREADS, 0, s>>>(
-        static_cast<const uint16_t*>(x_bf16), rows, K, ld_x, fp4_out, scale_out, shuffled ? 1 : 0,
-        snp);
+    if (factors != nullptr)
+        quantize_1x32_kernel<true><<<qgrid, QUANT_THREADS, 0, s>>>(
+            static_cast<const uint16_t*>(x_bf16), rows, K, ld_x, fp4_out, scale_out, shuffled ? 1 : 0,
+            snp, factors);
+    else
+        quantize_1x32_kernel<false><<<qgrid, QUANT_THREADS, 0, s>>>(
+            static_cast<const uint16_t*>(x_bf16), rows, K, ld_x, fp4_out, scale_out, shuffled ? 1 : 0,
+            snp, nullptr);
     if (shuffled && ((rows % 32) != 0 || (K / 32) != snp))
     {
         const int rpad = round_up(rows, 32);
@@ -299,6 +433,28 @@ extern "C" int mbs_quantize_mxfp4(const void* x_bf16, int rows, int K, int ld_x,
     }
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? MBS_OK : cuda_fail(e, "quantize launch");
+}
+
+}  // namespace
+}  // namespace mbs
+
+extern "C" int mbs_quantize_mxfp4(const void* x_bf16, int rows, int K, int ld_x, uint8_t* fp4_out,
+                                  uint8_t* scale_out, int shuffled, void* stream)
+{
+    return mbs::quantize_1x32("mbs_quantize_mxfp4", x_bf16, rows, K, ld_x, fp4_out, scale_out, nullptr,
+                              shuffled, stream);
+}
+
+extern "C" int mbs_quantize_mxfp4_mbs(const void* x_bf16, int rows, int K, int ld_x, uint8_t* fp4_out,
+                                      uint8_t* scale_out, uint8_t* factor_out, int shuffled, void* stream)
+{
+    if (factor_out == nullptr)
+    {
+        mbs::clear_error();
+        return mbs::fail(MBS_ERR_INVALID_ARGUMENT, "mbs_quantize_mxfp4_mbs: factor_out is NULL");
+    }
+    return mbs::quantize_1x32("mbs_quantize_mxfp4_mbs", x_bf16, rows, K, ld_x, fp4_out, scale_out,
+                              factor_out, shuffled, stream);
 }
 
 extern "C" int mbs_quantize_mxfp4_macro(const void* x_bf16, int rows, int K, int ld_x,

@@ -14,7 +14,7 @@ import torch
 from . import _lib
 from .mbs_gemm_a4w4 import _round_up, scale_n_pad
 
-__all__ = ["quantize_mxfp4", "quantize_mxfp4_macro", "shuffle_weight", "shuffle_scales",
+__all__ = ["quantize_mxfp4", "quantize_mxfp4_mbs", "quantize_mxfp4_macro", "shuffle_weight", "shuffle_scales",
            "macro_scale_ld", "quant_gemm_a4w4"]
 
 
@@ -53,6 +53,26 @@ def quantize_mxfp4(x: torch.Tensor, shuffle: bool = False):
         _lib.call("mbs_quantize_mxfp4", x.data_ptr(), R, K, int(x.stride(0)), q.data_ptr(),
                   s.data_ptr(), 1 if shuffle else 0, _stream(x.device))
     return q, s
+
+
+def quantize_mxfp4_mbs(x: torch.Tensor, shuffle: bool = False):
+    """bf16 [R, K] -> (fp4x2 [R, K/2], e8m0 scales, MBS factor bytes [R]).
+
+    Each row is quantised as x * (1 + b/256) with b its MBS factor (the top 8
+    mantissa bits of 6 / max|row|); pass the factors to gemm_a4w4 as A_factor
+    (activations) or B_factor (weight rows) to undo the scaling.  Scales as in
+    quantize_mxfp4."""
+    x, R, K = _check_x(x)
+    q = torch.empty((R, K // 2), dtype=torch.uint8, device=x.device)
+    if shuffle:
+        s = torch.empty((_round_up(R, 32), scale_n_pad(K)), dtype=torch.uint8, device=x.device)
+    else:
+        s = torch.empty((R, K // 32), dtype=torch.uint8, device=x.device)
+    f = torch.empty((R,), dtype=torch.uint8, device=x.device)
+    with torch.cuda.device(x.device):
+        _lib.call("mbs_quantize_mxfp4_mbs", x.data_ptr(), R, K, int(x.stride(0)), q.data_ptr(),
+                  s.data_ptr(), f.data_ptr(), 1 if shuffle else 0, _stream(x.device))
+    return q, s, f
 
 
 def quantize_mxfp4_macro(x: torch.Tensor):

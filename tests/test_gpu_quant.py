@@ -134,3 +134,61 @@ def test_quantize_rejects_bad_k():
     import mbs_b200
     with pytest.raises(RuntimeError, match="multiple of 32"):
         mbs_b200.quantize_mxfp4(torch.zeros(4, 48, dtype=torch.bfloat16, device="cuda"))
+
+
+@pytest.mark.parametrize("R,K", [(1, 32), (33, 96), (300, 2080), (64, 8192), (5, 16384)])
+@pytest.mark.parametrize("shuffle", [False, True])
+def test_quantize_mbs_bit_exact(R, K, shuffle):
+    """Fused MBS factor producer + quantiser against the oracle: codes, scales
+    and factor bytes, including zero / subnormal / Inf / NaN / huge rows."""
+    import mbs_b200
+    x = seeded_bf16(R, K, seed=R * 7 + K)
+    x = x * torch.exp2(torch.randint(-30, 30, (R, 1))).to(torch.bfloat16)
+    if R >= 7:
+        x[:7] = _special_rows(K)
+    q, s, f = mbs_b200.quantize_mxfp4_mbs(x.cuda(), shuffle=shuffle)
+    torch.cuda.synchronize()
+    q_ref, s_ref, f_ref = O.quantize_mxfp4_mbs(bf16_bits(x))
+    assert np.array_equal(f.cpu().numpy(), f_ref)
+    assert np.array_equal(q.cpu().numpy(), q_ref)
+    if shuffle:
+        assert np.array_equal(s.cpu().numpy(), O.shuffle_scales(s_ref, K))
+    else:
+        assert np.array_equal(s.cpu().numpy(), s_ref)
+
+
+def test_quantize_mbs_every_bf16_pattern():
+    import mbs_b200
+    bits = np.arange(65536, dtype=np.uint32).astype(np.uint16).reshape(64, 1024)
+    q, s, f = mbs_b200.quantize_mxfp4_mbs(_from_bits(bits).cuda())
+    torch.cuda.synchronize()
+    q_ref, s_ref, f_ref = O.quantize_mxfp4_mbs(bits)
+    assert np.array_equal(f.cpu().numpy(), f_ref)
+    assert np.array_equal(q.cpu().numpy(), q_ref)
+    assert np.array_equal(s.cpu().numpy(), s_ref)
+
+
+def test_mbs_end_to_end_gemm():
+    """MBS-quantised activations and weights through the GEMM with their factor
+    bytes: matches the oracle GEMM on the same bytes, and the factors undo
+    the row scaling (close to the bf16 product)."""
+    import mbs_b200
+    from tests.gpu_helpers import assert_gemm_close
+    M, N, K = 96, 512, 1024
+    g = torch.Generator().manual_seed(21)
+    xa = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    xw = (torch.randn(N, K, generator=g) * 0.02).to(torch.bfloat16)
+    qa, sa_sh, fa = mbs_b200.quantize_mxfp4_mbs(xa.cuda(), shuffle=True)
+    qw, sw, fw = mbs_b200.quantize_mxfp4_mbs(xw.cuda(), shuffle=False)
+    B = mbs_b200.shuffle_weight(qw)
+    Bs = mbs_b200.shuffle_scales(sw, K)
+    out = mbs_b200.gemm_a4w4(qa, B, sa_sh, Bs, fa, fw)
+    torch.cuda.synchronize()
+    qa_r, sa_r, fa_r = O.quantize_mxfp4_mbs(bf16_bits(xa))
+    qw_r, sw_r, fw_r = O.quantize_mxfp4_mbs(bf16_bits(xw))
+    ref = O.gemm_ref(qa_r, qw_r, sa_r, sw_r, fa_r, fw_r)
+    bound = O.gemm_abs_bound(qa_r, qw_r, sa_r, sw_r)
+    assert_gemm_close(out, ref, bound, "mbs gemm")
+    exact = xa.float() @ xw.float().T
+    rel = (out.float().cpu() - exact).abs().mean() / exact.abs().mean()
+    assert rel < 0.2

@@ -174,3 +174,68 @@ def test_check_gemm_detects_single_block_error():
     bad = O.gemm_ref(qa, qw, sa, sw_bad)
     ok, _, nbad = O.check_gemm(bad, ref, bound)
     assert not ok and nbad >= M // 2
+
+
+def test_mbs_factor_known_values():
+    """6.0 / max: max 1 -> 6 = 1.5 * 4 -> b = 128; max 6 or 3 -> mantissa 0;
+    max 5 -> 1.2 -> b = floor(0.2 * 256) = 51 (bits truncated); zero, Inf and
+    NaN rows -> 0."""
+    rows = np.zeros((7, 32), np.float32)
+    rows[0, 3] = -1.0
+    rows[1, 0] = 6.0
+    rows[2, 9] = 3.0
+    rows[3, 1] = 5.0
+    rows[5, 2] = np.inf
+    rows[6, 2] = np.nan
+    b = O.mbs_row_factor(rows)
+    assert b.tolist() == [128, 0, 0, 51, 0, 0, 0]
+    assert O.mbs_multiplier(np.array([51], np.uint8))[0] == np.float32(1.0 + 51 / 256)
+    # the factor table is the inverse of the multiplier, exactly as the reference defines it
+    assert np.all(O.byte_to_factor(np.arange(256)) ==
+                  (np.float32(1.0) / O.mbs_multiplier(np.arange(256))).astype(np.float32))
+
+
+def test_mbs_scaled_row_max_lands_just_below_six():
+    """After the multiplier the row max is 6 * 2^k * (1 - e) with 0 <= e < 2^-8
+    (truncated mantissa), so the largest code of the row is 6 or 4, never the
+    saturated spill of a max in (6, 8)."""
+    rng = np.random.default_rng(11)
+    x = (rng.standard_normal((64, 256)) * np.exp2(rng.integers(-20, 20, (64, 1)))).astype(np.float32)
+    xb = O.f32_to_bf16_bits(x)
+    xf = O.bf16_bits_to_f32(xb)
+    b = O.mbs_row_factor(xf)
+    scaled = np.max(np.abs(xf), axis=1) * O.mbs_multiplier(b)
+    mant = scaled / np.exp2(np.floor(np.log2(scaled)))      # in [1, 2)
+    assert np.all((mant <= 1.5) & (mant > 1.5 * (1 - 2.0 ** -7)))
+
+
+def test_mbs_quantiser_roundtrip_and_gemm_identity():
+    """dequant(q) * f(b) reconstructs x within the MXFP4 error, and the GEMM
+    oracle with the factors approximates the bf16 product at least as well as
+    plain per-1x32 quantisation on average."""
+    rng = np.random.default_rng(12)
+    M, N, K = 32, 48, 512
+    xa = O.f32_to_bf16_bits(rng.standard_normal((M, K)).astype(np.float32))
+    xw = O.f32_to_bf16_bits((rng.standard_normal((N, K)) * 0.02).astype(np.float32))
+    qa, sa, fa = O.quantize_mxfp4_mbs(xa)
+    qw, sw, fw = O.quantize_mxfp4_mbs(xw)
+    rec = O.dequant(qa, sa) * O.byte_to_factor(fa)[:, None]
+    xf = O.bf16_bits_to_f32(xa)
+    blk_max = np.repeat(np.max(np.abs(xf.reshape(M, K // 32, 32)), axis=-1), 32, axis=1)
+    assert np.all(np.abs(rec - xf) <= 0.25 * blk_max + 1e-30)
+    exact = xf @ O.bf16_bits_to_f32(xw).T
+    mbs = O.gemm_f32(qa, qw, sa, sw, fa, fw)
+    pa, psa = O.quantize_mxfp4(xa)
+    pw, psw = O.quantize_mxfp4(xw)
+    plain = O.gemm_f32(pa, pw, psa, psw)
+    assert np.mean(np.abs(mbs - exact)) <= np.mean(np.abs(plain - exact)) * 1.05
+
+
+def test_mbs_factor_zero_when_scaling_would_overflow():
+    big = np.full((2, 32), 3.0e38, np.float32)
+    big[1] = 1.0e38
+    b = O.mbs_row_factor(big)
+    assert b[0] == 0 and b[1] != 0
+    assert np.isfinite(1.0e38 * O.mbs_multiplier(b[1:]))
+    q, s, f = O.quantize_mxfp4_mbs(O.f32_to_bf16_bits(big))
+    assert np.all(s != 0xFF)
