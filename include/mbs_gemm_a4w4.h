@@ -103,6 +103,21 @@ int mbs_gemm_a4w4_launch_ws(const uint8_t* A, const uint8_t* B, const uint8_t* A
                             void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * As mbs_gemm_a4w4_launch_ws, with an output epilogue:
+ *   out[m][n] = bf16_rne( (acc[m][n] * (f(Af[m]) * f(Bf[n]))) * alpha + bias[n] )
+ * each step an fp32 operation rounded to nearest (alpha = 1 and bias = NULL
+ * give exactly the plain operator's result).  bias is bf16 [N] or NULL.
+ * workspace may be NULL (then the library's own per-(device, stream)
+ * workspace is used, as in gemm_a4w4_mxfp4_launch).  The alpha scale is the
+ * output scaling of the reference's assembly kernel (asm_vs_wg_kernel.md:
+ * 85-87); the bias has no reference counterpart.
+ */
+int mbs_gemm_a4w4_launch_ex(const uint8_t* A, const uint8_t* B, const uint8_t* AScale,
+                            const uint8_t* BScale, const uint8_t* AFactor, const uint8_t* BFactor,
+                            void* out, int M, int N, int K, int Mpad, int scaleN_pad, float alpha,
+                            const void* bias, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * Macro-block-scaling variant: B's e8m0 scales are shared by 32-row x 32-K
  * blocks and given plainly as BScaleMacro[ceil(N/32)][mb_ld] with
  * mb_ld = roundup(K/32, 16).  A and A_scale are as above.  Spec-defined

@@ -75,6 +75,8 @@ struct Params
     unsigned* err;         // sticky device error word
     const uint8_t* packed_b;  // packed weights (C_PACKED configurations)
     int act_rows;          // rows per activation TMA box (the activation operand's tile rows, or M)
+    float alpha;                  // output scale (1 = none)
+    const __nv_bfloat16* bias;    // [N] added to every output row, or null
 };
 
 constexpr int align_up(int x, int a) { return (x + a - 1) / a * a; }
@@ -135,7 +137,7 @@ struct Cfg
 
     // barriers: full, sfready, empty [STAGES]; acc_full, acc_empty [2]; tmem slot; abort
     static constexpr int BAR_BYTES = (3 * STAGES + 4) * 8 + 16;
-    static constexpr int EPI_BYTES = (BM + BN) * 4;  // epilogue factor staging
+    static constexpr int EPI_BYTES = (BM + 2 * BN) * 4;  // epilogue factor + bias staging
     static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + EPI_BYTES + 1024;  // +1024 alignment slack
     static_assert(SMEM_BYTES <= 232448, "shared memory budget");
     static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN");
@@ -614,13 +616,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         // an owner sums its contributors' partials in the idle pipeline stages when they fit
         constexpr bool STAGE_PARTIALS = PR * BN * 4 <= STAGES * CF::STAGE_BYTES;
         const bool has_factor = (p.a_factor != nullptr) || (p.b_factor != nullptr);
+        const bool has_alpha = p.alpha != 1.0f;
+        const bool has_bias = p.bias != nullptr;
         // R rows are activations (non-swap) or weights (swap); C columns the other.
         const uint8_t* r_factor = CF::SWAP ? p.b_factor : p.a_factor;
         const uint8_t* c_factor = CF::SWAP ? p.a_factor : p.b_factor;
         const int r_extent = CF::SWAP ? p.N : p.M;
         const int c_extent = CF::SWAP ? p.M : p.N;
-        float* fr_s = epi_f;       // [BM] row factors of the current tile
-        float* fc_s = epi_f + BM;  // [BN] column factors
+        float* fr_s = epi_f;            // [BM] row factors of the current tile
+        float* fc_s = epi_f + BM;       // [BN] column factors
+        float* bias_s = epi_f + BM + BN;  // [BN] column bias (non-swapped)
         int acc = 0;
         uint32_t acc_phase = 0;
         Work w;
@@ -630,7 +635,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             const int r0 = tr * BM, c0 = tc * BN;
             const bool nonowner = p.sk && w.k0 > 0;
             const bool owner = p.sk && w.k0 == 0 && w.k1 < p.k_stages;
-            if (has_factor && !nonowner)
+            if ((has_factor || (has_bias && !CF::SWAP)) && !nonowner)
             {
                 named_bar_sync(1, NUM_EPI_THREADS);  // previous tile's readers are done
                 if (et < BM)
@@ -642,6 +647,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 {
                     const int c = c0 + et;
                     fc_s[et] = (c_factor != nullptr && c < c_extent) ? byte_to_factor(c_factor[c]) : 1.0f;
+                    if (!CF::SWAP)
+                        bias_s[et] = (has_bias && c < c_extent) ? __bfloat162float(p.bias[c]) : 0.0f;
                 }
                 named_bar_sync(1, NUM_EPI_THREADS);
             }
@@ -765,6 +772,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 }
                 uint32_t packed[COLS / 2];
                 const float fr = has_factor ? fr_s[row] : 1.0f;
+                // swapped: the bias runs along the R rows (output columns n = r0 + row)
+                const float brow = (CF::SWAP && has_bias && row_valid) ? __bfloat162float(p.bias[r0 + row]) : 0.0f;
 #pragma unroll
                 for (int b0 = 0; b0 < NCH; b0 += BATCH)
                 {
@@ -800,6 +809,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         {
 #pragma unroll
                             for (int t = 0; t < 16; ++t) x[t] = __fmul_rn(x[t], __fmul_rn(fr, fc_s[cb + t]));
+                        }
+                        if (has_alpha)
+                        {
+#pragma unroll
+                            for (int t = 0; t < 16; ++t) x[t] = __fmul_rn(x[t], p.alpha);
+                        }
+                        if (has_bias)
+                        {
+#pragma unroll
+                            for (int t = 0; t < 16; ++t) x[t] = __fadd_rn(x[t], CF::SWAP ? brow : bias_s[cb + t]);
                         }
 #pragma unroll
                         for (int t = 0; t < 8; ++t)
@@ -1086,7 +1105,7 @@ struct CfgPair
     static_assert(SF_BASE + STAGES * SF_STAGE_COLS <= 512, "TMEM budget");
     // full, sfready, empty [STAGES]; acc_full, acc_empty; tmem slot; abort
     static constexpr int BAR_BYTES = (3 * STAGES + 2) * 8 + 16;
-    static constexpr int EPI_BYTES = (BM + BN) * 4;
+    static constexpr int EPI_BYTES = (BM + 2 * BN) * 4;  // factor + bias staging
     static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + EPI_BYTES + 1024;
     static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 };
@@ -1343,16 +1362,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) __cluster_dims__(2, 1, 1)
         constexpr int NCH = COLS / 16;
         constexpr int BATCH = 4;
         const bool has_factor = (p.a_factor != nullptr) || (p.b_factor != nullptr);
+        const bool has_alpha = p.alpha != 1.0f;
+        const bool has_bias = p.bias != nullptr;
         const uint32_t acc_empty0 = mapa_shared(smem_u32(acc_empty), 0);
         float* fr_s = epi_f;
         float* fc_s = epi_f + BM;
+        float* bias_s = epi_f + BM + BN;
         uint32_t acc_phase = 0;
         for (int t = cluster; t < ntiles; t += nclusters)
         {
             const int tr = t % tiles_r2, tc = t / tiles_r2;
             const int r0 = tr * 2 * BM + (int)rank * BM;
             const int c0 = tc * BN;
-            if (has_factor)
+            if (has_factor || has_bias)
             {
                 named_bar_sync(1, NUM_EPI_THREADS);
                 if (et < BM)
@@ -1364,6 +1386,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) __cluster_dims__(2, 1, 1)
                 {
                     const int c = c0 + et;
                     fc_s[et] = (p.b_factor != nullptr && c < p.N) ? byte_to_factor(p.b_factor[c]) : 1.0f;
+                    bias_s[et] = (has_bias && c < p.N) ? __bfloat162float(p.bias[c]) : 0.0f;
                 }
                 named_bar_sync(1, NUM_EPI_THREADS);
             }
@@ -1373,6 +1396,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) __cluster_dims__(2, 1, 1)
                 ok_acc = mbar_wait(acc_full, acc_phase, abort_flag);
                 MBS_TADD(tacc, 6);
             }
+            // all epilogue warps take the same branch, so none is left behind in a named barrier
+            ok_acc = named_bar_and(1, NUM_EPI_THREADS, ok_acc);
             if (!ok_acc)
             {
                 if (lane == 0) raise_error(p, abort_flag);
@@ -1401,6 +1426,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) __cluster_dims__(2, 1, 1)
                     {
 #pragma unroll
                         for (int u = 0; u < 16; ++u) x[u] = __fmul_rn(x[u], __fmul_rn(fr, fc_s[cb + u]));
+                    }
+                    if (has_alpha)
+                    {
+#pragma unroll
+                        for (int u = 0; u < 16; ++u) x[u] = __fmul_rn(x[u], p.alpha);
+                    }
+                    if (has_bias)
+                    {
+#pragma unroll
+                        for (int u = 0; u < 16; ++u) x[u] = __fadd_rn(x[u], bias_s[cb + u]);
                     }
 #pragma unroll
                     for (int u = 0; u < 8; ++u)
@@ -1472,6 +1507,8 @@ struct Problem
     int M, N, K, Mpad, snp, mb_ld;
     bool macro;
     bool packed = false;  // B is in the packed format (BS unused)
+    float alpha = 1.0f;   // output scale
+    const void* bias = nullptr;  // bf16 [N] or null
 };
 
 struct Plan
@@ -1777,6 +1814,8 @@ int launch_pair(const Problem& pb, const Plan& pl, const DeviceInfo& dev, void* 
     p.a_factor = pb.AF;
     p.b_factor = pb.BF;
     p.out = static_cast<__nv_bfloat16*>(pb.out);
+    p.alpha = pb.alpha;
+    p.bias = static_cast<const __nv_bfloat16*>(pb.bias);
     p.err = device_error_word(dev.device);
     if (p.err == nullptr) return fail(MBS_ERR_CUDA, "device error word unavailable");
     cudaLaunchConfig_t cfg = {};
@@ -1825,6 +1864,8 @@ int launch_cfg(const Problem& pb, const Plan& pl, const DeviceInfo& dev, void* w
     p.a_factor = pb.AF;
     p.b_factor = pb.BF;
     p.out = static_cast<__nv_bfloat16*>(pb.out);
+    p.alpha = pb.alpha;
+    p.bias = static_cast<const __nv_bfloat16*>(pb.bias);
     if (pl.sk)
     {
         p.flags = static_cast<unsigned*>(ws);
@@ -2033,6 +2074,20 @@ extern "C" int mbs_gemm_a4w4_launch_ws(const uint8_t* A, const uint8_t* B, const
     mbs::clear_error();
     Problem pb{A, B, AScale, BScale, AFactor, BFactor, out, M, N, K, Mpad, scaleN_pad, 0, false};
     return mbs::gemm::run(pb, workspace, workspace_bytes, false, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int mbs_gemm_a4w4_launch_ex(const uint8_t* A, const uint8_t* B, const uint8_t* AScale,
+                                       const uint8_t* BScale, const uint8_t* AFactor,
+                                       const uint8_t* BFactor, void* out, int M, int N, int K,
+                                       int Mpad, int scaleN_pad, float alpha, const void* bias,
+                                       void* workspace, size_t workspace_bytes, void* stream)
+{
+    mbs::clear_error();
+    Problem pb{A, B, AScale, BScale, AFactor, BFactor, out, M, N, K, Mpad, scaleN_pad, 0, false};
+    pb.alpha = alpha;
+    pb.bias = bias;
+    return mbs::gemm::run(pb, workspace, workspace_bytes, workspace == nullptr,
+                          reinterpret_cast<cudaStream_t>(stream));
 }
 
 extern "C" size_t mbs_packed_weight_bytes(int N, int K)

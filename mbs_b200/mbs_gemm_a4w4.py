@@ -132,14 +132,20 @@ def _ptr(t):
 
 def gemm_a4w4(A: torch.Tensor, B: torch.Tensor, A_scale: torch.Tensor, B_scale: torch.Tensor,
               A_factor: torch.Tensor | None = None, B_factor: torch.Tensor | None = None,
-              out: torch.Tensor | None = None) -> torch.Tensor:
+              out: torch.Tensor | None = None, alpha: float = 1.0,
+              bias: torch.Tensor | None = None) -> torch.Tensor:
     """out[M, N] bf16 = dequant(A) @ dequant(B)^T * f(A_factor) * f(B_factor)^T.
 
     A: [M, K/2] fp4x2 plain; B: [N, K/2] fp4x2 preshuffled (16x16);
     A_scale / B_scale: e8m0 in the shuffled layout (>= Mpad*scaleN_pad and
     roundup(N,32)*scaleN_pad bytes); factors: uint8 [M] / [N] or None,
     f(b) = 1 / (1 + b/256).  (interface/gemm_a4w4_pybind.cpp:7-18)
+    Extensions (keyword only in spirit; defaults leave the result unchanged):
+    `alpha` scales the fp32 result and `bias` (bf16 [N]) is added to every
+    row before the bf16 rounding.
     """
+    if alpha != 1.0 or bias is not None:
+        return _gemm_ex(A, B, A_scale, B_scale, A_factor, B_factor, out, float(alpha), bias)
     Au, Bu, Asc, Bsc, Afc, Bfc, M, N, K = _check_inputs(A, B, A_scale, B_scale, A_factor, B_factor)
     Mpad = _round_up(M, 32)
     snp = scale_n_pad(K)
@@ -155,6 +161,29 @@ def gemm_a4w4(A: torch.Tensor, B: torch.Tensor, A_scale: torch.Tensor, B_scale: 
         stream = torch.cuda.current_stream(A.device).cuda_stream
         _lib.call("mbs_gemm_a4w4_launch_ws", _ptr(Au), _ptr(Bu), _ptr(Asc), _ptr(Bsc), _ptr(Afc),
                   _ptr(Bfc), o.data_ptr(), M, N, K, Mpad, snp, _ptr(ws),
+                  0 if ws is None else ws.numel(), stream)
+    return o.narrow(0, 0, M)
+
+
+def _gemm_ex(A, B, A_scale, B_scale, A_factor, B_factor, out, alpha, bias):
+    Au, Bu, Asc, Bsc, Afc, Bfc, M, N, K = _check_inputs(A, B, A_scale, B_scale, A_factor, B_factor)
+    Mpad = _round_up(M, 32)
+    snp = scale_n_pad(K)
+    if Asc.numel() < Mpad * snp or Bsc.numel() < _round_up(N, 32) * snp:
+        raise RuntimeError("gemm_a4w4: scale buffers too small for the shape")
+    bias_t = None
+    if bias is not None:
+        if not bias.is_cuda or bias.device != A.device:
+            raise RuntimeError("gemm_a4w4: bias must be on A's device")
+        if bias.dtype != torch.bfloat16 or bias.numel() != N:
+            raise RuntimeError(f"gemm_a4w4: bias must be bf16 with N = {N} elements")
+        bias_t = bias.contiguous()
+    o = _out_buffer(out, Mpad, M, N, A.device)
+    with torch.cuda.device(A.device):
+        ws = workspace_for(M, N, K, A.device)
+        stream = torch.cuda.current_stream(A.device).cuda_stream
+        _lib.call("mbs_gemm_a4w4_launch_ex", _ptr(Au), _ptr(Bu), _ptr(Asc), _ptr(Bsc), _ptr(Afc),
+                  _ptr(Bfc), o.data_ptr(), M, N, K, Mpad, snp, alpha, _ptr(bias_t), _ptr(ws),
                   0 if ws is None else ws.numel(), stream)
     return o.narrow(0, 0, M)
 
