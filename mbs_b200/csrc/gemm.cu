@@ -1565,9 +1565,10 @@ size_t sk_partial_bytes(const Plan& pl);
 constexpr size_t kFlagBytes = MBS_GEMM_WS_FLAG_BYTES;
 constexpr int kMaxGrid = (int)(kFlagBytes / sizeof(unsigned));
 
-// Path and schedule choice.  Skinny M (decode) swaps the operands so the
-// weights fill the 128-row MMA dimension; small tile counts use stream-K so
-// every SM streams an equal share of the K work.
+// Path and schedule choice.  Skinny M (decode) loads only its 32 or 64
+// activation rows per stage and uses stream-K so every SM streams an equal
+// share of the weights; larger M runs data-parallel tiles (stream-K only for
+// a very deep K over few tiles).
 //   MBS_FORCE_SCHEDULE=1 (stream-K) / 2 (data-parallel), MBS_FORCE_GRID=<G>:
 //   debug overrides used by the tests to reach every schedule on small shapes.
 Plan make_plan(int M, int N, int K, int num_sms, bool packed = false)
@@ -1593,7 +1594,13 @@ Plan make_plan(int M, int N, int K, int num_sms, bool packed = false)
         pl.tiles_c = (N + pl.bn - 1) / pl.bn;
     }
     const long long tiles = (long long)pl.tiles_r * pl.tiles_c;
-    pl.sk = pl.swap || pl.r_rows < 128 || tiles < 2LL * num_sms;
+    // Stream-K where its partial tiles are small (skinny activations: 32- or
+    // 64-row partials, an HBM-bound stream) or where a data-parallel tile
+    // would run a very deep K alone on a mostly idle GPU.  With 128-row
+    // tiles every contributor moves a 128 KB fp32 partial, which measured
+    // 10-30 % slower than data-parallel tiles at M in 128..2048 even when
+    // those leave SMs idle.
+    pl.sk = pl.swap || pl.r_rows < 128 || (tiles * 4 <= num_sms && pl.k_stages >= 64);
     const int force = env_int("MBS_FORCE_SCHEDULE", 0);
     if (force == 1) pl.sk = true;
     if (force == 2) pl.sk = false;
@@ -1601,14 +1608,26 @@ Plan make_plan(int M, int N, int K, int num_sms, bool packed = false)
     const int fg = env_int("MBS_FORCE_GRID", 0);
     if (fg > 0 && fg < G) G = fg;
     const long long units = pl.sk ? tiles * pl.k_stages : tiles;
+    // Stream-K ranges of at least 8 K-stages (16 for 128-row partials) per
+    // CTA: with shorter ones the partial traffic of the many contributors to
+    // each tile outweighs the extra SMs (full decode shapes keep every SM).
+    if (pl.sk && !pl.swap && fg == 0)
+    {
+        const long long per = units / (pl.r_rows == 128 ? 16 : 8);
+        const long long cap = per > tiles ? per : tiles;
+        if (cap < G) G = (int)cap;
+    }
     pl.G = (int)(units < G ? units : G);
     pl.ws_bytes = pl.sk ? kFlagBytes + sk_partial_bytes(pl) : 0;
-    // Large data-parallel problems run on CTA pairs (256 x 256 tiles); their
-    // workspace holds the scale images.
-    pl.pair = !packed && !pl.swap && !pl.sk && env_int("MBS_FORCE_PAIR", 1) != 0;
+    // Data-parallel problems with at least 4 pair tiles run on CTA pairs
+    // (256 x 256 tiles; their workspace holds the scale images); below that
+    // the scale-image pre-pass (a second launch) costs more than the pair
+    // saves.
+    const long long t2 = (long long)((M + 2 * BM - 1) / (2 * BM)) * ((N + 255) / 256);
+    const int force_pair = env_int("MBS_FORCE_PAIR", -1);
+    pl.pair = !packed && !pl.swap && !pl.sk && force_pair != 0 && (t2 >= 4 || force_pair == 1);
     if (pl.pair)
     {
-        const long long t2 = (long long)((M + 2 * BM - 1) / (2 * BM)) * ((N + 255) / 256);
         const int c = G / 2;
         pl.G = 2 * (int)(t2 < c ? t2 : c);
         pl.ws_bytes = kFlagBytes + pair_image_a_bytes(M, K) + pair_image_b_bytes(N, K);

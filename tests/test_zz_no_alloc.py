@@ -61,10 +61,18 @@ def test_noalloc_matches_workspace_entry_point(M, N, K):
 def test_noalloc_rejects_shapes_beyond_its_scratch():
     from mbs_b200 import _lib
     L = _lib.lib()
-    # 1024x4096x1024: 128 tiles of 128x256 -> stream-K on 148 CTAs with
-    # 148 x 128 KB of partials, more than the 8 MiB static buffer
-    c = Case(1024, 4096, 1024, seed=5, factors=True)
-    out = torch.empty((1024, 4096), dtype=torch.bfloat16, device="cuda")
-    st = L.mbs_gemm_a4w4_launch_noalloc(*_args(c, out), _stream())
+    # 64x57344x1024: skinny stream-K on every SM with 64-row partials,
+    # 148 x 64 KB, more than the 8 MiB static buffer.  The entry point refuses
+    # before reading any operand, so zero-filled buffers of the right sizes do.
+    M, N, K = 64, 57344, 1024
+    assert L.mbs_gemm_a4w4_workspace_size(M, N, K) > 8 << 20
+    snp = O.scale_n_pad(K)
+    A = torch.zeros((M, K // 2), dtype=torch.uint8, device="cuda")
+    B = torch.zeros((N, K // 2), dtype=torch.uint8, device="cuda")
+    As = torch.zeros((M * snp,), dtype=torch.uint8, device="cuda")
+    Bs = torch.zeros((N * snp,), dtype=torch.uint8, device="cuda")
+    out = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
+    st = L.mbs_gemm_a4w4_launch_noalloc(A.data_ptr(), B.data_ptr(), As.data_ptr(), Bs.data_ptr(), None,
+                                        None, out.data_ptr(), M, N, K, M, snp, _stream())
     assert st == 5  # MBS_ERR_WORKSPACE
     assert b"static buffer" in L.mbs_last_error_message()
