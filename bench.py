@@ -51,6 +51,14 @@ def parse():
     ap.add_argument("--workload", choices=["prefill", "decode", "sharded"], default="prefill")
     ap.add_argument("--m", type=int, default=None, help="M for --workload decode (default 16)")
     ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--chunks", type=int, default=None,
+                    help="--workload sharded: row chunks whose exchange overlaps the next chunk's GEMM "
+                         "(default 4 on more than one GPU, 1 on one)")
+    ap.add_argument("--exchange", choices=["nccl", "copy"], default="copy",
+                    help="--workload sharded: exchange the C shards with NCCL or with copy engines "
+                         "through peer memory")
+    ap.add_argument("--comm-sms", type=int, default=16,
+                    help="--workload sharded with chunks > 1: SMs left free for the NCCL kernels")
     ap.add_argument("--skip-extras", action="store_true",
                     help="skip the e2e and CPU-baseline legs (profiling runs)")
     ap.add_argument("--soak-s", type=float, default=1.5,
@@ -436,25 +444,28 @@ def run_sharded(args):
             os.environ.setdefault("MASTER_PORT", "29533")
             _d.init_process_group("nccl", rank=0, world_size=1, device_id=dev)
     layer = ShardedA4W4(B, Bs, N, K)
+    chunks = args.chunks if args.chunks is not None else (4 if world > 1 else 1)
     stream = torch.cuda.current_stream(dev)
-    for _ in range(max(args.warmup, 3)):
-        layer(x)
-    torch.cuda.synchronize()
-    dist.barrier()
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
-           torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    for i in range(args.steps):
-        e0, e1, e2 = ev[i]
-        e0.record(stream)
-        c = layer.local(x)
-        e1.record(stream)
-        flat = torch.empty((world * M, nl), dtype=c.dtype, device=dev)
-        dist.all_gather_into_tensor(flat, c)
-        e2.record(stream)
-    torch.cuda.synchronize()
-    dist.barrier()
-    t = torch.tensor([sum(a.elapsed_time(b) for a, b, _ in ev) / args.steps,
-                      sum(a.elapsed_time(c) for a, _, c in ev) / args.steps], device=dev)
+
+    def timed(fn):
+        for _ in range(max(args.warmup, 3)):
+            fn()
+        torch.cuda.synchronize()
+        dist.barrier()
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(args.steps)]
+        for i in range(args.steps):
+            ev[i][0].record(stream)
+            fn()
+            ev[i][1].record(stream)
+        torch.cuda.synchronize()
+        dist.barrier()
+        return sum(a.elapsed_time(b) for a, b in ev) / args.steps
+
+    local_ms = timed(lambda: layer.local(x))           # quantise + GEMM alone
+    total_ms = timed(lambda: layer(x, chunks=chunks, comm_sms=args.comm_sms,
+                                   exchange=args.exchange))  # the whole layer
+    t = torch.tensor([local_ms, total_ms], device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     local_ms, total_ms = float(t[0]), float(t[1])
     flops = 2.0 * M * N * K
@@ -468,9 +479,18 @@ def run_sharded(args):
             "config": {"workload": "cfg4 M=16384 N=57344 K=8192 N-sharded", "parallelism": f"N-shards x{world}"},
             "quant_gemm_ms": round(local_ms, 4),
             "quant_gemm_tflops": round(flops / world / (local_ms * 1e-3) / 1e12 * world, 2),
-            "allgather_ms": round(total_ms - local_ms, 4),
-            "allgather_bytes_received_per_rank": (world - 1) * M * nl * 2,
+            "exposed_exchange_ms": round(total_ms - local_ms, 4),
+            "exchange": ("NCCL all-gather" if chunks == 1 else
+                         f"{chunks} row chunks, NCCL send/recv overlapped with the next chunk's GEMM "
+                         f"({args.comm_sms} SMs left to NCCL)") if args.exchange == "nccl" or world == 1 else
+                        f"{chunks} row chunks pushed into the peers' buffers by copy engines (CUDA IPC), "
+                        f"overlapped with the next chunk's GEMM",
+            "bytes_received_per_rank": (world - 1) * M * nl * 2,
         }), flush=True)
+    torch.cuda.synchronize()
+    dist.barrier()
+    if layer._peerbuf is not None:  # every rank is done with every buffer
+        layer._peerbuf.close()
     dist.barrier()
     dist.destroy_process_group()
 

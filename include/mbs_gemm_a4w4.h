@@ -233,6 +233,33 @@ int mbs_shuffle_scales(const uint8_t* plain, uint8_t* shuffled, int rows, int K,
 int mbs_set_profile_events(void* before_main, void* after_main);
 
 /*
+ * Tuning knob: on this host thread, launch the following GEMMs on at most
+ * max_ctas CTAs (0 = one per SM, the default), leaving SMs free for kernels
+ * that must run at the same time, such as the NCCL kernels of an all-gather
+ * overlapped with the GEMM.  Workspace sizes queried on this thread follow
+ * the same limit.  No reference counterpart.
+ */
+int mbs_set_grid_limit(int max_ctas);
+
+/*
+ * Peer-memory plumbing for exchanging GEMM output shards between the GPUs of
+ * one node (the N-sharded layer) with copy-engine
+ * transfers over NVLink instead of SM kernels:
+ *   mbs_ipc_alloc   cudaMalloc `bytes` on the current device and write its
+ *                   CUDA IPC handle (64 bytes) to handle_out;
+ *   mbs_ipc_open    map a peer's buffer from its handle (peer access enabled);
+ *   mbs_ipc_close / mbs_ipc_free   undo the two;
+ *   mbs_copy_async  one cudaMemcpyAsync of `bytes` between device pointers
+ *                   (local or peer) on `stream`.
+ * No reference counterpart (the reference has no multi-GPU path).
+ */
+int mbs_ipc_alloc(size_t bytes, void** ptr, void* handle_out);
+int mbs_ipc_open(const void* handle, void** peer_ptr);
+int mbs_ipc_close(void* peer_ptr);
+int mbs_ipc_free(void* ptr);
+int mbs_copy_async(void* dst, const void* src, size_t bytes, void* stream);
+
+/*
  * Sticky device-side error word of the current device: 0, or the code of a
  * kernel wait that ran out (MBS_ERR_DEVICE_TIMEOUT).  Synchronises the
  * device.  reset != 0 clears it.  No reference counterpart.

@@ -37,6 +37,12 @@ SIGNATURES = {
     "mbs_shuffle_scales": (_c_int, [_c_void_p, _c_void_p, _c_int, _c_int, _c_void_p]),
     "mbs_device_error": (_c_int, [ctypes.POINTER(_c_int), _c_int]),
     "mbs_set_profile_events": (_c_int, [_c_void_p, _c_void_p]),
+    "mbs_set_grid_limit": (_c_int, [_c_int]),
+    "mbs_ipc_alloc": (_c_int, [_c_size_t, ctypes.POINTER(_c_void_p), _c_void_p]),
+    "mbs_ipc_open": (_c_int, [_c_void_p, ctypes.POINTER(_c_void_p)]),
+    "mbs_ipc_close": (_c_int, [_c_void_p]),
+    "mbs_ipc_free": (_c_int, [_c_void_p]),
+    "mbs_copy_async": (_c_int, [_c_void_p, _c_void_p, _c_size_t, _c_void_p]),
     "mbs_packed_weight_bytes": (_c_size_t, [_c_int, _c_int]),
     "mbs_pack_weight": (_c_int, [_c_void_p, _c_void_p, _c_int, _c_int, _c_int, _c_void_p, _c_void_p]),
     "mbs_gemm_a4w4_packed_workspace_size": (_c_size_t, [_c_int] * 3),

@@ -1524,6 +1524,11 @@ struct Plan
 // stream immediately before and after the main GEMM kernel of the next calls.
 thread_local cudaEvent_t g_ev_before = nullptr, g_ev_after = nullptr;
 
+// Upper bound on the CTAs of the next GEMM launches from this host thread
+// (0 = one per SM): leaves SMs free for kernels that must run alongside, such
+// as the NCCL kernels of an overlapped all-gather.
+thread_local int g_grid_limit = 0;
+
 int record_before(cudaStream_t s)
 {
     if (g_ev_before == nullptr) return MBS_OK;
@@ -1605,6 +1610,7 @@ Plan make_plan(int M, int N, int K, int num_sms, bool packed = false)
     if (force == 1) pl.sk = true;
     if (force == 2) pl.sk = false;
     int G = num_sms < kMaxGrid ? num_sms : kMaxGrid;
+    if (g_grid_limit > 0 && g_grid_limit < G) G = g_grid_limit;
     const int fg = env_int("MBS_FORCE_GRID", 0);
     if (fg > 0 && fg < G) G = fg;
     const long long units = pl.sk ? tiles * pl.k_stages : tiles;
@@ -2047,6 +2053,14 @@ extern "C" int mbs_timing_read(unsigned long long* host, int reset)
     return e == cudaSuccess ? MBS_OK : MBS_ERR_CUDA;
 }
 #endif
+
+extern "C" int mbs_set_grid_limit(int max_ctas)
+{
+    mbs::clear_error();
+    if (max_ctas < 0) return mbs::fail(MBS_ERR_INVALID_ARGUMENT, "mbs_set_grid_limit: max_ctas < 0");
+    mbs::gemm::g_grid_limit = max_ctas;
+    return MBS_OK;
+}
 
 extern "C" int mbs_set_profile_events(void* before_main, void* after_main)
 {

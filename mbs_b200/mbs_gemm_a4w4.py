@@ -16,6 +16,7 @@ Launches go to the current torch CUDA stream of A's device, asynchronously.
 
 from __future__ import annotations
 
+import contextlib
 import ctypes
 import threading
 
@@ -23,7 +24,7 @@ import torch
 
 from . import _lib
 
-__all__ = ["gemm_a4w4", "gemm_a4w4_macro", "workspace_for", "device_error"]
+__all__ = ["gemm_a4w4", "gemm_a4w4_macro", "workspace_for", "device_error", "grid_limit"]
 
 # Workspace layout of include/mbs_gemm_a4w4.h: the first WS_FLAG_BYTES bytes
 # are the stream-K flag words (zero between launches), the rest is scratch.
@@ -45,6 +46,18 @@ def scale_n_pad(K: int) -> int:
 def _bytes(t: torch.Tensor) -> torch.Tensor:
     # .view(kByte).contiguous() as in interface/gemm_a4w4_pybind.cpp:25-30
     return t.view(torch.uint8).contiguous()
+
+
+@contextlib.contextmanager
+def grid_limit(max_ctas: int):
+    """Run the GEMMs launched inside the block (from this thread) on at most
+    `max_ctas` CTAs, leaving the other SMs to concurrent kernels such as an
+    overlapped NCCL all-gather.  0 = no limit."""
+    _lib.call("mbs_set_grid_limit", int(max_ctas))
+    try:
+        yield
+    finally:
+        _lib.call("mbs_set_grid_limit", 0)
 
 
 def cached_workspace(need: int, device: torch.device) -> torch.Tensor | None:

@@ -12,16 +12,36 @@ all-gather (NCCL over NVLink for CUDA tensors).
 The all-gather returns the shards stacked as [world, M, N/world]; `layout=
 "blocked"` hands that back as is (a view per rank is C[:, r*N/w:(r+1)*N/w]),
 `layout="rows"` pays one permute copy for a row-major [M, N].
+
+`exchange="copy"` (CUDA GPUs) moves the rows with copy engines instead:
+every rank maps its peers' output buffers through CUDA IPC and pushes each
+chunk of its block into them with cudaMemcpyAsync on a side stream while
+the next chunk's GEMM runs on all SMs; one-word NCCL all-reduces serve as
+device-side barriers.  With layout="blocked" the result is the layer's
+exchange buffer and stays valid until the next forward call.
+
+`chunks > 1` (with exchange="nccl") pipelines the exchange with the compute: A is processed in
+row chunks, each chunk's GEMM writes straight into this rank's block of the
+output, and its rows are exchanged with every peer by NCCL point-to-point
+sends/receives (straight into the peers' blocks) while the next chunk's
+GEMM runs.  The GEMM then runs on all SMs but `comm_sms`, which the NCCL
+kernels need to run alongside it (the GEMM's CTAs fill an SM each).
 """
 
 from __future__ import annotations
 
+import contextlib
 from typing import Callable, Optional
 
 import torch
 import torch.distributed as dist
 
 SHARD_ALIGN = 256
+
+
+def _lib_call(name, *args):
+    from . import _lib
+    return _lib.call(name, *args)
 
 
 def shard_rows(N: int, world: int, rank: int, align: int = SHARD_ALIGN) -> tuple[int, int]:
@@ -52,7 +72,7 @@ def shard_weight(B_shuffled: torch.Tensor, B_scale_shuffled: torch.Tensor, N: in
 class ShardedA4W4:
     """One rank's part of an N-sharded A4W4 linear layer.
 
-    `local_gemm(A_fp4, B, A_scale_shuffled, B_scale, A_factor, B_factor) -> C`
+    `local_gemm(A_fp4, B, A_scale_shuffled, B_scale, A_factor, B_factor, out=None) -> C`
     and `quantize(x) -> (A_fp4, A_scale_shuffled)` default to the CUDA
     operators of this package; they are parameters so that the collective and
     layout logic can be exercised on CPU process groups in tests.
@@ -69,6 +89,7 @@ class ShardedA4W4:
         if B_shard.shape[0] != self.n1 - self.n0 or B_shard.shape[1] != K // 2:
             raise ValueError(f"B_shard must be [{self.n1 - self.n0}, {K // 2}], got {tuple(B_shard.shape)}")
         self.B, self.B_scale, self.B_factor = B_shard, B_scale_shard, B_factor_shard
+        self._default_gemm = local_gemm is None
         if local_gemm is None or quantize is None:
             from .mbs_gemm_a4w4 import gemm_a4w4
             from .quant import quantize_mxfp4
@@ -76,6 +97,9 @@ class ShardedA4W4:
             quantize = quantize or (lambda x: quantize_mxfp4(x, shuffle=True))
         self._gemm = local_gemm
         self._quant = quantize
+        self._peerbuf = None   # PeerBuffer of the copy exchange, sized on first use
+        self._side = None
+        self._flag = None
 
     def local(self, x: torch.Tensor, A_factor: Optional[torch.Tensor] = None) -> torch.Tensor:
         """bf16 x [M, K] -> this rank's bf16 C columns [M, N/world]."""
@@ -83,7 +107,16 @@ class ShardedA4W4:
         return self._gemm(q, self.B, s, self.B_scale, A_factor, self.B_factor)
 
     def forward(self, x: torch.Tensor, A_factor: Optional[torch.Tensor] = None,
-                layout: str = "blocked") -> torch.Tensor:
+                layout: str = "blocked", chunks: int = 1, comm_sms: int = 16,
+                exchange: str = "nccl") -> torch.Tensor:
+        if layout not in ("blocked", "rows"):
+            raise ValueError(f"layout must be 'blocked' or 'rows', got {layout!r}")
+        if exchange not in ("nccl", "copy"):
+            raise ValueError(f"exchange must be 'nccl' or 'copy', got {exchange!r}")
+        if exchange == "copy" and self.world > 1:
+            return self._forward_copy(x, A_factor, layout, max(1, chunks))
+        if chunks > 1:
+            return self._forward_pipelined(x, A_factor, layout, chunks, comm_sms)
         c = self.local(x, A_factor).contiguous()
         M, nl = c.shape
         flat = torch.empty((self.world * M, nl), dtype=c.dtype, device=c.device)
@@ -94,5 +127,87 @@ class ShardedA4W4:
         if layout == "rows":
             return gathered.permute(1, 0, 2).reshape(M, self.world * nl)
         raise ValueError(f"layout must be 'blocked' or 'rows', got {layout!r}")
+
+    def _global_rank(self, r: int) -> int:
+        return r if self.group is None else dist.get_global_rank(self.group, r)
+
+    def _forward_pipelined(self, x, A_factor, layout, chunks, comm_sms):
+        M = int(x.shape[0])
+        nl = self.n1 - self.n0
+        step = max(32, (-(-M // chunks) + 31) // 32 * 32)  # chunk rows, a multiple of 32
+        out = torch.empty((self.world, M, nl), dtype=torch.bfloat16, device=x.device)
+        limit = contextlib.nullcontext()
+        if x.is_cuda and comm_sms > 0 and self.world > 1 and self._default_gemm:
+            from .mbs_gemm_a4w4 import grid_limit
+            sms = torch.cuda.get_device_properties(x.device).multi_processor_count
+            limit = grid_limit(max(2, sms - comm_sms))
+        works = []
+        with limit:
+            for r0 in range(0, M, step):
+                r1 = min(M, r0 + step)
+                q, s = self._quant(x[r0:r1])
+                fa = None if A_factor is None else A_factor[r0:r1]
+                mine = out[self.rank, r0:r1]
+                self._gemm(q, self.B, s, self.B_scale, fa, self.B_factor, out=mine)
+                ops = []
+                for r in range(self.world):
+                    if r != self.rank:
+                        ops.append(dist.P2POp(dist.isend, mine, self._global_rank(r), group=self.group))
+                        ops.append(dist.P2POp(dist.irecv, out[r, r0:r1], self._global_rank(r), group=self.group))
+                if ops:
+                    works.extend(dist.batch_isend_irecv(ops))
+        for w in works:
+            w.wait()
+        if layout == "blocked":
+            return out
+        return out.permute(1, 0, 2).reshape(M, self.world * nl)
+
+    def _barrier(self):
+        """Device-side barrier on the current stream: a one-word NCCL all-reduce
+        completes on a rank only after every rank's stream has reached it."""
+        if self._flag is None:
+            self._flag = torch.zeros(1, dtype=torch.int32, device=self.B.device)
+        dist.all_reduce(self._flag, group=self.group)
+
+    def _forward_copy(self, x, A_factor, layout, chunks):
+        """Copy-engine exchange: every chunk's rows go straight into each peer's
+        copy of the gathered output (CUDA IPC mapping, cudaMemcpyAsync on a side
+        stream), beside the next chunk's GEMM, which keeps every SM."""
+        from .peer import PeerBuffer
+        M = int(x.shape[0])
+        nl = self.n1 - self.n0
+        nbytes = self.world * M * nl * 2
+        if self._peerbuf is None or self._peerbuf.nbytes < nbytes:
+            if self._peerbuf is not None:
+                torch.cuda.synchronize(x.device)
+                self._barrier()
+                torch.cuda.synchronize(x.device)
+                self._peerbuf.close()
+            self._peerbuf = PeerBuffer(nbytes, x.device, self.group)
+            self._side = torch.cuda.Stream(x.device)
+        out = self._peerbuf.tensor((self.world, M, nl))
+        compute = torch.cuda.current_stream(x.device)
+        # nobody may write into a rank's buffer before that rank is done with the
+        # previous result (anything it queued before this call)
+        self._barrier()
+        step = max(32, (-(-M // chunks) + 31) // 32 * 32)
+        for r0 in range(0, M, step):
+            r1 = min(M, r0 + step)
+            q, s = self._quant(x[r0:r1])
+            fa = None if A_factor is None else A_factor[r0:r1]
+            mine = out[self.rank, r0:r1]
+            self._gemm(q, self.B, s, self.B_scale, fa, self.B_factor, out=mine)
+            self._side.wait_stream(compute)
+            off = (self.rank * M + r0) * nl * 2
+            for r in range(self.world):
+                if r != self.rank:
+                    _lib_call("mbs_copy_async", self._peerbuf.ptrs[r] + off, mine.data_ptr(), (r1 - r0) * nl * 2,
+                              self._side.cuda_stream)
+        with torch.cuda.stream(self._side):
+            self._barrier()  # every rank's copies into every buffer are complete
+        compute.wait_stream(self._side)
+        if layout == "blocked":
+            return out  # the layer's exchange buffer: valid until the next forward call
+        return out.permute(1, 0, 2).reshape(M, self.world * nl)
 
     __call__ = forward

@@ -39,14 +39,25 @@ def main():
         Ssh = torch.from_numpy(O.shuffle_scales(ws, K))
         b, s = shard_weight(Bsh, Ssh, N, K, world, rank)
         layer = ShardedA4W4(b.cuda(), s.cuda(), N, K)
-        out = layer(x.cuda(), layout="rows")
-        torch.cuda.synchronize()
         cols = np.concatenate([np.arange(r * N // world, r * N // world + 64) for r in range(world)])
         ref = O.gemm_ref(xq, wq[cols], xs, ws[cols])
         bound = O.gemm_abs_bound(xq, wq[cols], xs, ws[cols])
-        ok, ratio, nbad = O.check_gemm(out[:, torch.from_numpy(cols).cuda()].float().cpu().numpy(), ref, bound)
-        assert ok, f"rank {rank}: {nbad} bad elements (max ratio {ratio})"
+        # one all-gather, the pipelined point-to-point exchange, and the copy-engine
+        # exchange through peer memory (twice, reusing its buffer)
+        for exchange, chunks in (("nccl", 1), ("nccl", 3), ("copy", 1), ("copy", 3), ("copy", 3)):
+            out = layer(x.cuda(), layout="rows", chunks=chunks, exchange=exchange)
+            torch.cuda.synchronize()
+            got = out[:, torch.from_numpy(cols).cuda()].float().cpu().numpy()
+            ok, ratio, nbad = O.check_gemm(got, ref, bound)
+            assert ok, f"rank {rank} {exchange} chunks {chunks}: {nbad} bad elements (max ratio {ratio})"
+            blocked = layer(x.cuda(), layout="blocked", chunks=chunks, exchange=exchange)
+            torch.cuda.synchronize()
+            assert torch.equal(blocked.permute(1, 0, 2).reshape(M, N), out), f"{exchange} blocked vs rows"
         dist.barrier()
+        if layer._peerbuf is not None:
+            torch.cuda.synchronize()
+            dist.barrier()
+            layer._peerbuf.close()
         print(f"SHARDED_OK rank={rank} world={world}", flush=True)
     finally:
         dist.destroy_process_group()

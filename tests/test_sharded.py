@@ -67,28 +67,42 @@ def _gloo_worker(rank, world, port, M, N, K, q):
 
         # CPU stand-ins for the CUDA operators: the oracle on unshuffled bytes
         def quant(x):
-            return torch.from_numpy(xq), torch.from_numpy(O.shuffle_scales(xs, K))
+            r0 = int(x.data_ptr() - base.data_ptr()) // (x.element_size() * K)  # row offset of the view
+            rows = x.shape[0]
+            return (torch.from_numpy(xq[r0:r0 + rows].copy()),
+                    torch.from_numpy(O.shuffle_scales(xs[r0:r0 + rows], K)))
 
-        def gemm(A, B, As, Bs, Af, Bf):
+        def gemm(A, B, As, Bs, Af, Bf, out=None):
             nl = B.shape[0]
+            rows = A.shape[0]
             bp = O.unshuffle_weight(B.numpy())
             bs = O.unshuffle_scales(Bs.numpy(), nl, K)
-            return torch.from_numpy(O.gemm_ref(A.numpy(), bp, xs, bs)).to(torch.bfloat16)
+            a_s = O.unshuffle_scales(As.numpy(), rows, K)
+            c = torch.from_numpy(O.gemm_ref(A.numpy(), bp, a_s, bs)).to(torch.bfloat16)
+            if out is not None:
+                out.copy_(c)
+                return out
+            return c
 
+        base = torch.zeros(M, K)
         layer = ShardedA4W4(Bsh, Ssh, N, K, local_gemm=gemm, quantize=quant)
-        out_rows = layer(torch.zeros(M, K), layout="rows")
-        out_blocked = layer(torch.zeros(M, K), layout="blocked")
         ref = O.gemm_ref(xq, w, xs, ws)
-        q.put((rank, np.array_equal(out_rows.float().numpy(), ref),
-               tuple(out_blocked.shape),
-               np.array_equal(out_blocked[rank].float().numpy(),
-                              ref[:, rank * N // world:(rank + 1) * N // world])))
+        res = []
+        for chunks in (1, 3):
+            out_rows = layer(base, layout="rows", chunks=chunks)
+            out_blocked = layer(base, layout="blocked", chunks=chunks)
+            res.append((np.array_equal(out_rows.float().numpy(), ref), tuple(out_blocked.shape),
+                        np.array_equal(out_blocked[rank].float().numpy(),
+                                       ref[:, rank * N // world:(rank + 1) * N // world]),
+                        all(np.array_equal(out_blocked[r].float().numpy(),
+                                           ref[:, r * N // world:(r + 1) * N // world]) for r in range(world))))
+        q.put((rank, res))
     finally:
         dist.destroy_process_group()
 
 
 def test_sharded_allgather_on_gloo_world2():
-    M, N, K, world = 8, 512, 128, 2
+    M, N, K, world = 80, 512, 128, 2   # 3 chunks of 32, 32 and 16 rows
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
@@ -99,9 +113,10 @@ def test_sharded_allgather_on_gloo_world2():
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
-    for rank, rows_ok, bshape, block_ok in results:
-        assert rows_ok, f"rank {rank}: row-major gather differs from the oracle"
-        assert bshape == (world, M, N // world) and block_ok
+    for rank, res in results:
+        for chunks, (rows_ok, bshape, block_ok, all_ok) in zip((1, 3), res):
+            assert rows_ok, f"rank {rank} chunks {chunks}: row-major gather differs from the oracle"
+            assert bshape == (world, M, N // world) and block_ok and all_ok, f"rank {rank} chunks {chunks}"
 
 
 @pytest.mark.gpu
