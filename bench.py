@@ -54,9 +54,9 @@ def parse():
     ap.add_argument("--chunks", type=int, default=None,
                     help="--workload sharded: row chunks whose exchange overlaps the next chunk's GEMM "
                          "(default 4 on more than one GPU, 1 on one)")
-    ap.add_argument("--exchange", choices=["nccl", "copy"], default="copy",
-                    help="--workload sharded: exchange the C shards with NCCL or with copy engines "
-                         "through peer memory")
+    ap.add_argument("--exchange", choices=["nccl", "copy", "auto"], default="auto",
+                    help="--workload sharded: exchange the C shards with NCCL, with copy engines "
+                         "through peer memory, or the faster of the two for the GPU count")
     ap.add_argument("--comm-sms", type=int, default=16,
                     help="--workload sharded with chunks > 1: SMs left free for the NCCL kernels")
     ap.add_argument("--skip-extras", action="store_true",
@@ -444,7 +444,10 @@ def run_sharded(args):
             os.environ.setdefault("MASTER_PORT", "29533")
             _d.init_process_group("nccl", rank=0, world_size=1, device_id=dev)
     layer = ShardedA4W4(B, Bs, N, K)
-    chunks = args.chunks if args.chunks is not None else (4 if world > 1 else 1)
+    exchange = args.exchange
+    if exchange == "auto":
+        exchange = "copy" if world == 2 else "nccl"
+    chunks = args.chunks if args.chunks is not None else (4 if exchange == "copy" else 1)
     stream = torch.cuda.current_stream(dev)
 
     def timed(fn):
@@ -464,7 +467,7 @@ def run_sharded(args):
 
     local_ms = timed(lambda: layer.local(x))           # quantise + GEMM alone
     total_ms = timed(lambda: layer(x, chunks=chunks, comm_sms=args.comm_sms,
-                                   exchange=args.exchange))  # the whole layer
+                                   exchange=exchange))  # the whole layer
     t = torch.tensor([local_ms, total_ms], device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     local_ms, total_ms = float(t[0]), float(t[1])
@@ -482,7 +485,7 @@ def run_sharded(args):
             "exposed_exchange_ms": round(total_ms - local_ms, 4),
             "exchange": ("NCCL all-gather" if chunks == 1 else
                          f"{chunks} row chunks, NCCL send/recv overlapped with the next chunk's GEMM "
-                         f"({args.comm_sms} SMs left to NCCL)") if args.exchange == "nccl" or world == 1 else
+                         f"({args.comm_sms} SMs left to NCCL)") if exchange == "nccl" or world == 1 else
                         f"{chunks} row chunks pushed into the peers' buffers by copy engines (CUDA IPC), "
                         f"overlapped with the next chunk's GEMM",
             "bytes_received_per_rank": (world - 1) * M * nl * 2,
