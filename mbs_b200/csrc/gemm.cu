@@ -1011,6 +1011,9 @@ __global__ void __launch_bounds__(256) scale_image_kernel(const uint8_t* __restr
                                                           int b_macro, int mb_ld, uint8_t* __restrict__ img_a,
                                                           uint8_t* __restrict__ img_b)
 {
+    // the GEMM behind this kernel may start now: it loads its first operand
+    // stages and waits for this grid before it reads any image
+    griddep_launch_dependents();
     const long long na = (long long)a_blocks * ks_count * 16;
     const long long nb = (long long)b_tiles * ks_count * 2 * 16;
     for (long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x; t < na + nb;
@@ -1181,13 +1184,34 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) __cluster_dims__(2, 1, 1)
 #if MBS_TIMING
             tacc[12] += (unsigned long long)(clock64() - t_kernel0);  // prologue
 #endif
+            // The scale images are written by the kernel launched just
+            // before this one, which may still be running (programmatic
+            // dependent launch).  The first STAGES stages get their operands
+            // at once and their images after griddep_wait(); every later
+            // stage waits for an MMA that needed those images, so only this
+            // thread has to wait.  `full` is armed for operands and images
+            // together, so it completes only when both have landed.
+            auto load_images = [&](int g) {
+                const int t = cluster + (g / p.k_stages) * nclusters, ks = g % p.k_stages;
+                const int rb = (t % tiles_r2) * 2 + (int)rank, tc = t / tiles_r2;
+                uint8_t* st = smem + (g % STAGES) * CF::STAGE_BYTES;
+                const uint32_t fbar = full0 + (g % STAGES) * 8;
+                tma_load_2d_pair(st + CF::A_IMG_OFF, &tm_ia, fbar, 0, (rb * p.k_stages + ks) * (IMG_A_BYTES / 256));
+                tma_load_2d_pair(st + CF::B_IMG_OFF, &tm_ib, fbar, 0, (tc * p.k_stages + ks) * (IMG_B_BYTES / 256));
+            };
+            int g = 0;  // stage index in this cluster's sequence
             for (int t = cluster; t < ntiles; t += nclusters)
             {
                 const int tr = t % tiles_r2, tc = t / tiles_r2;
                 const int rb = tr * 2 + (int)rank;  // this CTA's 128-row block of A
                 const int nb0 = tc * BN + (int)rank * CF::BNH;
-                for (int ks = 0; ks < p.k_stages; ++ks)
+                for (int ks = 0; ks < p.k_stages; ++ks, ++g)
                 {
+                    if (g == STAGES)
+                    {
+                        griddep_wait();
+                        for (int d = 0; d < STAGES; ++d) load_images(d);
+                    }
                     bool ok_empty;
                     {
                         MBS_TSTART();
@@ -1204,8 +1228,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) __cluster_dims__(2, 1, 1)
                     if (leader) mbar_arrive_expect_tx(&full[slot], 2 * CF::TX);
                     tma_load_2d_pair(st + CF::A_DATA_OFF, &tm_a, fbar, ks * BKB, rb * BM);
                     tma_load_3d_pair(st + CF::B_DATA_OFF, &tm_b, fbar, 0, nb0 / 16, ks * 8);
-                    tma_load_2d_pair(st + CF::A_IMG_OFF, &tm_ia, fbar, 0, (rb * p.k_stages + ks) * (IMG_A_BYTES / 256));
-                    tma_load_2d_pair(st + CF::B_IMG_OFF, &tm_ib, fbar, 0, (tc * p.k_stages + ks) * (IMG_B_BYTES / 256));
+                    if (g >= STAGES) load_images(g);
 #if MBS_TIMING
                     tacc[10] += 1;
 #endif
@@ -1215,6 +1238,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) __cluster_dims__(2, 1, 1)
                         phase ^= 1;
                     }
                 }
+            }
+            if (g <= STAGES)
+            {
+                // a sequence of at most STAGES stages never reached the wait
+                // above (it runs at the top of stage STAGES): its images are owed
+                griddep_wait();
+                for (int d = 0; d < g; ++d) load_images(d);
             }
         pair_producer_done:;
         }
@@ -1529,6 +1559,7 @@ thread_local cudaEvent_t g_ev_before = nullptr, g_ev_after = nullptr;
 // as the NCCL kernels of an overlapped all-gather.
 thread_local int g_grid_limit = 0;
 
+
 int record_before(cudaStream_t s)
 {
     if (g_ev_before == nullptr) return MBS_OK;
@@ -1547,6 +1578,14 @@ int env_int(const char* name, int dflt)
 {
     const char* v = getenv(name);
     return (v != nullptr && *v != 0) ? atoi(v) : dflt;
+}
+
+// The pair GEMM starts behind its scale-image pre-pass by programmatic
+// dependent launch; MBS_PAIR_PDL=0 launches it in plain stream order.
+bool pair_pdl_enabled()
+{
+    static const bool on = env_int("MBS_PAIR_PDL", 1) != 0;
+    return on;
 }
 
 // Workspace of the CTA-pair path: the A and B scale images.
@@ -1848,8 +1887,13 @@ int launch_pair(const Problem& pb, const Plan& pl, const DeviceInfo& dev, void* 
     cfg.blockDim = dim3(NUM_THREADS);
     cfg.dynamicSmemBytes = CF::SMEM_BYTES;
     cfg.stream = stream;
-    cfg.attrs = nullptr;
-    cfg.numAttrs = 0;  // cluster shape comes from __cluster_dims__
+    // programmatic dependent launch: the GEMM may start while the image
+    // pre-pass runs (cluster shape comes from __cluster_dims__)
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pair_pdl_enabled() ? 1 : 0;
     st = record_before(stream);
     if (st) return st;
     cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, tm_a, tm_b, tm_ia, tm_ib, p);

@@ -423,6 +423,21 @@ __device__ __forceinline__ bool named_bar_and(int id, int nthreads, bool pred)
     return r != 0;
 }
 
+// Programmatic dependent launch: a kernel launched with programmatic stream
+// serialisation may start before the kernel ahead of it in the stream ends;
+// griddep_wait() blocks until that kernel has completed and its writes are
+// visible, griddep_launch_dependents() lets the next kernel start early.
+// Both are no-ops when the launch did not ask for it.
+__device__ __forceinline__ void griddep_wait()
+{
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+__device__ __forceinline__ void griddep_launch_dependents()
+{
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p)
 {
     unsigned v;

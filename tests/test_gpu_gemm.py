@@ -99,6 +99,23 @@ def test_one_workspace_serves_every_schedule(force_env):
         assert_gemm_close(out, ref, bound, f"step {i} {M}x{N}x{K} {env}")
 
 
+@pytest.mark.parametrize("M,N,K,macro", [(512, 1024, 2048, False), (300, 1024, 1088, False),
+                                         (512, 1024, 2048, True), (700, 768, 1600, True)])
+def test_cta_pair_path(force_env, M, N, K, macro):
+    """The CTA-pair kernel on ragged M (rows past M are computed from padding
+    and never stored), a partial last K stage and both B scale layouts."""
+    import mbs_b200
+    force_env(MBS_FORCE_SCHEDULE=2, MBS_FORCE_PAIR=1)
+    c = Case(M, N, K, seed=M + K, factors=True, macro=macro)
+    if macro:
+        out = mbs_b200.gemm_a4w4_macro(c.A, c.B, c.A_scale, c.B_scale, c.A_factor, c.B_factor)
+    else:
+        out = _gemm(c)
+    torch.cuda.synchronize()
+    ref, bound = c.reference()
+    assert_gemm_close(out, ref, bound, f"pair {M}x{N}x{K} macro={macro}")
+
+
 @pytest.mark.parametrize("M,N,K", [(384, 1024, 512), (1000, 2048, 256)])
 def test_data_parallel_schedule(force_env, M, N, K):
     force_env(MBS_FORCE_SCHEDULE=2, MBS_FORCE_GRID=7)
