@@ -960,28 +960,35 @@ __global__ void __launch_bounds__(256) pack_weight_kernel(const uint8_t* __restr
 }
 
 // ====================================================================== CTA pair
-// Prefill kernel on CTA pairs (cluster of 2): one tcgen05.mma.cta_group::2
-// computes a 256 x 256 x 64 block, each CTA contributing 128 rows of A and a
-// 128-row half of B from its own shared memory and holding its 128 x 256
-// accumulator in its own TMEM.  Per SM this halves the B bytes that TMA
-// writes into and the MMA reads out of shared memory compared with the
-// single-CTA 128 x 256 tile.
+// Prefill kernel on CTA pairs (cluster of 2).  A pair tile is 256 rows of A
+// by BN = 256 or 384 columns: per 64-K step one tcgen05.mma.cta_group::2 of
+// 256 x 256 and, for BN = 384, a second one of 256 x 128 on the same A.  Each
+// CTA contributes 128 rows of A and half of each MMA's B rows (128, plus 64)
+// from its own shared memory and holds its 128 x BN accumulator in its own
+// TMEM (accumulator column j = output column c0 + j).  Per SM the pair halves
+// the B bytes TMA writes into shared memory compared with a single-CTA tile,
+// and BN = 384 moves 20 % fewer operand bytes per FLOP than 256 (44 vs 35 KB
+// per stage for 1.5x the MMA work).
 //
-// Scales reach it as "scale images" written by scale_image_kernel: per
-// 128-row block of A and per 256-row tile of B, per K stage, the 512-byte
-// 32x16B blocks tcgen05.cp.32x128b.warpx4 copies into TMEM (the copy
-// replicates them to all four lane quarters).  Every image is reused by all
-// tiles of its row / column, so building them once per call costs a few
-// microseconds and removes all scale work from the GEMM.
+// Scales reach it as "scale images" written by scale_image_kernel: per K
+// stage and 128-row block of A or B, the two 512-byte 32x16B blocks
+// tcgen05.cp.32x128b.warpx4 copies into TMEM (the copy replicates them to all
+// four lane quarters).  Every image is reused by all tiles of its rows, so
+// building them once per call costs a few microseconds and removes all scale
+// work from the GEMM.
 //
 // Protocol (leader = cluster rank 0):
 //   * both producers wait on their own `empty` slot (the leader's commit
-//     multicasts to both), then TMA their A tile, B half, A-scale image and
-//     the pair's B-scale image with .cta_group::2, completing on the LEADER's
-//     `full` barrier, which the leader's producer arms with both CTAs' bytes;
-//   * the leader's scale-copy thread (warp 2) waits on `full`, issues
-//     tcgen05.cp.cta_group::2 (each CTA's shared memory -> its own TMEM) into
-//     the slot's scale columns and commits to the leader's `sfready`;
+//     multicasts to both), then TMA their A tile, B rows, A-scale image and
+//     the tile's B-scale images with .cta_group::2, completing on the
+//     LEADER's `full` barrier, which the leader's producer arms with both
+//     CTAs' bytes;
+//   * the leader's scale-copy thread (warp 2) waits on `full` and on its TMEM
+//     scale slot being free (for BN = 384 there are fewer scale slots than
+//     stages: the slot of stage g is free once the MMAs of stage g - SF_SLOTS
+//     completed, i.e. that stage's `empty` commit), issues
+//     tcgen05.cp.cta_group::2 (each CTA's shared memory -> its own TMEM) and
+//     commits to the leader's `sfready`;
 //   * the leader's MMA thread waits on `full` and `sfready`, issues the pair
 //     MMAs and multicasts its commits to both CTAs' `empty` / `acc_full`.
 //     (Keeping tcgen05.cp out of the MMA thread matters: a thread that issues
@@ -990,15 +997,15 @@ __global__ void __launch_bounds__(256) pack_weight_kernel(const uint8_t* __restr
 //   * each CTA's epilogue drains its own TMEM and arrives on the leader's
 //     `acc_empty` (16 warps).
 
-constexpr int IMG_A_BYTES = 2 * 512;      // per 128 A rows per K stage: [q] blocks
-constexpr int IMG_B_BYTES = 2 * 2 * 512;  // per 256 B rows per K stage: [q][128-row half] blocks
+constexpr int IMG_BLOCK = 2 * 512;  // scale image of 128 rows per K stage: [q] 32x16B blocks
 
-// flatS scales (or macro-block B scales) -> scale images.
-//   A image [rb128][ks][q][l][16 B]: word w of row l, byte k = SF(128rb + 32w + l, 8ks + 4q + k)
-//   B image [tb256][ks][q][b][l][16 B]: word w = SF(256tb + 128b + 32w + l, ...)
-// i.e. per (block, K stage, K-group set q) the 32x16B block tcgen05.cp
-// .32x128b.warpx4 takes.  Rows outside the scale buffer give 0.
-// One thread per (128-row block, K stage, row-in-16 rho): it loads the 16
+// flatS scales (or macro-block B scales) -> scale images
+//   img[ks][blk][q][l][16 B]: word w of row l, byte k = SF(128 blk + 32 w + l, 8 ks + 4 q + k)
+// i.e. per (K stage, 128-row block, K-group set q) the 32x16B block
+// tcgen05.cp.32x128b.warpx4 takes.  K-stage-major, so one stage's blocks of
+// consecutive rows are contiguous (one TMA box loads a tile's B blocks).
+// Rows outside the scale buffer give 0.
+// One thread per (K stage, 128-row block, row-in-16 rho): it loads the 16
 // flatS words of the block's four 32-row groups at that rho (word k*16 + rho
 // of each group's 256-byte chunk holds the scales of rows rho and rho + 16
 // for the K-group k of both sets of 4), transposes them with byte
@@ -1007,7 +1014,7 @@ constexpr int IMG_B_BYTES = 2 * 2 * 512;  // per 256 B rows per K stage: [q][128
 // image rows are copies.
 __global__ void __launch_bounds__(256) scale_image_kernel(const uint8_t* __restrict__ sa, int a_rows_buf,
                                                           int a_blocks, const uint8_t* __restrict__ sb,
-                                                          int b_rows_buf, int b_tiles, int snp, int ks_count,
+                                                          int b_rows_buf, int b_blocks, int snp, int ks_count,
                                                           int b_macro, int mb_ld, uint8_t* __restrict__ img_a,
                                                           uint8_t* __restrict__ img_b)
 {
@@ -1015,7 +1022,7 @@ __global__ void __launch_bounds__(256) scale_image_kernel(const uint8_t* __restr
     // stages and waits for this grid before it reads any image
     griddep_launch_dependents();
     const long long na = (long long)a_blocks * ks_count * 16;
-    const long long nb = (long long)b_tiles * ks_count * 2 * 16;
+    const long long nb = (long long)b_blocks * ks_count * 16;
     for (long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x; t < na + nb;
          t += (long long)gridDim.x * blockDim.x)
     {
@@ -1023,15 +1030,10 @@ __global__ void __launch_bounds__(256) scale_image_kernel(const uint8_t* __restr
         long long u = is_a ? t : t - na;
         const int rho = (int)(u & 15);
         u >>= 4;
-        int b = 0;
-        if (!is_a)
-        {
-            b = (int)(u & 1);
-            u >>= 1;
-        }
-        const int ks = (int)(u % ks_count);
-        const long long blk = u / ks_count;
-        const long long row0 = is_a ? blk * 128 : blk * 256 + 128 * b;  // first row of the 128-row block
+        const int nblk = is_a ? a_blocks : b_blocks;
+        const long long blk = u % nblk;
+        const int ks = (int)(u / nblk);
+        const long long row0 = blk * 128;
         const int rows_buf = is_a ? a_rows_buf : b_rows_buf;
         const uint8_t* src = is_a ? sa : sb;
         uint32_t o[4][4];  // [group][p], p = 2q + h
@@ -1076,36 +1078,47 @@ __global__ void __launch_bounds__(256) scale_image_kernel(const uint8_t* __restr
                 o[g][3] = __byte_perm(t2, t3, 0x7632);
             }
         }
+        uint8_t* img = (is_a ? img_a : img_b) + ((long long)ks * nblk + blk) * IMG_BLOCK;
 #pragma unroll
         for (int pp = 0; pp < 4; ++pp)
         {
             const int h = pp & 1, q = pp >> 1;
             const uint4 v4 = make_uint4(o[0][pp], o[1][pp], o[2][pp], o[3][pp]);
-            uint8_t* dst = is_a ? img_a + (blk * ks_count + ks) * IMG_A_BYTES + q * 512
-                                : img_b + (blk * ks_count + ks) * IMG_B_BYTES + q * 1024 + b * 512;
-            *reinterpret_cast<uint4*>(dst + (16 * h + rho) * 16) = v4;
+            *reinterpret_cast<uint4*>(img + q * 512 + (16 * h + rho) * 16) = v4;
         }
     }
 }
 
-template <int STAGES_>
+template <int STAGES_, int BN_>
 struct CfgPair
 {
-    static constexpr int BN = 256;   // pair N (each CTA holds a 128-row half of B)
-    static constexpr int BNH = 128;
+    static constexpr int BN = BN_;           // pair tile columns
+    static constexpr int N2 = BN - 256;      // columns of the second MMA (0 or 128)
+    static_assert(N2 == 0 || N2 == 128, "pair tiles are 256 or 384 columns wide");
+    static constexpr int B1_ROWS = 128;      // B rows per CTA for the N = 256 MMA
+    static constexpr int B2_ROWS = N2 / 2;   // ... for the N = 128 MMA
     static constexpr int STAGES = STAGES_;
+    static constexpr int B_BLOCKS = BN / 128;  // 128-row scale image blocks of B per stage
     static constexpr int A_DATA = BM * BKB;
-    static constexpr int B_DATA = BNH * BKB;
+    static constexpr int B1_DATA = B1_ROWS * BKB;
+    static constexpr int B2_DATA = B2_ROWS * BKB;
     static constexpr int A_DATA_OFF = 0;
-    static constexpr int B_DATA_OFF = A_DATA;
-    static constexpr int A_IMG_OFF = B_DATA_OFF + B_DATA;
-    static constexpr int B_IMG_OFF = A_IMG_OFF + IMG_A_BYTES;
-    static constexpr int STAGE_BYTES = align_up(B_IMG_OFF + IMG_B_BYTES, 1024);
-    static constexpr uint32_t TX = A_DATA + B_DATA + IMG_A_BYTES + IMG_B_BYTES;  // per CTA
-    static constexpr int SF_STAGE_COLS = 8 + 16;
+    static constexpr int B1_DATA_OFF = A_DATA;
+    static constexpr int B2_DATA_OFF = B1_DATA_OFF + B1_DATA;
+    static constexpr int A_IMG_OFF = B2_DATA_OFF + B2_DATA;
+    static constexpr int B_IMG_OFF = A_IMG_OFF + IMG_BLOCK;
+    static constexpr int STAGE_BYTES = align_up(B_IMG_OFF + B_BLOCKS * IMG_BLOCK, 1024);
+    static constexpr uint32_t TX = A_DATA + B1_DATA + B2_DATA + (1 + B_BLOCKS) * IMG_BLOCK;  // per CTA
+    // TMEM: accumulator columns [0, BN); then per scale slot SFA [q] (4 columns
+    // each), SFB of the N = 256 MMA [q] (8 each), SFB of the N = 128 MMA [q] (4 each)
+    static constexpr int SFB1_OFF = 8;
+    static constexpr int SFB2_OFF = 24;
+    static constexpr int SF_STAGE_COLS = 8 + 16 + (N2 ? 8 : 0);
     static constexpr int SF_BASE = BN;  // one accumulator buffer
+    static constexpr int SF_SLOTS_MAX = (512 - BN) / SF_STAGE_COLS;
+    static constexpr int SF_SLOTS = STAGES < SF_SLOTS_MAX ? STAGES : SF_SLOTS_MAX;
     static constexpr int TMEM_COLS = 512;
-    static_assert(SF_BASE + STAGES * SF_STAGE_COLS <= 512, "TMEM budget");
+    static_assert(SF_BASE + SF_SLOTS * SF_STAGE_COLS <= 512, "TMEM budget");
     // full, sfready, empty [STAGES]; acc_full, acc_empty; tmem slot; abort
     static constexpr int BAR_BYTES = (3 * STAGES + 2) * 8 + 16;
     static constexpr int EPI_BYTES = (BM + 2 * BN) * 4;  // factor + bias staging
@@ -1116,8 +1129,8 @@ struct CfgPair
 template <class CF>
 __global__ void __launch_bounds__(NUM_THREADS, 1) __cluster_dims__(2, 1, 1)
     mxf4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
-                          const __grid_constant__ CUtensorMap tm_ia, const __grid_constant__ CUtensorMap tm_ib,
-                          const Params p)
+                          const __grid_constant__ CUtensorMap tm_b2, const __grid_constant__ CUtensorMap tm_ia,
+                          const __grid_constant__ CUtensorMap tm_ib, const Params p)
 {
     constexpr int BN = CF::BN;
     constexpr int STAGES = CF::STAGES;
@@ -1158,6 +1171,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) __cluster_dims__(2, 1, 1)
         fence_mbar_init();
         prefetch_tmap(&tm_a);
         prefetch_tmap(&tm_b);
+        if (CF::N2) prefetch_tmap(&tm_b2);
         prefetch_tmap(&tm_ia);
         prefetch_tmap(&tm_ib);
     }
@@ -1179,6 +1193,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) __cluster_dims__(2, 1, 1)
         if (lane == 0)
         {
             const uint32_t full0 = mapa_shared(smem_u32(full), 0);  // leader's full[0]
+            const int a_blocks = tiles_r2 * 2, b_blocks = tiles_c * CF::B_BLOCKS;  // image blocks per K stage
             int slot = 0;
             uint32_t phase = 0;
 #if MBS_TIMING
@@ -1196,15 +1211,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) __cluster_dims__(2, 1, 1)
                 const int rb = (t % tiles_r2) * 2 + (int)rank, tc = t / tiles_r2;
                 uint8_t* st = smem + (g % STAGES) * CF::STAGE_BYTES;
                 const uint32_t fbar = full0 + (g % STAGES) * 8;
-                tma_load_2d_pair(st + CF::A_IMG_OFF, &tm_ia, fbar, 0, (rb * p.k_stages + ks) * (IMG_A_BYTES / 256));
-                tma_load_2d_pair(st + CF::B_IMG_OFF, &tm_ib, fbar, 0, (tc * p.k_stages + ks) * (IMG_B_BYTES / 256));
+                tma_load_2d_pair(st + CF::A_IMG_OFF, &tm_ia, fbar, 0, (ks * a_blocks + rb) * (IMG_BLOCK / 256));
+                tma_load_2d_pair(st + CF::B_IMG_OFF, &tm_ib, fbar, 0,
+                                 (ks * b_blocks + tc * CF::B_BLOCKS) * (IMG_BLOCK / 256));
             };
             int g = 0;  // stage index in this cluster's sequence
             for (int t = cluster; t < ntiles; t += nclusters)
             {
                 const int tr = t % tiles_r2, tc = t / tiles_r2;
                 const int rb = tr * 2 + (int)rank;  // this CTA's 128-row block of A
-                const int nb0 = tc * BN + (int)rank * CF::BNH;
+                // this CTA's B rows: half of the N = 256 MMA's, half of the N = 128 MMA's
+                const int nb1 = tc * BN + (int)rank * CF::B1_ROWS;
+                const int nb2 = tc * BN + 256 + (int)rank * CF::B2_ROWS;
                 for (int ks = 0; ks < p.k_stages; ++ks, ++g)
                 {
                     if (g == STAGES)
@@ -1227,7 +1245,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) __cluster_dims__(2, 1, 1)
                     const uint32_t fbar = full0 + slot * 8;
                     if (leader) mbar_arrive_expect_tx(&full[slot], 2 * CF::TX);
                     tma_load_2d_pair(st + CF::A_DATA_OFF, &tm_a, fbar, ks * BKB, rb * BM);
-                    tma_load_3d_pair(st + CF::B_DATA_OFF, &tm_b, fbar, 0, nb0 / 16, ks * 8);
+                    tma_load_3d_pair(st + CF::B1_DATA_OFF, &tm_b, fbar, 0, nb1 / 16, ks * 8);
+                    if (CF::N2) tma_load_3d_pair(st + CF::B2_DATA_OFF, &tm_b2, fbar, 0, nb2 / 16, ks * 8);
                     if (g >= STAGES) load_images(g);
 #if MBS_TIMING
                     tacc[10] += 1;
@@ -1253,7 +1272,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) __cluster_dims__(2, 1, 1)
     {
         if (lane == 0 && leader)
         {
-            int slot = 0;
+            int slot = 0, sfs = 0;  // operand slot, TMEM scale slot
             uint32_t phase = 0;
             uint32_t acc_phase = 0;
 #if MBS_TIMING
@@ -1296,22 +1315,30 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) __cluster_dims__(2, 1, 1)
                     MBS_TSTART();
                     tc_fence_after();
                     const uint8_t* st = smem + slot * CF::STAGE_BYTES;
-                    const uint32_t sf_a = tmem_base + CF::SF_BASE + slot * CF::SF_STAGE_COLS;
-                    const uint32_t sf_b = sf_a + 8;
+                    const uint32_t sf_a = tmem_base + CF::SF_BASE + sfs * CF::SF_STAGE_COLS;
                     const uint32_t a_base = smem_u32(st + CF::A_DATA_OFF);
-                    const uint32_t b_base = smem_u32(st + CF::B_DATA_OFF);
+                    const uint32_t b1_base = smem_u32(st + CF::B1_DATA_OFF);
+                    const uint32_t b2_base = smem_u32(st + CF::B2_DATA_OFF);
 #pragma unroll
                     for (int j = 0; j < BK / MMA_K; ++j)
                     {
                         if (ks * BK + j * MMA_K >= p.K) break;
                         const uint64_t a_desc = make_smem_desc(a_base + j * 32, 16, 1024, 2);
-                        const uint64_t b_desc =
-                            make_smem_desc(b_base + j * 2 * (CF::BNH * 16), CF::BNH * 16, 128, 0);
                         const uint32_t id = (uint32_t)(j & 1) * 2;
                         const uint32_t q = (uint32_t)(j >> 1);
-                        tc_mma_mxf4_pair(tmem_base, a_desc, b_desc, make_idesc_mxf4(2 * BM, BN, id, id),
-                                         (sf_a + 4 * q) | (id << 30), (sf_b + 8 * q) | (id << 30),
-                                         (ks > 0 || j > 0) ? 1u : 0u);
+                        const uint32_t sfa = (sf_a + 4 * q) | (id << 30);
+                        const uint32_t acc = (ks > 0 || j > 0) ? 1u : 0u;
+                        const uint64_t b1_desc =
+                            make_smem_desc(b1_base + j * 2 * (CF::B1_ROWS * 16), CF::B1_ROWS * 16, 128, 0);
+                        tc_mma_mxf4_pair(tmem_base, a_desc, b1_desc, make_idesc_mxf4(2 * BM, 256, id, id), sfa,
+                                         (sf_a + CF::SFB1_OFF + 8 * q) | (id << 30), acc);
+                        if (CF::N2)
+                        {
+                            const uint64_t b2_desc =
+                                make_smem_desc(b2_base + j * 2 * (CF::B2_ROWS * 16), CF::B2_ROWS * 16, 128, 0);
+                            tc_mma_mxf4_pair(tmem_base + 256, a_desc, b2_desc, make_idesc_mxf4(2 * BM, CF::N2, id, id),
+                                             sfa, (sf_a + CF::SFB2_OFF + 4 * q) | (id << 30), acc);
+                        }
                     }
                     tc_commit_pair_mc(&empty[slot], 0x3);
                     MBS_TADD(tacc, 11);
@@ -1320,6 +1347,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) __cluster_dims__(2, 1, 1)
                         slot = 0;
                         phase ^= 1;
                     }
+                    if (++sfs == CF::SF_SLOTS) sfs = 0;
                 }
                 if (!ok) break;
                 {
@@ -1344,14 +1372,28 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) __cluster_dims__(2, 1, 1)
         // which then waits on sfready (cheap) instead.
         if (lane == 0 && leader)
         {
-            int slot = 0;
-            uint32_t phase = 0;
+            int slot = 0, sfs = 0, eslot = 0;
+            uint32_t phase = 0, ephase = 0;
+            long long g = 0;
             for (int t = cluster; t < ntiles; t += nclusters)
             {
                 bool ok = true;
-                for (int ks = 0; ks < p.k_stages; ++ks)
+                for (int ks = 0; ks < p.k_stages; ++ks, ++g)
                 {
-                    if (!mbar_wait(&full[slot], phase, abort_flag))
+                    // the scale slot of stage g was last read by the MMAs of
+                    // stage g - SF_SLOTS (their `empty` commit); with a scale
+                    // slot per operand slot, `full` already implies it
+                    bool ok_wait = mbar_wait(&full[slot], phase, abort_flag);
+                    if (CF::SF_SLOTS < STAGES && g >= CF::SF_SLOTS)
+                    {
+                        ok_wait = ok_wait && mbar_wait(&empty[eslot], ephase, abort_flag);
+                        if (++eslot == STAGES)
+                        {
+                            eslot = 0;
+                            ephase ^= 1;
+                        }
+                    }
+                    if (!ok_wait)
                     {
                         raise_error(p, abort_flag);
                         ok = false;
@@ -1359,23 +1401,29 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) __cluster_dims__(2, 1, 1)
                     }
                     tc_fence_after();
                     const uint8_t* st = smem + slot * CF::STAGE_BYTES;
-                    const uint32_t sf_a = tmem_base + CF::SF_BASE + slot * CF::SF_STAGE_COLS;
-                    const uint32_t sf_b = sf_a + 8;
-                    // SFA: one 32x16B block per K-group set q; SFB: per q, one per 128-row half
+                    const uint32_t sf_a = tmem_base + CF::SF_BASE + sfs * CF::SF_STAGE_COLS;
+                    // SFA: one 32x16B block per K-group set q; SFB: per q, one per 128-row block
 #pragma unroll
                     for (int q = 0; q < 2; ++q)
+                    {
                         tc_cp_32x128b_warpx4_pair(sf_a + 4 * q,
                                                   make_smem_desc(smem_u32(st + CF::A_IMG_OFF + q * 512), 0, 128, 0));
 #pragma unroll
-                    for (int a = 0; a < 4; ++a)
-                        tc_cp_32x128b_warpx4_pair(sf_b + 4 * a,
-                                                  make_smem_desc(smem_u32(st + CF::B_IMG_OFF + a * 512), 0, 128, 0));
+                        for (int b = 0; b < CF::B_BLOCKS; ++b)
+                        {
+                            const uint32_t col = b < 2 ? CF::SFB1_OFF + 8 * q + 4 * b : CF::SFB2_OFF + 4 * q;
+                            tc_cp_32x128b_warpx4_pair(
+                                sf_a + col,
+                                make_smem_desc(smem_u32(st + CF::B_IMG_OFF + b * IMG_BLOCK + q * 512), 0, 128, 0));
+                        }
+                    }
                     tc_commit_pair_mc(&sfready[slot], 0x1);
                     if (++slot == STAGES)
                     {
                         slot = 0;
                         phase ^= 1;
                     }
+                    if (++sfs == CF::SF_SLOTS) sfs = 0;
                 }
                 if (!ok) break;
             }
@@ -1390,7 +1438,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) __cluster_dims__(2, 1, 1)
         const int et = threadIdx.x - EPI_WARP0 * 32;
         constexpr int COLS = BN / 2;
         constexpr int NCH = COLS / 16;
-        constexpr int BATCH = 4;
+        constexpr int BATCH = COLS > 128 ? 2 : 4;  // 384-column tiles hold 96 packed words per thread
         const bool has_factor = (p.a_factor != nullptr) || (p.b_factor != nullptr);
         const bool has_alpha = p.alpha != 1.0f;
         const bool has_bias = p.bias != nullptr;
@@ -1412,11 +1460,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) __cluster_dims__(2, 1, 1)
                     const int r = r0 + et;
                     fr_s[et] = (p.a_factor != nullptr && r < p.M) ? byte_to_factor(p.a_factor[r]) : 1.0f;
                 }
-                if (et < BN)
+                for (int j = et; j < BN; j += NUM_EPI_THREADS)
                 {
-                    const int c = c0 + et;
-                    fc_s[et] = (p.b_factor != nullptr && c < p.N) ? byte_to_factor(p.b_factor[c]) : 1.0f;
-                    bias_s[et] = (has_bias && c < p.N) ? __bfloat162float(p.bias[c]) : 0.0f;
+                    const int c = c0 + j;
+                    fc_s[j] = (p.b_factor != nullptr && c < p.N) ? byte_to_factor(p.b_factor[c]) : 1.0f;
+                    bias_s[j] = (has_bias && c < p.N) ? __bfloat162float(p.bias[c]) : 0.0f;
                 }
                 named_bar_sync(1, NUM_EPI_THREADS);
             }
@@ -1546,6 +1594,7 @@ struct Plan
     int bn;
     int r_rows;  // rows of A loaded per stage (non-swapped single-CTA path)
     bool swap, sk, pair;
+    int pair_bn;  // CTA-pair tile columns (256 or 384)
     int G, tiles_r, tiles_c, k_stages;
     size_t ws_bytes;
 };
@@ -1592,12 +1641,13 @@ bool pair_pdl_enabled()
 size_t pair_image_a_bytes(int M, int K)
 {
     const size_t blocks = (size_t)((M + 2 * BM - 1) / (2 * BM)) * 2;
-    return blocks * ((K + BK - 1) / BK) * IMG_A_BYTES;
+    return blocks * ((K + BK - 1) / BK) * IMG_BLOCK;
 }
 
-size_t pair_image_b_bytes(int N, int K)
+size_t pair_image_b_bytes(int N, int K, int pair_bn)
 {
-    return (size_t)((N + 255) / 256) * ((K + BK - 1) / BK) * IMG_B_BYTES;
+    const size_t blocks = (size_t)((N + pair_bn - 1) / pair_bn) * (pair_bn / 128);
+    return blocks * ((K + BK - 1) / BK) * IMG_BLOCK;
 }
 
 struct Plan;
@@ -1665,17 +1715,36 @@ Plan make_plan(int M, int N, int K, int num_sms, bool packed = false)
     pl.G = (int)(units < G ? units : G);
     pl.ws_bytes = pl.sk ? kFlagBytes + sk_partial_bytes(pl) : 0;
     // Data-parallel problems with at least 4 pair tiles run on CTA pairs
-    // (256 x 256 tiles; their workspace holds the scale images); below that
-    // the scale-image pre-pass (a second launch) costs more than the pair
-    // saves.
-    const long long t2 = (long long)((M + 2 * BM - 1) / (2 * BM)) * ((N + 255) / 256);
+    // (256-row tiles; their workspace holds the scale images); below that the
+    // scale-image pre-pass (a second launch) costs more than the pair saves.
+    const long long tr2 = (M + 2 * BM - 1) / (2 * BM);
+    const long long t2 = tr2 * ((N + 255) / 256);
     const int force_pair = env_int("MBS_FORCE_PAIR", -1);
     pl.pair = !packed && !pl.swap && !pl.sk && force_pair != 0 && (t2 >= 4 || force_pair == 1);
     if (pl.pair)
     {
+        // 384-column tiles do 1.5x the MMA work of 256-column ones for 1.26x
+        // the bytes and measure ~1.39x the time, but come in coarser rounds
+        // over the clusters: take the width with the smaller (rounds of tiles
+        // per cluster) x (time per tile).  MBS_PAIR_BN=256/384 overrides.
         const int c = G / 2;
-        pl.G = 2 * (int)(t2 < c ? t2 : c);
-        pl.ws_bytes = kFlagBytes + pair_image_a_bytes(M, K) + pair_image_b_bytes(N, K);
+        const long long t3 = tr2 * ((N + 383) / 384);
+        const double cost256 = (double)((t2 + c - 1) / c);
+        const double cost384 = (double)((t3 + c - 1) / c) * 1.39;
+        const int force_bn = env_int("MBS_PAIR_BN", 0);
+        pl.pair_bn = force_bn == 256 || force_bn == 384 ? force_bn : (cost384 < cost256 ? 384 : 256);
+        const long long tp = pl.pair_bn == 384 ? t3 : t2;
+        const size_t ia = pair_image_a_bytes(M, K), ib = pair_image_b_bytes(N, K, pl.pair_bn);
+        // TMA row coordinates of the images are 32-bit
+        if (ia / 256 < (size_t)INT32_MAX && ib / 256 < (size_t)INT32_MAX)
+        {
+            pl.G = 2 * (int)(tp < c ? tp : c);
+            pl.ws_bytes = kFlagBytes + ia + ib;
+        }
+        else
+        {
+            pl.pair = false;
+        }
     }
     return pl;
 }
@@ -1792,10 +1861,12 @@ int make_maps(const Problem& pb, const Plan& pl, CUtensorMap* tm_r, CUtensorMap*
     return st;
 }
 
-// TMA descriptors of the CTA-pair kernel: A boxes of 128 rows, B boxes of a
-// 128-row half, and the scale images as rows of 256 bytes.
-int make_maps_pair(const Problem& pb, void* img_a, size_t img_a_bytes, void* img_b, size_t img_b_bytes,
-                   CUtensorMap* tm_a, CUtensorMap* tm_b, CUtensorMap* tm_ia, CUtensorMap* tm_ib)
+// TMA descriptors of the CTA-pair kernel: A boxes of 128 rows, B boxes of the
+// CTA's 128 (and 64) rows, and the scale images as rows of 256 bytes (one
+// 128-row block of A, a tile's 2 or 3 blocks of B).
+int make_maps_pair(const Problem& pb, int pair_bn, void* img_a, size_t img_a_bytes, void* img_b,
+                   size_t img_b_bytes, CUtensorMap* tm_a, CUtensorMap* tm_b, CUtensorMap* tm_b2, CUtensorMap* tm_ia,
+                   CUtensorMap* tm_ib)
 {
     const uint64_t Kp = (uint64_t)pb.K / 2;
     int st;
@@ -1807,18 +1878,26 @@ int make_maps_pair(const Problem& pb, void* img_a, size_t img_a_bytes, void* img
                          CU_TENSOR_MAP_SWIZZLE_128B);
         if (st) return st;
     }
+    for (int which = 0; which < 2; ++which)
     {
+        const int rows = which == 0 ? 128 : 64;
+        CUtensorMap* m = which == 0 ? tm_b : tm_b2;
+        if (which == 1 && pair_bn == 256)
+        {
+            *m = *tm_b;  // unused
+            break;
+        }
         const uint64_t dims[3] = {256, (uint64_t)pb.N / 16, (uint64_t)pb.K / 32};
         const uint64_t strides[2] = {(uint64_t)pb.K * 8, 256};
-        const uint32_t box[3] = {256, 128 / 16, BK / 32};
-        st = encode_tmap(tm_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, (void*)pb.B, dims, strides, box,
+        const uint32_t box[3] = {256, (uint32_t)rows / 16, BK / 32};
+        st = encode_tmap(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, (void*)pb.B, dims, strides, box,
                          CU_TENSOR_MAP_SWIZZLE_NONE);
         if (st) return st;
     }
     {
         const uint64_t dims[2] = {256, (uint64_t)(img_a_bytes / 256)};
         const uint64_t strides[1] = {256};
-        const uint32_t box[2] = {256, IMG_A_BYTES / 256};
+        const uint32_t box[2] = {256, IMG_BLOCK / 256};
         st = encode_tmap(tm_ia, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, img_a, dims, strides, box,
                          CU_TENSOR_MAP_SWIZZLE_NONE);
         if (st) return st;
@@ -1826,7 +1905,7 @@ int make_maps_pair(const Problem& pb, void* img_a, size_t img_a_bytes, void* img
     {
         const uint64_t dims[2] = {256, (uint64_t)(img_b_bytes / 256)};
         const uint64_t strides[1] = {256};
-        const uint32_t box[2] = {256, IMG_B_BYTES / 256};
+        const uint32_t box[2] = {256, (uint32_t)(pair_bn / 128) * (IMG_BLOCK / 256)};
         st = encode_tmap(tm_ib, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, img_b, dims, strides, box,
                          CU_TENSOR_MAP_SWIZZLE_NONE);
     }
@@ -1850,21 +1929,21 @@ int launch_pair(const Problem& pb, const Plan& pl, const DeviceInfo& dev, void* 
         }
     }
     const size_t ia = pair_image_a_bytes(pb.M, pb.K);
-    const size_t ib = pair_image_b_bytes(pb.N, pb.K);
+    const size_t ib = pair_image_b_bytes(pb.N, pb.K, CF::BN);
     uint8_t* img_a = static_cast<uint8_t*>(ws) + kFlagBytes;
     uint8_t* img_b = img_a + ia;
-    CUtensorMap tm_a, tm_b, tm_ia, tm_ib;
-    int st = make_maps_pair(pb, img_a, ia, img_b, ib, &tm_a, &tm_b, &tm_ia, &tm_ib);
+    CUtensorMap tm_a, tm_b, tm_b2, tm_ia, tm_ib;
+    int st = make_maps_pair(pb, CF::BN, img_a, ia, img_b, ib, &tm_a, &tm_b, &tm_b2, &tm_ia, &tm_ib);
     if (st) return st;
     // 1) scale images
     {
-        const int a_blocks = (int)(ia / ((size_t)pl.k_stages * IMG_A_BYTES));
-        const int b_tiles = (int)(ib / ((size_t)pl.k_stages * IMG_B_BYTES));
-        const long long threads = (long long)a_blocks * pl.k_stages * 16 + (long long)b_tiles * pl.k_stages * 32;
+        const int a_blocks = (int)(ia / ((size_t)pl.k_stages * IMG_BLOCK));
+        const int b_blocks = (int)(ib / ((size_t)pl.k_stages * IMG_BLOCK));
+        const long long threads = (long long)(a_blocks + b_blocks) * pl.k_stages * 16;
         long long blocks = (threads + 255) / 256;
         if (blocks > (long long)dev.num_sms * 8) blocks = (long long)dev.num_sms * 8;
         scale_image_kernel<<<(int)blocks, 256, 0, stream>>>(pb.AS, pb.Mpad, a_blocks, pb.BS,
-                                                            round_up(pb.N, 32), b_tiles, pb.snp, pl.k_stages,
+                                                            round_up(pb.N, 32), b_blocks, pb.snp, pl.k_stages,
                                                             pb.macro ? 1 : 0, pb.mb_ld, img_a, img_b);
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return cuda_fail(e, "scale image launch");
@@ -1896,7 +1975,7 @@ int launch_pair(const Problem& pb, const Plan& pl, const DeviceInfo& dev, void* 
     cfg.numAttrs = pair_pdl_enabled() ? 1 : 0;
     st = record_before(stream);
     if (st) return st;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, tm_a, tm_b, tm_ia, tm_ib, p);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, tm_a, tm_b, tm_b2, tm_ia, tm_ib, p);
     if (e != cudaSuccess) return cuda_fail(e, "gemm launch (pair)");
     return record_after(stream);
 }
@@ -1970,7 +2049,9 @@ int dispatch(const Problem& pb, const Plan& pl, const DeviceInfo& dev, void* ws,
         if (pl.r_rows == 64) return launch_cfg<Cfg<256, false, false, 5, 64, true>>(pb, pl, dev, ws, s);
         return launch_cfg<Cfg<256, false, false, 4, 128, true>>(pb, pl, dev, ws, s);
     }
-    if (pl.pair) return launch_pair<CfgPair<6>>(pb, pl, dev, ws, s);
+    if (pl.pair)
+        return pl.pair_bn == 384 ? launch_pair<CfgPair<5, 384>>(pb, pl, dev, ws, s)
+                                 : launch_pair<CfgPair<6, 256>>(pb, pl, dev, ws, s);
     if (pl.swap)
     {
         if (pl.bn == 32)

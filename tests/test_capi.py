@@ -81,11 +81,16 @@ def test_quant_and_shuffle_validation_without_device(lib):
 def test_workspace_size_is_host_only(lib):
     lib.mbs_gemm_a4w4_workspace_size.restype = ctypes.c_size_t
     # decode shapes use stream-K partials; a large prefill runs on CTA pairs
-    # whose workspace holds the scale images (1 KB per 128 rows of A and 2 KB
-    # per 256 rows of B, per 256-element K stage)
+    # whose workspace holds the scale images (1 KB per 128-row block of A or B
+    # per 256-element K stage; B's blocks cover whole pair tiles)
     assert lib.mbs_gemm_a4w4_workspace_size(16, 57344, 8192) > 0
-    # flag words first, then the pair path's A and B scale images
-    assert lib.mbs_gemm_a4w4_workspace_size(8192, 8192, 8192) == 4096 + 64 * 32 * 1024 + 32 * 32 * 2048
+    # flag words first, then the pair path's A and B scale images: 8192^3
+    # takes 384-column pair tiles on 148 SMs (10 rounds of 74 clusters x 1.39
+    # against 14 rounds of 256-column tiles), so B's blocks cover 22 tiles x 3
+    assert lib.mbs_gemm_a4w4_workspace_size(8192, 8192, 8192) == 4096 + 64 * 32 * 1024 + 66 * 32 * 1024
+    # 256-column tiles where both widths take one round: 2048 x 2048 x 1024
+    # is 64 tiles of 256 columns (8 x 2 B blocks per stage) against 48 of 384
+    assert lib.mbs_gemm_a4w4_workspace_size(2048, 2048, 1024) == 4096 + 16 * 4 * 1024 + 16 * 4 * 1024
     # stream-K: flag words, then one [BN=256][32 rows] fp32 partial slot per CTA (G = 148 SMs
     # is not known without a device, so only the layout's lower bound is checked)
     for shape in [(16, 57344, 8192), (1, 16, 64), (300, 272, 1088)]:

@@ -27,10 +27,11 @@ def _gemm(case, factors=True, out=None):
 
 @pytest.fixture
 def force_env():
-    saved = {k: os.environ.get(k) for k in ("MBS_FORCE_SCHEDULE", "MBS_FORCE_GRID")}
+    saved = {}
 
     def set_(**kw):
         for k, v in kw.items():
+            saved.setdefault(k, os.environ.get(k))
             os.environ[k] = str(v)
     yield set_
     for k, v in saved.items():
@@ -99,21 +100,28 @@ def test_one_workspace_serves_every_schedule(force_env):
         assert_gemm_close(out, ref, bound, f"step {i} {M}x{N}x{K} {env}")
 
 
-@pytest.mark.parametrize("M,N,K,macro", [(512, 1024, 2048, False), (300, 1024, 1088, False),
-                                         (512, 1024, 2048, True), (700, 768, 1600, True)])
-def test_cta_pair_path(force_env, M, N, K, macro):
-    """The CTA-pair kernel on ragged M (rows past M are computed from padding
-    and never stored), a partial last K stage and both B scale layouts."""
+@pytest.mark.parametrize("bn", [256, 384])
+@pytest.mark.parametrize("M,N,K,macro,grid", [(512, 1024, 2048, False, 0), (300, 1024, 1088, False, 0),
+                                              (256, 1040, 512, False, 0), (512, 1024, 2048, True, 0),
+                                              (700, 768, 1600, True, 0), (1000, 2000, 768, False, 6)])
+def test_cta_pair_path(force_env, M, N, K, macro, grid, bn):
+    """The CTA-pair kernel at both tile widths (256 columns; 384 as an N=256
+    plus an N=128 MMA): ragged M (rows past M are computed from padding and
+    never stored), ragged N inside a tile's second MMA, a partial last K
+    stage, both B scale layouts, and several tiles per cluster."""
     import mbs_b200
-    force_env(MBS_FORCE_SCHEDULE=2, MBS_FORCE_PAIR=1)
-    c = Case(M, N, K, seed=M + K, factors=True, macro=macro)
+    env = dict(MBS_FORCE_SCHEDULE=2, MBS_FORCE_PAIR=1, MBS_PAIR_BN=bn)
+    if grid:
+        env["MBS_FORCE_GRID"] = grid
+    force_env(**env)
+    c = Case(M, N, K, seed=M + K + bn, factors=True, macro=macro)
     if macro:
         out = mbs_b200.gemm_a4w4_macro(c.A, c.B, c.A_scale, c.B_scale, c.A_factor, c.B_factor)
     else:
         out = _gemm(c)
     torch.cuda.synchronize()
     ref, bound = c.reference()
-    assert_gemm_close(out, ref, bound, f"pair {M}x{N}x{K} macro={macro}")
+    assert_gemm_close(out, ref, bound, f"pair{bn} {M}x{N}x{K} macro={macro} grid={grid}")
 
 
 @pytest.mark.parametrize("M,N,K", [(384, 1024, 512), (1000, 2048, 256)])
