@@ -77,6 +77,7 @@ struct Params
     int act_rows;          // rows per activation TMA box (the activation operand's tile rows, or M)
     float alpha;                  // output scale (1 = none)
     const __nv_bfloat16* bias;    // [N] added to every output row, or null
+    int out_v8;                   // 1: `out` is 32-byte aligned, rows are stored 32 bytes per instruction
 };
 
 constexpr int align_up(int x, int a) { return (x + a - 1) / a * a; }
@@ -844,11 +845,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                             const int n = c0 + half * COLS + ch * 16;
                             if (n < p.N)
                             {
-                                uint4* dst = reinterpret_cast<uint4*>(orow + n);
-                                dst[0] = make_uint4(packed[ch * 8 + 0], packed[ch * 8 + 1], packed[ch * 8 + 2],
-                                                    packed[ch * 8 + 3]);
-                                dst[1] = make_uint4(packed[ch * 8 + 4], packed[ch * 8 + 5], packed[ch * 8 + 6],
-                                                    packed[ch * 8 + 7]);
+                                if (p.out_v8)
+                                {
+                                    st_global_v8(orow + n, packed[ch * 8 + 0], packed[ch * 8 + 1],
+                                                 packed[ch * 8 + 2], packed[ch * 8 + 3], packed[ch * 8 + 4],
+                                                 packed[ch * 8 + 5], packed[ch * 8 + 6], packed[ch * 8 + 7]);
+                                }
+                                else
+                                {
+                                    uint4* dst = reinterpret_cast<uint4*>(orow + n);
+                                    dst[0] = make_uint4(packed[ch * 8 + 0], packed[ch * 8 + 1],
+                                                        packed[ch * 8 + 2], packed[ch * 8 + 3]);
+                                    dst[1] = make_uint4(packed[ch * 8 + 4], packed[ch * 8 + 5],
+                                                        packed[ch * 8 + 6], packed[ch * 8 + 7]);
+                                }
                             }
                         }
                     }
@@ -1542,11 +1552,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) __cluster_dims__(2, 1, 1)
                     const int n = c0 + half * COLS + ch * 16;
                     if (n < p.N)
                     {
-                        uint4* dst = reinterpret_cast<uint4*>(orow + n);
-                        dst[0] = make_uint4(packed[ch * 8 + 0], packed[ch * 8 + 1], packed[ch * 8 + 2],
-                                            packed[ch * 8 + 3]);
-                        dst[1] = make_uint4(packed[ch * 8 + 4], packed[ch * 8 + 5], packed[ch * 8 + 6],
-                                            packed[ch * 8 + 7]);
+                        if (p.out_v8)
+                        {
+                            st_global_v8(orow + n, packed[ch * 8 + 0], packed[ch * 8 + 1], packed[ch * 8 + 2],
+                                         packed[ch * 8 + 3], packed[ch * 8 + 4], packed[ch * 8 + 5],
+                                         packed[ch * 8 + 6], packed[ch * 8 + 7]);
+                        }
+                        else
+                        {
+                            uint4* dst = reinterpret_cast<uint4*>(orow + n);
+                            dst[0] = make_uint4(packed[ch * 8 + 0], packed[ch * 8 + 1], packed[ch * 8 + 2],
+                                                packed[ch * 8 + 3]);
+                            dst[1] = make_uint4(packed[ch * 8 + 4], packed[ch * 8 + 5], packed[ch * 8 + 6],
+                                                packed[ch * 8 + 7]);
+                        }
                     }
                 }
             }
@@ -1957,6 +1976,7 @@ int launch_pair(const Problem& pb, const Plan& pl, const DeviceInfo& dev, void* 
     p.a_factor = pb.AF;
     p.b_factor = pb.BF;
     p.out = static_cast<__nv_bfloat16*>(pb.out);
+    p.out_v8 = (reinterpret_cast<uintptr_t>(pb.out) & 31) == 0 ? 1 : 0;  // rows are N * 2 bytes, N % 16 == 0
     p.alpha = pb.alpha;
     p.bias = static_cast<const __nv_bfloat16*>(pb.bias);
     p.err = device_error_word(dev.device);
@@ -2012,6 +2032,7 @@ int launch_cfg(const Problem& pb, const Plan& pl, const DeviceInfo& dev, void* w
     p.a_factor = pb.AF;
     p.b_factor = pb.BF;
     p.out = static_cast<__nv_bfloat16*>(pb.out);
+    p.out_v8 = (reinterpret_cast<uintptr_t>(pb.out) & 31) == 0 ? 1 : 0;  // rows are N * 2 bytes, N % 16 == 0
     p.alpha = pb.alpha;
     p.bias = static_cast<const __nv_bfloat16*>(pb.bias);
     if (pl.sk)

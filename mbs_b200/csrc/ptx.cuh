@@ -438,6 +438,17 @@ __device__ __forceinline__ void griddep_launch_dependents()
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// 32 bytes to global memory with one 256-bit store; `p` must be 32-byte
+// aligned.  Fills whole 32-byte sectors per store instruction where two
+// 16-byte stores would each fill half of one.
+__device__ __forceinline__ void st_global_v8(void* p, uint32_t v0, uint32_t v1, uint32_t v2, uint32_t v3,
+                                             uint32_t v4, uint32_t v5, uint32_t v6, uint32_t v7)
+{
+    asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "r"(v0), "r"(v1), "r"(v2),
+                 "r"(v3), "r"(v4), "r"(v5), "r"(v6), "r"(v7)
+                 : "memory");
+}
+
 __device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p)
 {
     unsigned v;

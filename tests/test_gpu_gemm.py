@@ -146,6 +146,30 @@ def test_output_canary_rows_untouched():
     assert_gemm_close(buf[:M], ref, bound, "canary")
 
 
+@pytest.mark.parametrize("env", [dict(MBS_FORCE_SCHEDULE=2, MBS_FORCE_PAIR=1, MBS_PAIR_BN=256),
+                                 dict(MBS_FORCE_SCHEDULE=2, MBS_FORCE_PAIR=1, MBS_PAIR_BN=384),
+                                 dict(MBS_FORCE_SCHEDULE=2, MBS_FORCE_PAIR=0),
+                                 dict(MBS_FORCE_SCHEDULE=1, MBS_FORCE_GRID=5)])
+def test_output_only_16_byte_aligned(force_env, env):
+    """The epilogues store 32 bytes per instruction when `out` is 32-byte
+    aligned; an output 16 bytes past such a boundary takes the 16-byte
+    stores, with the same values and nothing written outside it."""
+    force_env(**env)
+    M, N, K = 300, 1040, 512
+    c = Case(M, N, K, seed=21, factors=True)
+    Mpad = (M + 31) // 32 * 32
+    flat = torch.full((Mpad * N + 16,), -7.0, dtype=torch.bfloat16, device="cuda")
+    buf = flat[8:8 + Mpad * N].view(Mpad, N)
+    assert buf.data_ptr() % 32 == 16
+    out = _gemm(c, out=buf)
+    torch.cuda.synchronize()
+    assert out.data_ptr() == buf.data_ptr()
+    assert torch.all(flat[:8] == -7.0) and torch.all(flat[8 + Mpad * N:] == -7.0)
+    assert torch.all(buf[M:] == -7.0)
+    ref, bound = c.reference()
+    assert_gemm_close(buf[:M], ref, bound, f"16-byte aligned out {env}")
+
+
 def test_four_argument_call_and_dtype_views():
     """bench_one.py:31 calls with 4 args; fp4/e8m0 dtypes are byte-reinterpreted."""
     import mbs_b200
