@@ -6,7 +6,11 @@
 One step = one gemm_a4w4 call on the workload (default: BASELINE config[2],
 M = N = K = 8192, MXFP4 A and B quantised from seeded N(0,1) bf16, bf16 out).
 `value` is device-timed (CUDA events on the launching stream) with inputs
-resident in HBM and L2 flushed before every step; `e2e` times the public
+resident in HBM; prefill flushes L2 before every step, decode (whose weights
+alone exceed L2) replays its K steps back to back from one CUDA graph with
+events around all of them (the reference's bench_one.py:34-47 also times
+back-to-back iterations), and also reports one isolated
+call after a flush (`isolated_call`); `e2e` times the public
 operator with host (pinned) operands copied in and the result copied out
 inside the timed region.  Under torchrun every rank runs its own workload
 (weak scaling: replicas, no collective in the timed region) and the JSON
@@ -33,6 +37,7 @@ sys.path.insert(0, REPO)
 
 FP4_PER_BF16 = 4.0  # dense FP4 : BF16 tensor throughput on B200 (9 : 2.25 PFLOP/s nominal)
 L2_FLUSH_BYTES = 256 << 20
+L2_BYTES = 126 * 1000 * 1000  # B200 L2
 
 THROTTLE_BITS = {
     0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
@@ -205,6 +210,12 @@ def run_mbs(args):
     def step():
         mbs_b200.gemm_a4w4(A, B, As, Bs, out=out)
 
+    # Decode: the weights alone are larger than L2, so steps run back to back
+    # with events around all of them (the reference's bench_one.py:34-47 times
+    # this way); every other workload flushes L2 before each timed step.
+    w_bytes = N * K // 2 + N * K // 32
+    b2b = args.workload != "prefill" and w_bytes > L2_BYTES
+
     for _ in range(max(args.warmup, 3)):
         step()
     torch.cuda.synchronize()
@@ -219,6 +230,16 @@ def run_mbs(args):
         ev.record(stream)  # materialise the CUDA events
     torch.cuda.synchronize()
     L = _lib.lib()
+    graph = None
+    if b2b:
+        # the K back-to-back steps replay from one CUDA graph, so host-side
+        # launch cost cannot starve the GPU between them
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(args.steps):
+                step()
+        graph.replay()
+        torch.cuda.synchronize()
     with ClockSampler(local) as clk:
         # untimed soak: keeps the GPU under this load while the sampler starts
         t_soak = time.perf_counter() + (0.0 if args.skip_extras else args.soak_s)
@@ -226,17 +247,24 @@ def run_mbs(args):
             for _ in range(20):
                 flush_l2(0)
                 step()
+            if graph is not None:
+                graph.replay()
             torch.cuda.synchronize()
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
         t_wall = time.perf_counter()
-        for i in range(args.steps):
-            flush_l2(i)  # evict the operands from L2 before every timed step
-            L.mbs_set_profile_events(k_starts[i].cuda_event, k_ends[i].cuda_event)
-            starts[i].record(stream)
-            step()
-            ends[i].record(stream)
+        if b2b:
+            starts[0].record(stream)
+            graph.replay()
+            ends[0].record(stream)
+        else:
+            for i in range(args.steps):
+                flush_l2(i)  # evict the operands from L2 before every timed step
+                L.mbs_set_profile_events(k_starts[i].cuda_event, k_ends[i].cuda_event)
+                starts[i].record(stream)
+                step()
+                ends[i].record(stream)
         L.mbs_set_profile_events(None, None)
         torch.cuda.synchronize()
         if world > 1:
@@ -244,9 +272,31 @@ def run_mbs(args):
         t_wall = time.perf_counter() - t_wall
         if not args.skip_extras:
             time.sleep(0.25)  # let the sampler record the end of the timed region
-    per_step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
-    kernel_ms = sum(s.elapsed_time(e) for s, e in zip(k_starts, k_ends)) / args.steps
-    total_ms = sum(per_step_ms)
+    launches = launches_per_call(M, N, K)
+    if b2b:
+        total_ms = starts[0].elapsed_time(ends[0])
+        kernel_ms = total_ms / args.steps  # one GEMM kernel per step, back to back
+        assert launches == 1, "back-to-back timing assumes one kernel per call"
+    else:
+        total_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
+        kernel_ms = sum(s.elapsed_time(e) for s, e in zip(k_starts, k_ends)) / args.steps
+    isolated = None
+    if b2b and not args.skip_extras:
+        # beside the headline: one call at a time after an L2 flush (median of 5)
+        iso = []
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        for i in range(5):
+            flush_l2(i)
+            L.mbs_set_profile_events(k_starts[0].cuda_event, k_ends[0].cuda_event)
+            c0.record(stream)
+            step()
+            c1.record(stream)
+            L.mbs_set_profile_events(None, None)
+            torch.cuda.synchronize()
+            iso.append((c0.elapsed_time(c1), k_starts[0].elapsed_time(k_ends[0])))
+        iso.sort()
+        isolated = {"call_ms": round(iso[2][0], 5), "kernel_ms": round(iso[2][1], 5),
+                    "what": "one call after an L2 flush, events around the call and around its kernel"}
     if world > 1:
         t = torch.tensor([total_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -323,16 +373,20 @@ def run_mbs(args):
         "scaling": "weak", "vs_baseline": None, "dtype": "e2m1 (fp32 accumulate, bf16 out)",
         "data": "synthetic (seeded N(0,1) bf16 quantised to MXFP4 on device)",
         "config": {"workload": wl_name, "M": M, "N": N, "K": K,
-                   "l2": "flushed before every step (256 MB write + 256 MB read)",
+                   "l2": (f"weights ({w_bytes} B) larger than L2: steps back to back (one CUDA graph of the K "
+                          "steps), events around all of them"
+                          if b2b else "flushed before every step (256 MB write + 256 MB read)"),
                    "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
         "roofline": roof,
         "clocks": clk.summary(),
         "e2e": {"value": round(world * flops / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOPS",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": round(e2e_ms, 4)},
-        "gpu_launches": args.steps * launches_per_call(M, N, K),
+        "gpu_launches": args.steps * launches,
         "wall_s": round(t_wall, 3),
     }
+    if isolated is not None:
+        line["isolated_call"] = isolated
     if rank == 0 and world == 1:
         line["cpu_baseline"] = cpu_baseline(M, N, K)
     if rank == 0:
@@ -344,13 +398,10 @@ def run_mbs(args):
 
 
 def launches_per_call(M, N, K):
-    """Kernels one gemm_a4w4 call launches: the GEMM, plus the scale-image
-    kernel on the CTA-pair (large problem) path, whose workspace is non-zero
-    and not stream-K."""
+    """Kernels one gemm_a4w4 call launches (the library's own plan: the GEMM,
+    plus the scale-image kernel on the CTA-pair path)."""
     from mbs_b200 import _lib
-    big = M > 64 and _lib.lib().mbs_gemm_a4w4_workspace_size(M, N, K) > 0 and \
-        (M + 127) // 128 * ((N + 255) // 256) >= 296
-    return 2 if big else 1
+    return int(_lib.lib().mbs_gemm_a4w4_kernels_per_call(M, N, K))
 
 
 def _cpu_sample(M, N, K, rows, seed=0):

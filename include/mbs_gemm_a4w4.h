@@ -79,6 +79,15 @@ int gemm_a4w4_mxfp4_launch(const uint8_t* A, const uint8_t* B, const uint8_t* AS
 size_t mbs_gemm_a4w4_workspace_size(int M, int N, int K);
 
 /*
+ * Kernels one mbs_gemm_a4w4_launch_ws / gemm_a4w4_mxfp4_launch call of this
+ * shape launches on the current device (2 on the CTA-pair path: the
+ * scale-image pass and the GEMM; 1 otherwise).  Host-only, no CUDA work; -1
+ * for a non-positive size.  No reference counterpart (the reference launches
+ * one kernel per call).
+ */
+int mbs_gemm_a4w4_kernels_per_call(int M, int N, int K);
+
+/*
  * Workspace layout shared by every schedule: the first
  * MBS_GEMM_WS_FLAG_BYTES bytes hold the stream-K completion flags (one word
  * per CTA), which must be zero when a launch starts; the rest is per-launch

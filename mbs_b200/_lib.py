@@ -20,6 +20,7 @@ SIGNATURES = {
     "mbs_last_error_message": (_c_char_p, []),
     "gemm_a4w4_mxfp4_launch": (_c_int, [_c_void_p] * 7 + [_c_int] * 5 + [_c_void_p]),
     "mbs_gemm_a4w4_workspace_size": (_c_size_t, [_c_int] * 3),
+    "mbs_gemm_a4w4_kernels_per_call": (_c_int, [_c_int] * 3),
     "mbs_gemm_a4w4_launch_ws": (_c_int, [_c_void_p] * 7 + [_c_int] * 5 + [_c_void_p, _c_size_t,
                                                                            _c_void_p]),
     "mbs_gemm_a4w4_launch_noalloc": (_c_int, [_c_void_p] * 7 + [_c_int] * 5 + [_c_void_p]),

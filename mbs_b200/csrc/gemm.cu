@@ -381,6 +381,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // Programmatic dependent launch: this grid may have started while the
+    // kernel ahead of it in the stream was still running.  Every thread waits
+    // for that kernel here, before its first global-memory access (a no-op
+    // for a plain launch), then lets the next kernel start its prologue on
+    // the SMs this grid frees.
+    griddep_wait();
+    griddep_launch_dependents();
 
     if (warp == 0)
     {
@@ -1656,6 +1663,15 @@ bool pair_pdl_enabled()
     return on;
 }
 
+// The single-CTA GEMM may start while the kernel before it in the stream
+// finishes (programmatic dependent launch); MBS_PDL=0 launches it in plain
+// stream order.
+bool pdl_enabled()
+{
+    static const bool on = env_int("MBS_PDL", 1) != 0;
+    return on;
+}
+
 // Workspace of the CTA-pair path: the A and B scale images.
 size_t pair_image_a_bytes(int M, int K)
 {
@@ -2050,11 +2066,15 @@ int launch_cfg(const Problem& pb, const Plan& pl, const DeviceInfo& dev, void* w
     cfg.blockDim = dim3(NUM_THREADS);
     cfg.dynamicSmemBytes = CF::SMEM_BYTES;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeCooperative;  // stream-K owners wait on other CTAs
     attr[0].val.cooperative = pl.sk ? 1 : 0;
+    // may start while the previous kernel in the stream finishes (the kernel
+    // waits for it before touching global memory)
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = pdl_enabled() ? 2 : 1;
     st = record_before(stream);
     if (st) return st;
     cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, tm_r, tm_c, tm_rsf, tm_csf, p);
@@ -2242,6 +2262,24 @@ extern "C" size_t mbs_gemm_a4w4_workspace_size(int M, int N, int K)
     }
     if (M <= 0 || N <= 0 || K <= 0) return 0;
     return mbs::gemm::make_plan(M, N, K, num_sms).ws_bytes;
+}
+
+extern "C" int mbs_gemm_a4w4_kernels_per_call(int M, int N, int K)
+{
+    if (M <= 0 || N <= 0 || K <= 0) return -1;
+    int num_sms = 148;
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess)
+    {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && n > 0)
+            num_sms = n;
+    }
+    else
+    {
+        cudaGetLastError();
+    }
+    return mbs::gemm::make_plan(M, N, K, num_sms).pair ? 2 : 1;
 }
 
 extern "C" int mbs_gemm_a4w4_launch_ws(const uint8_t* A, const uint8_t* B, const uint8_t* AScale,

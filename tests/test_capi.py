@@ -99,6 +99,14 @@ def test_workspace_size_is_host_only(lib):
     assert lib.mbs_gemm_a4w4_workspace_size(0, 16, 64) == 0
 
 
+def test_kernels_per_call_is_host_only(lib):
+    # the CTA-pair path adds its scale-image pass; decode and small shapes launch one kernel
+    assert lib.mbs_gemm_a4w4_kernels_per_call(8192, 8192, 8192) == 2
+    assert lib.mbs_gemm_a4w4_kernels_per_call(16, 57344, 8192) == 1
+    assert lib.mbs_gemm_a4w4_kernels_per_call(256, 512, 1024) == 1
+    assert lib.mbs_gemm_a4w4_kernels_per_call(0, 16, 64) == -1
+
+
 def test_workspace_flag_region_matches_header():
     from mbs_b200 import mbs_gemm_a4w4
     hdr = open(os.path.join(REPO, "include", "mbs_gemm_a4w4.h")).read()
