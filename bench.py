@@ -313,26 +313,44 @@ def run_mbs(args):
         if world > 1:
             dist.destroy_process_group()
         return
-    # e2e: public operator on host operands (pinned), copies inside the timed region
+    # e2e: public operator on host operands (pinned), copies inside the timed
+    # region.  Consecutive steps alternate between two streams, each with its
+    # own device and host buffers, so one step's result copy (device to host)
+    # overlaps the next step's operand copies (host to device) on the other
+    # copy engine, as a serving loop would run them.
     hA, hB = A.cpu().pin_memory(), B.cpu().pin_memory()
     hAs, hBs = As.cpu().pin_memory(), Bs.cpu().pin_memory()
-    hout = torch.empty((M, N), dtype=torch.bfloat16).pin_memory()
-    dA, dB, dAs, dBs = (torch.empty_like(t, device=dev) for t in (hA, hB, hAs, hBs))
+    lanes = []
+    for _ in range(2):
+        lanes.append({
+            "stream": torch.cuda.Stream(dev),
+            "dev": [torch.empty_like(t, device=dev) for t in (hA, hB, hAs, hBs)],
+            "out": torch.empty(((M + 31) // 32 * 32, N), dtype=torch.bfloat16, device=dev),
+            "hout": torch.empty((M, N), dtype=torch.bfloat16).pin_memory(),
+        })
 
-    def e2e_step():
-        dA.copy_(hA, non_blocking=True)
-        dB.copy_(hB, non_blocking=True)
-        dAs.copy_(hAs, non_blocking=True)
-        dBs.copy_(hBs, non_blocking=True)
-        o = mbs_b200.gemm_a4w4(dA, dB, dAs, dBs)
-        hout.copy_(o, non_blocking=True)
+    def e2e_step(i):
+        ln = lanes[i % 2]
+        with torch.cuda.stream(ln["stream"]):
+            dA, dB, dAs, dBs = ln["dev"]
+            dA.copy_(hA, non_blocking=True)
+            dB.copy_(hB, non_blocking=True)
+            dAs.copy_(hAs, non_blocking=True)
+            dBs.copy_(hBs, non_blocking=True)
+            o = mbs_b200.gemm_a4w4(dA, dB, dAs, dBs, out=ln["out"])
+            ln["hout"].copy_(o, non_blocking=True)
 
-    e2e_step()
+    e2e_step(0)
+    e2e_step(1)
     torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record(stream)
-    for _ in range(args.e2e_steps):
-        e2e_step()
+    for ln in lanes:
+        ln["stream"].wait_event(ev0)
+    for i in range(args.e2e_steps):
+        e2e_step(i)
+    for ln in lanes:
+        stream.wait_stream(ln["stream"])
     ev1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = ev0.elapsed_time(ev1) / args.e2e_steps
@@ -340,6 +358,7 @@ def run_mbs(args):
         t = torch.tensor([e2e_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
+    hout = lanes[0]["hout"]
     h2d = sum(t.numel() * t.element_size() for t in (hA, hB, hAs, hBs))
     d2h = hout.numel() * hout.element_size()
 
