@@ -78,6 +78,9 @@ struct Params
     float alpha;                  // output scale (1 = none)
     const __nv_bfloat16* bias;    // [N] added to every output row, or null
     int out_v8;                   // 1: `out` is 32-byte aligned, rows are stored 32 bytes per instruction
+    int wide_c;                   // CTA pairs, 384-column configuration: column tiles [0, wide_c) are
+                                  // 384 wide, the rest (up to tiles_c) 256 wide
+    int img_b_blocks;             // ... 128-row blocks per K stage of the B scale images
 };
 
 constexpr int align_up(int x, int a) { return (x + a - 1) / a * a; }
@@ -1202,15 +1205,24 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) __cluster_dims__(2, 1, 1)
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
     const int tiles_r2 = (p.M + 2 * BM - 1) / (2 * BM);
-    const int tiles_c = (p.N + BN - 1) / BN;
+    // Column tiles: all BN wide, or, in the 384-column configuration, the
+    // first p.wide_c 384 wide and the rest 256 wide (a 256-wide tile issues
+    // only the N = 256 MMA and skips the second MMA's B rows), so that the
+    // rounds of tiles over the clusters come out even.
+    const int tiles_c = CF::N2 ? p.tiles_c : (p.N + BN - 1) / BN;
     const int ntiles = tiles_r2 * tiles_c;
+    auto col0 = [&](int tc) {
+        return CF::N2 ? (tc < p.wide_c ? tc * 384 : p.wide_c * 384 + (tc - p.wide_c) * 256) : tc * BN;
+    };
+    auto is_wide = [&](int tc) { return CF::N2 != 0 && tc < p.wide_c; };
 
     if (warp == 0)
     {
         if (lane == 0)
         {
             const uint32_t full0 = mapa_shared(smem_u32(full), 0);  // leader's full[0]
-            const int a_blocks = tiles_r2 * 2, b_blocks = tiles_c * CF::B_BLOCKS;  // image blocks per K stage
+            // image blocks per K stage
+            const int a_blocks = tiles_r2 * 2, b_blocks = CF::N2 ? p.img_b_blocks : tiles_c * CF::B_BLOCKS;
             int slot = 0;
             uint32_t phase = 0;
 #if MBS_TIMING
@@ -1230,7 +1242,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) __cluster_dims__(2, 1, 1)
                 const uint32_t fbar = full0 + (g % STAGES) * 8;
                 tma_load_2d_pair(st + CF::A_IMG_OFF, &tm_ia, fbar, 0, (ks * a_blocks + rb) * (IMG_BLOCK / 256));
                 tma_load_2d_pair(st + CF::B_IMG_OFF, &tm_ib, fbar, 0,
-                                 (ks * b_blocks + tc * CF::B_BLOCKS) * (IMG_BLOCK / 256));
+                                 (ks * b_blocks + col0(tc) / 128) * (IMG_BLOCK / 256));
             };
             int g = 0;  // stage index in this cluster's sequence
             for (int t = cluster; t < ntiles; t += nclusters)
@@ -1238,8 +1250,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) __cluster_dims__(2, 1, 1)
                 const int tr = t % tiles_r2, tc = t / tiles_r2;
                 const int rb = tr * 2 + (int)rank;  // this CTA's 128-row block of A
                 // this CTA's B rows: half of the N = 256 MMA's, half of the N = 128 MMA's
-                const int nb1 = tc * BN + (int)rank * CF::B1_ROWS;
-                const int nb2 = tc * BN + 256 + (int)rank * CF::B2_ROWS;
+                const int nb1 = col0(tc) + (int)rank * CF::B1_ROWS;
+                const int nb2 = col0(tc) + 256 + (int)rank * CF::B2_ROWS;
+                const bool wide = is_wide(tc);
                 for (int ks = 0; ks < p.k_stages; ++ks, ++g)
                 {
                     if (g == STAGES)
@@ -1260,10 +1273,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) __cluster_dims__(2, 1, 1)
                     }
                     uint8_t* st = smem + slot * CF::STAGE_BYTES;
                     const uint32_t fbar = full0 + slot * 8;
-                    if (leader) mbar_arrive_expect_tx(&full[slot], 2 * CF::TX);
+                    if (leader) mbar_arrive_expect_tx(&full[slot], 2 * (wide ? CF::TX : CF::TX - CF::B2_DATA));
                     tma_load_2d_pair(st + CF::A_DATA_OFF, &tm_a, fbar, ks * BKB, rb * BM);
                     tma_load_3d_pair(st + CF::B1_DATA_OFF, &tm_b, fbar, 0, nb1 / 16, ks * 8);
-                    if (CF::N2) tma_load_3d_pair(st + CF::B2_DATA_OFF, &tm_b2, fbar, 0, nb2 / 16, ks * 8);
+                    if (wide) tma_load_3d_pair(st + CF::B2_DATA_OFF, &tm_b2, fbar, 0, nb2 / 16, ks * 8);
                     if (g >= STAGES) load_images(g);
 #if MBS_TIMING
                     tacc[10] += 1;
@@ -1297,6 +1310,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) __cluster_dims__(2, 1, 1)
 #endif
             for (int t = cluster; t < ntiles; t += nclusters)
             {
+                const bool wide = is_wide(t / tiles_r2);
                 bool ok_acc;
                 {
                     MBS_TSTART();
@@ -1349,7 +1363,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) __cluster_dims__(2, 1, 1)
                             make_smem_desc(b1_base + j * 2 * (CF::B1_ROWS * 16), CF::B1_ROWS * 16, 128, 0);
                         tc_mma_mxf4_pair(tmem_base, a_desc, b1_desc, make_idesc_mxf4(2 * BM, 256, id, id), sfa,
                                          (sf_a + CF::SFB1_OFF + 8 * q) | (id << 30), acc);
-                        if (CF::N2)
+                        if (wide)
                         {
                             const uint64_t b2_desc =
                                 make_smem_desc(b2_base + j * 2 * (CF::B2_ROWS * 16), CF::B2_ROWS * 16, 128, 0);
@@ -1468,7 +1482,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) __cluster_dims__(2, 1, 1)
         {
             const int tr = t % tiles_r2, tc = t / tiles_r2;
             const int r0 = tr * 2 * BM + (int)rank * BM;
-            const int c0 = tc * BN;
+            const int c0 = col0(tc);
+            const int c_end = c0 + (CF::N2 && !is_wide(tc) ? 256 : BN);  // columns this tile computes
             if (has_factor || has_bias)
             {
                 named_bar_sync(1, NUM_EPI_THREADS);
@@ -1557,7 +1572,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) __cluster_dims__(2, 1, 1)
                 for (int ch = 0; ch < NCH; ++ch)
                 {
                     const int n = c0 + half * COLS + ch * 16;
-                    if (n < p.N)
+                    if (n < p.N && n < c_end)
                     {
                         if (p.out_v8)
                         {
@@ -1620,7 +1635,9 @@ struct Plan
     int bn;
     int r_rows;  // rows of A loaded per stage (non-swapped single-CTA path)
     bool swap, sk, pair;
-    int pair_bn;  // CTA-pair tile columns (256 or 384)
+    int pair_bn;  // CTA-pair configuration: 256-column tiles, or 384 (mixed with 256)
+    int pair_tiles_c, pair_wide_c;  // ... column tiles, of which the first pair_wide_c 384 wide
+    int pair_img_b_blocks;          // ... 128-row B scale image blocks per K stage
     int G, tiles_r, tiles_c, k_stages;
     size_t ws_bytes;
 };
@@ -1679,11 +1696,6 @@ size_t pair_image_a_bytes(int M, int K)
     return blocks * ((K + BK - 1) / BK) * IMG_BLOCK;
 }
 
-size_t pair_image_b_bytes(int N, int K, int pair_bn)
-{
-    const size_t blocks = (size_t)((N + pair_bn - 1) / pair_bn) * (pair_bn / 128);
-    return blocks * ((K + BK - 1) / BK) * IMG_BLOCK;
-}
 
 struct Plan;
 size_t sk_partial_bytes(const Plan& pl);
@@ -1759,17 +1771,56 @@ Plan make_plan(int M, int N, int K, int num_sms, bool packed = false)
     if (pl.pair)
     {
         // 384-column tiles do 1.5x the MMA work of 256-column ones for 1.26x
-        // the bytes and measure ~1.39x the time, but come in coarser rounds
-        // over the clusters: take the width with the smaller (rounds of tiles
-        // per cluster) x (time per tile).  MBS_PAIR_BN=256/384 overrides.
+        // the bytes and measure ~1.39x the time.  Two configurations: all
+        // tiles 256 wide (6 pipeline stages), or nw 384-wide column tiles
+        // followed by 256-wide ones (5 stages of 44 KB; a 256-wide tile
+        // there measures ~1.1x a 256-wide tile of the first).  Tiles go to
+        // the clusters round-robin, wide ones first; take the layout whose
+        // busiest cluster has the least work.  MBS_PAIR_BN=256 / 384 forces
+        // all-256 / all-384 tiles, MBS_PAIR_WIDE=nw a given mix.
         const int c = G / 2;
-        const long long t3 = tr2 * ((N + 383) / 384);
-        const double cost256 = (double)((t2 + c - 1) / c);
-        const double cost384 = (double)((t3 + c - 1) / c) * 1.39;
         const int force_bn = env_int("MBS_PAIR_BN", 0);
-        pl.pair_bn = force_bn == 256 || force_bn == 384 ? force_bn : (cost384 < cost256 ? 384 : 256);
-        const long long tp = pl.pair_bn == 384 ? t3 : t2;
-        const size_t ia = pair_image_a_bytes(M, K), ib = pair_image_b_bytes(N, K, pl.pair_bn);
+        const int force_wide = env_int("MBS_PAIR_WIDE", 0);
+        auto busiest = [&](long long T, long long A, double w_wide, double w_narrow) {
+            double mx = 0;
+            const long long cl = T < c ? T : c;
+            for (long long k = 0; k < cl; ++k)
+            {
+                const long long n_k = (T - 1 - k) / c + 1;
+                const long long a_k = k < A ? (A - 1 - k) / c + 1 : 0;
+                const double load = (double)a_k * w_wide + (double)(n_k - a_k) * w_narrow;
+                if (load > mx) mx = load;
+            }
+            return mx;
+        };
+        const double cost256 = busiest(t2, 0, 1.0, 1.0);
+        double best = 1e300;
+        int best_nw = 0, best_nn = 0;
+        const int max_wide = (N + 383) / 384;
+        for (int nw = 1; nw <= max_wide; ++nw)
+        {
+            const int rest = N - nw * 384;
+            const int nn = rest > 0 ? (rest + 255) / 256 : 0;
+            if (force_wide > 0 && nw != (force_wide < max_wide ? force_wide : max_wide)) continue;
+            if (force_bn == 384 && nw != max_wide) continue;
+            const double cost = busiest(tr2 * (nw + nn), tr2 * nw, 1.39, 1.1);
+            if (cost < best)
+            {
+                best = cost;
+                best_nw = nw;
+                best_nn = nn;
+            }
+        }
+        const bool use384 = force_bn == 384 || force_wide > 0 || (force_bn != 256 && best < cost256);
+        pl.pair_bn = use384 ? 384 : 256;
+        pl.pair_wide_c = use384 ? best_nw : 0;
+        pl.pair_tiles_c = use384 ? best_nw + best_nn : (N + 255) / 256;
+        const long long tp = tr2 * pl.pair_tiles_c;
+        // B scale images: whole tiles of 128-row blocks, plus one block so the
+        // last 256-wide tile's 3-block image box stays inside the buffer
+        pl.pair_img_b_blocks = use384 ? (best_nw * 384 + best_nn * 256) / 128 + 1 : pl.pair_tiles_c * 2;
+        const size_t ia = pair_image_a_bytes(M, K);
+        const size_t ib = (size_t)pl.pair_img_b_blocks * pl.k_stages * IMG_BLOCK;
         // TMA row coordinates of the images are 32-bit
         if (ia / 256 < (size_t)INT32_MAX && ib / 256 < (size_t)INT32_MAX)
         {
@@ -1964,7 +2015,7 @@ int launch_pair(const Problem& pb, const Plan& pl, const DeviceInfo& dev, void* 
         }
     }
     const size_t ia = pair_image_a_bytes(pb.M, pb.K);
-    const size_t ib = pair_image_b_bytes(pb.N, pb.K, CF::BN);
+    const size_t ib = (size_t)pl.pair_img_b_blocks * pl.k_stages * IMG_BLOCK;
     uint8_t* img_a = static_cast<uint8_t*>(ws) + kFlagBytes;
     uint8_t* img_b = img_a + ia;
     CUtensorMap tm_a, tm_b, tm_b2, tm_ia, tm_ib;
@@ -1995,6 +2046,9 @@ int launch_pair(const Problem& pb, const Plan& pl, const DeviceInfo& dev, void* 
     p.out_v8 = (reinterpret_cast<uintptr_t>(pb.out) & 31) == 0 ? 1 : 0;  // rows are N * 2 bytes, N % 16 == 0
     p.alpha = pb.alpha;
     p.bias = static_cast<const __nv_bfloat16*>(pb.bias);
+    p.tiles_c = pl.pair_tiles_c;
+    p.wide_c = pl.pair_wide_c;
+    p.img_b_blocks = pl.pair_img_b_blocks;
     p.err = device_error_word(dev.device);
     if (p.err == nullptr) return fail(MBS_ERR_CUDA, "device error word unavailable");
     cudaLaunchConfig_t cfg = {};

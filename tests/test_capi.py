@@ -85,9 +85,10 @@ def test_workspace_size_is_host_only(lib):
     # per 256-element K stage; B's blocks cover whole pair tiles)
     assert lib.mbs_gemm_a4w4_workspace_size(16, 57344, 8192) > 0
     # flag words first, then the pair path's A and B scale images: 8192^3
-    # takes 384-column pair tiles on 148 SMs (10 rounds of 74 clusters x 1.39
-    # against 14 rounds of 256-column tiles), so B's blocks cover 22 tiles x 3
-    assert lib.mbs_gemm_a4w4_workspace_size(8192, 8192, 8192) == 4096 + 64 * 32 * 1024 + 66 * 32 * 1024
+    # takes 18 column tiles 384 wide and 5 tiles 256 wide (the busiest of 74
+    # clusters does 8 wide + 2 narrow tiles, against 14 tiles of 256 or 10 of
+    # 384), so B's images cover 8192 / 128 = 64 blocks, plus one
+    assert lib.mbs_gemm_a4w4_workspace_size(8192, 8192, 8192) == 4096 + 64 * 32 * 1024 + 65 * 32 * 1024
     # 256-column tiles where both widths take one round: 2048 x 2048 x 1024
     # is 64 tiles of 256 columns (8 x 2 B blocks per stage) against 48 of 384
     assert lib.mbs_gemm_a4w4_workspace_size(2048, 2048, 1024) == 4096 + 16 * 4 * 1024 + 16 * 4 * 1024

@@ -16,6 +16,7 @@ pytestmark = pytest.mark.gpu
 SCHEDULES = {
     "pair": dict(MBS_FORCE_SCHEDULE="2", MBS_FORCE_PAIR="1", MBS_PAIR_BN="256"),  # CTA pairs
     "pair384": dict(MBS_FORCE_SCHEDULE="2", MBS_FORCE_PAIR="1", MBS_PAIR_BN="384"),
+    "pair_mix": dict(MBS_FORCE_SCHEDULE="2", MBS_FORCE_PAIR="1", MBS_PAIR_WIDE="1"),
     "dp_single": dict(MBS_FORCE_SCHEDULE="2", MBS_FORCE_PAIR="0"),
     "stream_k": dict(MBS_FORCE_SCHEDULE="1", MBS_FORCE_GRID="17"),
     "swap": dict(MBS_FORCE_SWAP="1"),
@@ -24,7 +25,8 @@ SCHEDULES = {
 
 @pytest.fixture
 def env():
-    keys = ("MBS_FORCE_SCHEDULE", "MBS_FORCE_GRID", "MBS_FORCE_PAIR", "MBS_FORCE_SWAP", "MBS_PAIR_BN")
+    keys = ("MBS_FORCE_SCHEDULE", "MBS_FORCE_GRID", "MBS_FORCE_PAIR", "MBS_FORCE_SWAP", "MBS_PAIR_BN",
+            "MBS_PAIR_WIDE")
     saved = {k: os.environ.get(k) for k in keys}
     yield os.environ
     for k, v in saved.items():
@@ -35,6 +37,7 @@ def env():
 
 
 @pytest.mark.parametrize("sched,M,N,K", [("pair", 512, 512, 1024), ("pair384", 300, 1040, 1024),
+                                         ("pair_mix", 300, 1040, 1024),
                                          ("dp_single", 200, 768, 512),
                                          ("stream_k", 40, 2048, 2048), ("swap", 24, 1024, 512)])
 @pytest.mark.parametrize("alpha,with_bias", [(0.5, False), (-3.25, True), (1.0, True), (7.0, True)])

@@ -100,21 +100,27 @@ def test_one_workspace_serves_every_schedule(force_env):
         assert_gemm_close(out, ref, bound, f"step {i} {M}x{N}x{K} {env}")
 
 
-@pytest.mark.parametrize("bn", [256, 384])
+@pytest.mark.parametrize("bn", [256, 384, "mix"])
 @pytest.mark.parametrize("M,N,K,macro,grid", [(512, 1024, 2048, False, 0), (300, 1024, 1088, False, 0),
                                               (256, 1040, 512, False, 0), (512, 1024, 2048, True, 0),
                                               (700, 768, 1600, True, 0), (1000, 2000, 768, False, 6)])
 def test_cta_pair_path(force_env, M, N, K, macro, grid, bn):
-    """The CTA-pair kernel at both tile widths (256 columns; 384 as an N=256
-    plus an N=128 MMA): ragged M (rows past M are computed from padding and
-    never stored), ragged N inside a tile's second MMA, a partial last K
-    stage, both B scale layouts, and several tiles per cluster."""
+    """The CTA-pair kernel with all tiles 256 columns wide, all 384 (an N=256
+    plus an N=128 MMA), and mixed (one 384-wide column tile, then 256-wide
+    ones in the 384-column configuration): ragged M (rows past M are computed
+    from padding and never stored), ragged N inside a tile's second MMA and
+    inside a narrow tile, a partial last K stage, both B scale layouts, and
+    several tiles per cluster."""
     import mbs_b200
-    env = dict(MBS_FORCE_SCHEDULE=2, MBS_FORCE_PAIR=1, MBS_PAIR_BN=bn)
+    env = dict(MBS_FORCE_SCHEDULE=2, MBS_FORCE_PAIR=1)
+    if bn == "mix":
+        env["MBS_PAIR_WIDE"] = 1
+    else:
+        env["MBS_PAIR_BN"] = bn
     if grid:
         env["MBS_FORCE_GRID"] = grid
     force_env(**env)
-    c = Case(M, N, K, seed=M + K + bn, factors=True, macro=macro)
+    c = Case(M, N, K, seed=M + K + (1 if bn == "mix" else bn), factors=True, macro=macro)
     if macro:
         out = mbs_b200.gemm_a4w4_macro(c.A, c.B, c.A_scale, c.B_scale, c.A_factor, c.B_factor)
     else:
