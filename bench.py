@@ -553,9 +553,10 @@ def run_sharded(args):
             "quant_gemm_ms": round(local_ms, 4),
             "quant_gemm_tflops": round(flops / world / (local_ms * 1e-3) / 1e12 * world, 2),
             "exposed_exchange_ms": round(total_ms - local_ms, 4),
-            "exchange": ("NCCL all-gather" if chunks == 1 else
+            "exchange": "none (one rank holds the whole output)" if world == 1 else
+                        ("NCCL all-gather" if chunks == 1 else
                          f"{chunks} row chunks, NCCL send/recv overlapped with the next chunk's GEMM "
-                         f"({args.comm_sms} SMs left to NCCL)") if exchange == "nccl" or world == 1 else
+                         f"({args.comm_sms} SMs left to NCCL)") if exchange == "nccl" else
                         f"{chunks} row chunks pushed into the peers' buffers by copy engines (CUDA IPC), "
                         f"overlapped with the next chunk's GEMM",
             "bytes_received_per_rank": (world - 1) * M * nl * 2,

@@ -125,6 +125,9 @@ class ShardedA4W4:
             return self._forward_pipelined(x, A_factor, layout, chunks, comm_sms)
         c = self.local(x, A_factor).contiguous()
         M, nl = c.shape
+        if self.world == 1:
+            # nothing to exchange: the local block is the whole output
+            return c.view(1, M, nl) if layout == "blocked" else c
         flat = torch.empty((self.world * M, nl), dtype=c.dtype, device=c.device)
         dist.all_gather_into_tensor(flat, c, group=self.group)
         gathered = flat.view(self.world, M, nl)
