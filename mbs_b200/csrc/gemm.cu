@@ -751,23 +751,36 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                             float4 a[U];
 #pragma unroll
                             for (int u = 0; u < U; ++u) a[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-                            for (int cc = c_first; cc <= c_last; ++cc)
+                            // two contributors per round trip: both sets of loads are in
+                            // flight before the adds, which keep the contributors' order
+                            for (int cc = c_first; cc <= c_last; cc += 2)
                             {
-                                const float4* src = part4 + (size_t)cc * N4;
-                                float4 b[U];
+                                const bool two = cc + 1 <= c_last;
+                                const float4* src0 = part4 + (size_t)cc * N4;
+                                const float4* src1 = part4 + (size_t)(two ? cc + 1 : cc) * N4;
+                                float4 b0[U], b1[U];
 #pragma unroll
                                 for (int u = 0; u < U; ++u)
                                 {
                                     const int e4 = base + u * NUM_EPI_THREADS;
-                                    b[u] = e4 < N4 ? __ldcg(src + e4) : make_float4(0.f, 0.f, 0.f, 0.f);
+                                    const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+                                    b0[u] = e4 < N4 ? __ldcg(src0 + e4) : z;
+                                    b1[u] = (two && e4 < N4) ? __ldcg(src1 + e4) : z;
                                 }
 #pragma unroll
                                 for (int u = 0; u < U; ++u)
                                 {
-                                    a[u].x += b[u].x;
-                                    a[u].y += b[u].y;
-                                    a[u].z += b[u].z;
-                                    a[u].w += b[u].w;
+                                    a[u].x += b0[u].x;
+                                    a[u].y += b0[u].y;
+                                    a[u].z += b0[u].z;
+                                    a[u].w += b0[u].w;
+                                    if (two)
+                                    {
+                                        a[u].x += b1[u].x;
+                                        a[u].y += b1[u].y;
+                                        a[u].z += b1[u].z;
+                                        a[u].w += b1[u].w;
+                                    }
                                 }
                             }
 #pragma unroll
