@@ -491,15 +491,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 bool ok = true;
                 for (int ks = w.k0; ks < w.k1; ++ks)
                 {
-                    bool ok_full, ok_sf;
+                    // `sfready` implies `full`: both transposer warps arrive on it
+                    // only after their own wait on this stage's `full` (release /
+                    // acquire through the two barriers), so one barrier test per
+                    // stage suffices here.
+                    bool ok_sf;
                     {
                         MBS_TSTART();
-                        ok_full = mbar_wait(&full[slot], phase, abort_flag);
-                        MBS_TADD(tacc, 2);
-                    }
-                    {
-                        MBS_TSTART();
-                        ok_sf = ok_full && mbar_wait(&sfready[slot], phase, abort_flag);
+                        ok_sf = mbar_wait(&sfready[slot], phase, abort_flag);
                         MBS_TADD(tacc, 3);
                     }
                     if (!ok_sf)
