@@ -283,6 +283,37 @@ def test_prefill_8192_cubed_sampled_and_scale_property():
     assert_gemm_close(out[tr][:, tcol], ref, bound, "8192^3")
 
 
+def test_config3_macro_full_size_sampled():
+    """BASELINE config[3] at full size (4096 x 7168 x 18432; macro-block B
+    scales, N(0, 0.02) weights, activations with 1 % x20 outliers, MBS
+    factors): the planner's own mixed 384/256-column CTA-pair layout, parity
+    on a 128 x 128 sample of rows and columns."""
+    import mbs_b200
+    M, N, K = 4096, 7168, 18432
+    g = torch.Generator(device="cuda").manual_seed(33)
+    x = torch.randn(M, K, device="cuda", generator=g)
+    x = torch.where(torch.rand(M, K, device="cuda", generator=g) < 0.01, x * 20, x).to(torch.bfloat16)
+    w = (torch.randn(N, K, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    qa, sa_sh = mbs_b200.quantize_mxfp4(x, shuffle=True)
+    _, sa = mbs_b200.quantize_mxfp4(x, shuffle=False)
+    qw, mb = mbs_b200.quantize_mxfp4_macro(w)
+    del x, w
+    B = mbs_b200.shuffle_weight(qw)
+    fa = torch.randint(0, 256, (M,), dtype=torch.uint8, device="cuda", generator=g)
+    fb = torch.randint(0, 256, (N,), dtype=torch.uint8, device="cuda", generator=g)
+    out = mbs_b200.gemm_a4w4_macro(qa, B, sa_sh, mb, fa, fb)
+    torch.cuda.synchronize()
+    rows = np.sort(np.random.default_rng(3).choice(M, 128, replace=False))
+    cols = np.sort(np.random.default_rng(4).choice(N, 128, replace=False))
+    tr, tcol = torch.from_numpy(rows).cuda(), torch.from_numpy(cols).cuda()
+    sb = O.expand_macro_scales(mb.cpu().numpy(), N, K)[cols]
+    qa_s, qw_s, sa_s = qa[tr].cpu().numpy(), qw[tcol].cpu().numpy(), sa[tr].cpu().numpy()
+    ref = O.gemm_ref(qa_s, qw_s, sa_s, sb, fa[tr].cpu().numpy().reshape(-1, 1),
+                     fb[tcol].cpu().numpy().reshape(-1, 1))
+    bound = O.gemm_abs_bound(qa_s, qw_s, sa_s, sb)
+    assert_gemm_close(out[tr][:, tcol], ref, bound, "config[3] full size")
+
+
 @pytest.mark.parametrize("M,N,K", [(256, 512, 1024), (33, 96, 576), (8, 256, 512)])
 def test_macro_block_variant(M, N, K):
     import mbs_b200
