@@ -119,6 +119,10 @@ __device__ __forceinline__ int64_t flat_s(int r, int b, int snp)
 // empty block.
 constexpr int QUANT_UNROLL = 4;
 constexpr int QUANT_THREADS = 256;
+// CTAs per SM the register budget must allow: each holds its row's loads in
+// registers, so the rows in flight per SM (and the MBS variant, which waits
+// for a CTA-wide row max, most of all) scale with it
+constexpr int QUANT_MIN_CTAS = 6;
 
 // MBS = true: each row is first reduced to its max |x| (one read of the row,
 // kept in L2 for the second), its factor byte b is written to `factors`, and
@@ -207,7 +211,7 @@ __device__ __forceinline__ float mbs_row_multiplier(uint32_t am, int r, uint8_t*
 // of up to QUANT_THREADS * QUANT_UNROLL octets (K <= 8192) stays in registers
 // between the two steps; longer rows are read twice (the second read from L2).
 template <bool MBS>
-__global__ void __launch_bounds__(QUANT_THREADS) quantize_1x32_kernel(const uint16_t* __restrict__ x,
+__global__ void __launch_bounds__(QUANT_THREADS, QUANT_MIN_CTAS) quantize_1x32_kernel(const uint16_t* __restrict__ x,
                                                                       int rows, int K, int ld_x,
                                                                       uint8_t* __restrict__ q,
                                                                       uint8_t* __restrict__ sc, int shuffled,
