@@ -81,6 +81,7 @@ struct Params
     int wide_c;                   // CTA pairs, 384-column configuration: column tiles [0, wide_c) are
                                   // 384 wide, the rest (up to tiles_c) 256 wide
     int img_b_blocks;             // ... 128-row blocks per K stage of the B scale images
+    int ksplit;                   // single-CTA kernel, > 1: cluster split-K over clusters of ksplit CTAs
 };
 
 constexpr int align_up(int x, int a) { return (x + a - 1) / a * a; }
@@ -145,6 +146,11 @@ struct Cfg
     static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + EPI_BYTES + 1024;  // +1024 alignment slack
     static_assert(SMEM_BYTES <= 232448, "shared memory budget");
     static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN");
+
+    // Cluster split-K: a CTA's buffer of S partial slices (S <= 8, each
+    // 128 / S rows + 1 pad row of BN / 4 16-byte column groups) lives in the
+    // idle pipeline stages.
+    static constexpr bool SPLIT_OK = !SWAP && R_ROWS == 128 && (BM + 8) * (BN / 4) * 16 <= STAGES * STAGE_BYTES;
 };
 
 // ------------------------------------------------------------------ schedule
@@ -179,6 +185,18 @@ __device__ __forceinline__ int sk_last_starting_before(const Params& p, long lon
 // idx-th work item of this CTA; false when exhausted.
 __device__ __forceinline__ bool get_work(const Params& p, int idx, Work& w)
 {
+    if (p.ksplit > 1)
+    {
+        // cluster split-K: the ksplit CTAs of a cluster (consecutive blockIdx.x,
+        // cluster rank = blockIdx.x % ksplit) share one tile, rank r taking K
+        // stages [r * k_stages / ksplit, (r + 1) * k_stages / ksplit)
+        if (idx > 0) return false;
+        const int rank = (int)(blockIdx.x % (unsigned)p.ksplit);
+        w.tile = (int)(blockIdx.x / (unsigned)p.ksplit);
+        w.k0 = (int)muldiv(rank, p.k_stages, p.ksplit);
+        w.k1 = (int)muldiv(rank + 1, p.k_stages, p.ksplit);
+        return true;
+    }
     if (!p.sk)
     {
         const long long t = (long long)blockIdx.x + (long long)idx * gridDim.x;
@@ -222,6 +240,8 @@ __device__ __forceinline__ void raise_error(const Params& p, volatile int* abort
 //   6 epilogue waits on `acc_full`   7 epilogue work
 //   8 stream-K owner flag wait       9 CTA lifetime (thread 0)
 //  10 stages issued (producer)      11 MMA issue work
+//  12 split-K: first cluster barrier 13 split-K: push + second barrier
+//  14 kernel start -> past griddep_wait  15 split-K: finish
 #ifndef MBS_TIMING
 #define MBS_TIMING 0
 #endif
@@ -323,6 +343,153 @@ __device__ __forceinline__ void transpose_side(const uint8_t* raw, uint8_t* atom
     }
 }
 
+// Cluster split-K.  Cluster rank r finishes rows [r R, (r + 1) R) of the
+// tile, R = 128 / S.  Each CTA's buffer (in its pipeline stages, idle once
+// the whole cluster holds complete accumulators) has S slots, slot s holding
+// rank s's partial of the rows this CTA finishes, stored by 16-byte column
+// group q and row: group (s, q) is R + 1 rows of 16 bytes, so
+//   byte offset of (slot s, group q, row lr) = ((s * BN/4 + q) * (R + 1) + lr) * 16.
+// A warp storing its 32 accumulator rows' group q writes 512 contiguous
+// bytes (stores into another CTA's shared memory move in packets; 16-byte
+// pieces scattered over rows ran ~3x slower), and a warp reading 32
+// consecutive groups of one row steps by R + 1 rows: distinct banks.
+__device__ __forceinline__ int split_off(int s, int q, int lr, int rows, int c4)
+{
+    return ((s * c4 + q) * (rows + 1) + lr) * 16;
+}
+
+// The hand-over (epilogue threads, after a cluster barrier): each CTA pushes
+// its fp32 partial straight from TMEM, rows [j R, (j + 1) R) into slot r of
+// rank j's buffer; its own rows with plain shared stores (~3x the rate of
+// stores into another CTA).  With S <= 4 a warp's 32 rows have a single
+// destination, so the branch is warp-uniform.  An empty K range pushes zeros.
+template <class CF>
+__device__ __forceinline__ void split_push(const Params& p, const uint8_t* smem, uint32_t tmem_base, int warp,
+                                           int lane, bool any)
+{
+    constexpr int COLS = CF::BN / 2;
+    constexpr int C4 = CF::BN / 4;
+    constexpr int NCH = COLS / 16;
+    constexpr int BATCH = NCH < 4 ? NCH : 4;
+    const int quarter = warp & 3, half = (warp - EPI_WARP0) >> 2;
+    const int row = quarter * 32 + lane;  // accumulator row (TMEM lane)
+    const int S = p.ksplit, rows = BM / S;
+    const int rank = (int)(blockIdx.x % (unsigned)S);
+    const int dst = row / rows, lr = row % rows;
+    const bool local = dst == rank;
+    const uint32_t rbase = mapa_shared(smem_u32(smem), (uint32_t)dst);
+    uint8_t* lbase = const_cast<uint8_t*>(smem);
+    const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + half * COLS;
+#pragma unroll
+    for (int b0 = 0; b0 < NCH; b0 += BATCH)
+    {
+        uint32_t v[BATCH][16];
+#pragma unroll
+        for (int b = 0; b < BATCH; ++b) tc_ld_32x32b_x16(taddr + (b0 + b) * 16, v[b]);
+        tc_wait_ld();
+#pragma unroll
+        for (int b = 0; b < BATCH; ++b)
+        {
+#pragma unroll
+            for (int t = 0; t < 4; ++t)
+            {
+                const int q = half * (COLS / 4) + (b0 + b) * 4 + t;  // 16-byte column group of the tile
+                const int off = split_off(rank, q, lr, rows, C4);
+                const uint4 val = any ? make_uint4(v[b][4 * t], v[b][4 * t + 1], v[b][4 * t + 2], v[b][4 * t + 3])
+                                      : make_uint4(0u, 0u, 0u, 0u);
+                if (local)
+                    *reinterpret_cast<uint4*>(lbase + off) = val;
+                else
+                    st_shared_cluster_v4(rbase + (uint32_t)off, val.x, val.y, val.z, val.w);
+            }
+        }
+    }
+}
+
+// The finish (all threads, after the pushes and a cluster barrier): rank r
+// sums its R rows over the S slots of its own buffer in slot order 0, 1, ...
+// (every run adds in the same order), applies factors, alpha and bias as the
+// single-pass epilogue does and stores bf16: a warp covers 32 consecutive
+// column groups of one row, 256 contiguous output bytes.
+template <class CF>
+__device__ __forceinline__ void split_finish(const Params& p, const uint8_t* smem, const float* epi_f, int et)
+{
+    constexpr int BN = CF::BN;
+    constexpr int C4 = BN / 4;
+    constexpr int NT = NUM_THREADS;
+    constexpr int U = 8;
+    const int S = p.ksplit;
+    const int rank = (int)(blockIdx.x % (unsigned)S);
+    const int rows = BM / S;
+    const int tile = (int)(blockIdx.x / (unsigned)S);
+    const int tr = tile % p.tiles_r, tc = tile / p.tiles_r;
+    const int r0 = tr * BM, c0 = tc * BN;
+    const float* fr_s = epi_f;
+    const float* fc_s = epi_f + BM;
+    const float* bias_s = epi_f + BM + BN;
+    const bool has_factor = (p.a_factor != nullptr) || (p.b_factor != nullptr);
+    const bool has_alpha = p.alpha != 1.0f;
+    const bool has_bias = p.bias != nullptr;
+    const int units = rows * C4;
+    for (int u0 = et; u0 < units; u0 += NT * U)
+    {
+        float4 a[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) a[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int src = 0; src < S; ++src)
+        {
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+            {
+                const int idx = u0 + u * NT;
+                if (idx < units)
+                {
+                    const float4 b =
+                        *reinterpret_cast<const float4*>(smem + split_off(src, idx % C4, idx / C4, rows, C4));
+                    if (src == 0)
+                    {
+                        a[u] = b;
+                    }
+                    else
+                    {
+                        a[u].x += b.x;
+                        a[u].y += b.y;
+                        a[u].z += b.z;
+                        a[u].w += b.w;
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+        {
+            const int idx = u0 + u * NT;
+            const int tl = rank * rows + idx / C4, c = (idx % C4) * 4;  // tile row, tile column
+            const int m = r0 + tl, n = c0 + c;
+            if (idx >= units || m >= p.M || n >= p.N) continue;
+            float x[4] = {a[u].x, a[u].y, a[u].z, a[u].w};
+            if (has_factor)
+            {
+#pragma unroll
+                for (int t = 0; t < 4; ++t) x[t] = __fmul_rn(x[t], __fmul_rn(fr_s[tl], fc_s[c + t]));
+            }
+            if (has_alpha)
+            {
+#pragma unroll
+                for (int t = 0; t < 4; ++t) x[t] = __fmul_rn(x[t], p.alpha);
+            }
+            if (has_bias)
+            {
+#pragma unroll
+                for (int t = 0; t < 4; ++t) x[t] = __fadd_rn(x[t], bias_s[c + t]);
+            }
+            __nv_bfloat162 h0 = __floats2bfloat162_rn(x[0], x[1]);
+            __nv_bfloat162 h1 = __floats2bfloat162_rn(x[2], x[3]);
+            *reinterpret_cast<uint2*>(p.out + (size_t)m * p.N + n) =
+                make_uint2(*reinterpret_cast<uint32_t*>(&h0), *reinterpret_cast<uint32_t*>(&h1));
+        }
+    }
+}
 
 // ------------------------------------------------------------------ kernel
 template <class CF>
@@ -391,6 +558,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     // the SMs this grid frees.
     griddep_wait();
     griddep_launch_dependents();
+#if MBS_TIMING
+    if (threadIdx.x == 0) tacc[14] = (unsigned long long)(clock64() - t_kernel0);
+#endif
 
     if (warp == 0)
     {
@@ -679,7 +849,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             tc_fence_after();
             const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN + half * COLS;
             const bool row_valid = r0 + row < r_extent;
-            if (nonowner)
+            if (CF::SPLIT_OK && p.ksplit > 1)
+            {
+                // cluster split-K: the accumulator stays in TMEM until the whole
+                // cluster has its own (split_push after the role loops)
+            }
+            else if (nonowner)
             {
                 float* part = p.partials + (size_t)blockIdx.x * (PR * BN);
 #pragma unroll 1
@@ -925,6 +1100,43 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    __syncwarp();
+    if constexpr (CF::SPLIT_OK)
+    {
+        if (p.ksplit > 1)
+        {
+            // Every role loop above ends (its waits are bounded), so every thread
+            // of every CTA of the cluster reaches both barriers.
+#if MBS_TIMING
+            const long long t_red0 = clock64();
+#endif
+            cluster_sync();  // every CTA of the cluster: accumulator complete, stages idle
+#if MBS_TIMING
+            const long long t_red1 = clock64();
+#endif
+            if (warp >= EPI_WARP0)
+            {
+                Work w;
+                const bool any = get_work(p, 0, w) && w.k1 > w.k0;
+                split_push<CF>(p, smem, tmem_base, warp, lane, any);
+            }
+            tc_fence_before();
+            cluster_sync();  // every slice in place
+            tc_fence_after();
+#if MBS_TIMING
+            const long long t_red2 = clock64();
+#endif
+            split_finish<CF>(p, smem, epi_f, threadIdx.x);
+#if MBS_TIMING
+            if (threadIdx.x == EPI_WARP0 * 32)
+            {
+                tacc[12] += (unsigned long long)(t_red1 - t_red0);
+                tacc[13] += (unsigned long long)(t_red2 - t_red1);
+                tacc[15] += (unsigned long long)(clock64() - t_red2);
+            }
+#endif
+        }
+    }
     __syncwarp();
     if (warp == 1) tmem_dealloc(tmem_base, CF::TMEM_COLS);
 #if MBS_TIMING
@@ -1652,6 +1864,7 @@ struct Plan
     int pair_bn;  // CTA-pair configuration: 256-column tiles, or 384 (mixed with 256)
     int pair_tiles_c, pair_wide_c;  // ... column tiles, of which the first pair_wide_c 384 wide
     int pair_img_b_blocks;          // ... 128-row B scale image blocks per K stage
+    int ksplit;                     // single-CTA kernel: cluster split-K factor (1 = none)
     int G, tiles_r, tiles_c, k_stages;
     size_t ws_bytes;
 };
@@ -1749,6 +1962,48 @@ Plan make_plan(int M, int N, int K, int num_sms, bool packed = false)
         pl.tiles_c = (N + pl.bn - 1) / pl.bn;
     }
     const long long tiles = (long long)pl.tiles_r * pl.tiles_c;
+    // Cluster split-K for few 128-row tiles: the S CTAs of a cluster run one
+    // tile's K stages in S ranges and add their fp32 partials through
+    // distributed shared memory, so S times the SMs stream the operands and no
+    // partial touches global memory.  Measured back to back on B200 against
+    // the unsplit schedules: S = 4 pays once every CTA keeps 4 or more K
+    // stages (1024x1024x5120 16.9 -> 13.9 us, 512x1024x8192 22.4 -> 14.2,
+    // 128x7168x16384 29.4 -> 21.5), S = 2 once it keeps 4 (1024x1024x2048
+    // 12.3 -> 11.4, 2048x1024x5120 17.4 -> 16.4); shorter ranges lose
+    // (256x512x1024 8.0 -> 9.9 at S = 2), and so do clusters of 8 (fewer fit
+    // at a time) or more CTAs than SMs.  The hand-over costs ~4-6 us per CTA
+    // (shared memory of another CTA moves ~40 GB/s per SM), so a split must
+    // save more K stages than that.  The schedule overrides below turn it off;
+    // MBS_KSPLIT=S forces S (2, 4 or 8), 0 turns it off.
+    pl.ksplit = 1;
+    {
+        const int force_split = env_int("MBS_KSPLIT", -1);
+        const bool overridden = env_int("MBS_FORCE_SCHEDULE", 0) != 0 || env_int("MBS_FORCE_GRID", 0) != 0 ||
+                                env_int("MBS_FORCE_PAIR", -1) == 1;
+        int lim = num_sms;
+        if (g_grid_limit > 0 && g_grid_limit < lim) lim = g_grid_limit;
+        if (!pl.swap && pl.r_rows == 128 && force_split != 0 && (force_split > 1 || !overridden))
+        {
+            for (int S = 8; S >= 2; S /= 2)
+            {
+                const bool want = force_split > 1 ? S == force_split
+                                                  : (S <= 4 && tiles * S <= lim && pl.k_stages >= (S == 4 ? 16 : 8));
+                if (want && S <= pl.k_stages && tiles * S < (1LL << 31))
+                {
+                    pl.ksplit = S;
+                    break;
+                }
+            }
+        }
+        if (pl.ksplit > 1)
+        {
+            pl.sk = false;
+            pl.pair = false;
+            pl.G = (int)(tiles * pl.ksplit);
+            pl.ws_bytes = 0;
+            return pl;
+        }
+    }
     // Stream-K where its partial tiles are small (skinny activations: 32- or
     // 64-row partials, an HBM-bound stream) or where a data-parallel tile
     // would run a very deep K alone on a mostly idle GPU.  With 128-row
@@ -2128,21 +2383,41 @@ int launch_cfg(const Problem& pb, const Plan& pl, const DeviceInfo& dev, void* w
     if (p.err == nullptr) return fail(MBS_ERR_CUDA, "device error word unavailable");
     p.packed_b = pb.packed ? pb.B : nullptr;
     p.act_rows = act_box_rows(pb, pl);
+    p.ksplit = pl.ksplit;
+    if (pl.ksplit > 1 && !CF::SPLIT_OK) return fail(MBS_ERR_CUDA, "cluster split-K planned for a configuration without it");
 
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(pl.G);
     cfg.blockDim = dim3(NUM_THREADS);
     cfg.dynamicSmemBytes = CF::SMEM_BYTES;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[2];
-    attr[0].id = cudaLaunchAttributeCooperative;  // stream-K owners wait on other CTAs
-    attr[0].val.cooperative = pl.sk ? 1 : 0;
+    cudaLaunchAttribute attr[3];
+    int na = 0;
+    if (pl.ksplit > 1)
+    {
+        // cluster split-K: the CTAs of a cluster sum their partials in each other's shared memory
+        attr[na].id = cudaLaunchAttributeClusterDimension;
+        attr[na].val.clusterDim.x = (unsigned)pl.ksplit;
+        attr[na].val.clusterDim.y = 1;
+        attr[na].val.clusterDim.z = 1;
+        ++na;
+    }
+    else
+    {
+        attr[na].id = cudaLaunchAttributeCooperative;  // stream-K owners wait on other CTAs
+        attr[na].val.cooperative = pl.sk ? 1 : 0;
+        ++na;
+    }
     // may start while the previous kernel in the stream finishes (the kernel
     // waits for it before touching global memory)
-    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    if (pdl_enabled())
+    {
+        attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[na].val.programmaticStreamSerializationAllowed = 1;
+        ++na;
+    }
     cfg.attrs = attr;
-    cfg.numAttrs = pdl_enabled() ? 2 : 1;
+    cfg.numAttrs = na;
     st = record_before(stream);
     if (st) return st;
     cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, tm_r, tm_c, tm_rsf, tm_csf, p);

@@ -274,7 +274,18 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank)
     return r;
 }
 
-// Cluster-wide barrier (all threads of both CTAs).  The non-.aligned forms
+// 16-byte store into the shared memory of any CTA of the cluster
+// (`cluster_addr` from mapa_shared); made visible to the other CTAs by a
+// following cluster_sync() (release / acquire).
+__device__ __forceinline__ void st_shared_cluster_v4(uint32_t cluster_addr, uint32_t a, uint32_t b, uint32_t c,
+                                                     uint32_t d)
+{
+    asm volatile("st.shared::cluster.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(cluster_addr), "r"(a), "r"(b), "r"(c),
+                 "r"(d)
+                 : "memory");
+}
+
+// Cluster-wide barrier (all threads of every CTA).  The non-.aligned forms
 // tolerate warps whose lanes arrive at different times.
 __device__ __forceinline__ void cluster_sync()
 {

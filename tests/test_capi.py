@@ -105,6 +105,8 @@ def test_kernels_per_call_is_host_only(lib):
     assert lib.mbs_gemm_a4w4_kernels_per_call(8192, 8192, 8192) == 2
     assert lib.mbs_gemm_a4w4_kernels_per_call(16, 57344, 8192) == 1
     assert lib.mbs_gemm_a4w4_kernels_per_call(256, 512, 1024) == 1
+    assert lib.mbs_gemm_a4w4_kernels_per_call(1024, 1024, 5120) == 1  # cluster split-K
+    assert lib.mbs_gemm_a4w4_kernels_per_call(2048, 2048, 8192) == 2
     assert lib.mbs_gemm_a4w4_kernels_per_call(0, 16, 64) == -1
 
 

@@ -20,13 +20,14 @@ SCHEDULES = {
     "dp_single": dict(MBS_FORCE_SCHEDULE="2", MBS_FORCE_PAIR="0"),
     "stream_k": dict(MBS_FORCE_SCHEDULE="1", MBS_FORCE_GRID="17"),
     "swap": dict(MBS_FORCE_SWAP="1"),
+    "ksplit": dict(MBS_KSPLIT="4"),  # cluster split-K
 }
 
 
 @pytest.fixture
 def env():
     keys = ("MBS_FORCE_SCHEDULE", "MBS_FORCE_GRID", "MBS_FORCE_PAIR", "MBS_FORCE_SWAP", "MBS_PAIR_BN",
-            "MBS_PAIR_WIDE")
+            "MBS_PAIR_WIDE", "MBS_KSPLIT")
     saved = {k: os.environ.get(k) for k in keys}
     yield os.environ
     for k, v in saved.items():
@@ -39,7 +40,8 @@ def env():
 @pytest.mark.parametrize("sched,M,N,K", [("pair", 512, 512, 1024), ("pair384", 300, 1040, 1024),
                                          ("pair_mix", 300, 1040, 1024),
                                          ("dp_single", 200, 768, 512),
-                                         ("stream_k", 40, 2048, 2048), ("swap", 24, 1024, 512)])
+                                         ("stream_k", 40, 2048, 2048), ("swap", 24, 1024, 512),
+                                         ("ksplit", 200, 768, 2048)])
 @pytest.mark.parametrize("alpha,with_bias", [(0.5, False), (-3.25, True), (1.0, True), (7.0, True)])
 def test_alpha_bias(env, sched, M, N, K, alpha, with_bias):
     import mbs_b200

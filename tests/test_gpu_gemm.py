@@ -83,15 +83,17 @@ def test_one_workspace_serves_every_schedule(force_env):
     workspace: scale images and wide stream-K partial slots written by one
     launch must never read as another schedule's completion flags."""
     seq = [
-        (dict(), (512, 512, 1024)),                                         # CTA pairs: scale images
+        (dict(MBS_FORCE_PAIR=1), (512, 512, 1024)),                         # CTA pairs: scale images
+        (dict(), (300, 1024, 2048)),                                        # cluster split-K: no workspace
         (dict(MBS_FORCE_SCHEDULE=1), (300, 1024, 2048)),                    # stream-K, 128-row slots
         (dict(MBS_FORCE_SCHEDULE=1, MBS_FORCE_GRID=17), (2, 2048, 4096)),   # 3 CTAs per tile
         (dict(MBS_FORCE_SCHEDULE=1, MBS_FORCE_GRID=29), (48, 1024, 4096)),  # 64-row slots
         (dict(MBS_FORCE_SCHEDULE=1, MBS_FORCE_GRID=17), (2, 2048, 4096)),
     ]
     for i, (env, (M, N, K)) in enumerate(seq):
-        os.environ.pop("MBS_FORCE_SCHEDULE", None)
-        os.environ.pop("MBS_FORCE_GRID", None)
+        for k in ("MBS_FORCE_SCHEDULE", "MBS_FORCE_GRID", "MBS_FORCE_PAIR"):
+            force_env(**{k: ""})
+            os.environ.pop(k)
         force_env(**env)
         c = Case(M, N, K, seed=100 + i, factors=True)
         out = _gemm(c)
@@ -128,6 +130,34 @@ def test_cta_pair_path(force_env, M, N, K, macro, grid, bn):
     torch.cuda.synchronize()
     ref, bound = c.reference()
     assert_gemm_close(out, ref, bound, f"pair{bn} {M}x{N}x{K} macro={macro} grid={grid}")
+
+
+@pytest.mark.parametrize("S,M,N,K,kind", [
+    (2, 300, 272, 1088, "plain"),    # ragged M and N, partial last K stage, 5 stages over 2
+    (4, 129, 784, 4160, "plain"),    # one row past a tile, 17 stages over 4
+    (8, 256, 512, 2048, "plain"),    # one stage per rank
+    (8, 200, 1024, 2304, "macro"),   # macro-block B scales, 9 stages over 8
+    (4, 160, 1280, 3072, "packed"),  # packed weights
+    (4, 1024, 1024, 5120, "plain"),  # the reference's small deep-K shape (default plan)
+])
+def test_cluster_split_k(force_env, S, M, N, K, kind):
+    """Cluster split-K: the S CTAs of a cluster take S K ranges of one tile
+    and add their fp32 partials through distributed shared memory, each
+    finishing 128 / S rows."""
+    import mbs_b200
+    if (M, N, K) != (1024, 1024, 5120):
+        force_env(MBS_KSPLIT=S)
+    c = Case(M, N, K, seed=M + N + S, factors=True, macro=kind == "macro", b_std=0.02 if kind == "packed" else 1.0)
+    if kind == "macro":
+        out = mbs_b200.gemm_a4w4_macro(c.A, c.B, c.A_scale, c.B_scale, c.A_factor, c.B_factor)
+    elif kind == "packed":
+        pw = mbs_b200.pack_weight(c.B, c.B_scale)
+        out = mbs_b200.gemm_a4w4_packed(c.A, pw, c.A_scale, c.A_factor, c.B_factor)
+    else:
+        out = _gemm(c)
+    torch.cuda.synchronize()
+    ref, bound = c.reference()
+    assert_gemm_close(out, ref, bound, f"ksplit{S} {M}x{N}x{K} {kind}")
 
 
 @pytest.mark.parametrize("M,N,K", [(384, 1024, 512), (1000, 2048, 256)])
