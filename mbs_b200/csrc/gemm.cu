@@ -1965,16 +1965,20 @@ Plan make_plan(int M, int N, int K, int num_sms, bool packed = false)
     // Cluster split-K for few 128-row tiles: the S CTAs of a cluster run one
     // tile's K stages in S ranges and add their fp32 partials through
     // distributed shared memory, so S times the SMs stream the operands and no
-    // partial touches global memory.  Measured back to back on B200 against
-    // the unsplit schedules: S = 4 pays once every CTA keeps 4 or more K
-    // stages (1024x1024x5120 16.9 -> 13.9 us, 512x1024x8192 22.4 -> 14.2,
-    // 128x7168x16384 29.4 -> 21.5), S = 2 once it keeps 4 (1024x1024x2048
-    // 12.3 -> 11.4, 2048x1024x5120 17.4 -> 16.4); shorter ranges lose
-    // (256x512x1024 8.0 -> 9.9 at S = 2), and so do clusters of 8 (fewer fit
-    // at a time) or more CTAs than SMs.  The hand-over costs ~4-6 us per CTA
-    // (shared memory of another CTA moves ~40 GB/s per SM), so a split must
-    // save more K stages than that.  The schedule overrides below turn it off;
-    // MBS_KSPLIT=S forces S (2, 4 or 8), 0 turns it off.
+    // partial touches global memory.  Tiles are 128 x 256 or 128 x 128 (the
+    // narrower tile doubles the clusters and halves each CTA's hand-over, but
+    // moves 1.5x the operand bytes per FLOP).  Among (BN, S) in {256, 128} x
+    // {2, 4} whose CTAs fit on the SMs, the plan takes the least estimated
+    // time per CTA,
+    //   6.1 us + 0.0132 us/KB * operand KB + 0.0497 us/KB * KB handed to other CTAs,
+    // a fit to back-to-back B200 timings (1024x1024x5120 16.9 us on CTA
+    // pairs -> 13.8 at 256 x S4 -> 12.5 at 128 x S2; 256x1024x8192 22.3 ->
+    // 11.5 at 128 x S4; 1024x1024x2048 12.3 -> 9.3 at 128 x S2;
+    // 128x7168x16384 29.4 -> 21.3 at 256 x S4).  A split needs 8 or more K
+    // stages (256x512x1024, 4 stages: 8.0 -> 9.9 us at S = 2); clusters of 8
+    // fit too few at a time.  The schedule overrides below turn it off;
+    // MBS_KSPLIT=S forces S (2, 4 or 8) with MBS_SPLIT_BN=128 or 256
+    // (default 256), MBS_KSPLIT=0 turns it off.
     pl.ksplit = 1;
     {
         const int force_split = env_int("MBS_KSPLIT", -1);
@@ -1982,24 +1986,44 @@ Plan make_plan(int M, int N, int K, int num_sms, bool packed = false)
                                 env_int("MBS_FORCE_PAIR", -1) == 1;
         int lim = num_sms;
         if (g_grid_limit > 0 && g_grid_limit < lim) lim = g_grid_limit;
-        if (!pl.swap && pl.r_rows == 128 && force_split != 0 && (force_split > 1 || !overridden))
+        int split_bn = 256;
+        if (!pl.swap && pl.r_rows == 128 && force_split > 1)
         {
-            for (int S = 8; S >= 2; S /= 2)
+            if (force_split <= pl.k_stages && force_split <= 8 && tiles * force_split < (1LL << 31))
             {
-                const bool want = force_split > 1 ? S == force_split
-                                                  : (S <= 4 && tiles * S <= lim && pl.k_stages >= (S == 4 ? 16 : 8));
-                if (want && S <= pl.k_stages && tiles * S < (1LL << 31))
+                pl.ksplit = force_split;
+                split_bn = (env_int("MBS_SPLIT_BN", 256) == 128 && !packed) ? 128 : 256;
+            }
+        }
+        else if (!pl.swap && pl.r_rows == 128 && force_split != 0 && !overridden && pl.k_stages >= 8)
+        {
+            double best = 1e300;
+            for (int bn : {256, 128})
+            {
+                if (bn == 128 && packed) continue;  // packed weights come in 256-row tiles
+                const long long t = (long long)pl.tiles_r * ((N + bn - 1) / bn);
+                const double stage_kb = bn == 256 ? 51.0 : 34.0;  // A + B tiles + raw scales per K stage
+                for (int S : {2, 4})
                 {
-                    pl.ksplit = S;
-                    break;
+                    if (t * S > lim || pl.k_stages < 2 * S) continue;
+                    const double per_cta = 6.1 + 0.0132 * ((pl.k_stages + S - 1) / S) * stage_kb +
+                                           0.0497 * (double)(S - 1) / S * (bn / 2);
+                    if (per_cta < best)
+                    {
+                        best = per_cta;
+                        pl.ksplit = S;
+                        split_bn = bn;
+                    }
                 }
             }
         }
         if (pl.ksplit > 1)
         {
+            pl.bn = split_bn;
+            pl.tiles_c = (N + split_bn - 1) / split_bn;
             pl.sk = false;
             pl.pair = false;
-            pl.G = (int)(tiles * pl.ksplit);
+            pl.G = (int)((long long)pl.tiles_r * pl.tiles_c * pl.ksplit);
             pl.ws_bytes = 0;
             return pl;
         }
@@ -2444,6 +2468,9 @@ int dispatch(const Problem& pb, const Plan& pl, const DeviceInfo& dev, void* ws,
         return pb.macro ? launch_cfg<Cfg<64, true, true, 8>>(pb, pl, dev, ws, s)
                         : launch_cfg<Cfg<64, true, false, 8>>(pb, pl, dev, ws, s);
     }
+    if (pl.bn == 128)
+        return pb.macro ? launch_cfg<Cfg<128, false, true, 6>>(pb, pl, dev, ws, s)
+                        : launch_cfg<Cfg<128, false, false, 6>>(pb, pl, dev, ws, s);
     if (pl.r_rows == 32)
         return pb.macro ? launch_cfg<Cfg<256, false, true, 5, 32>>(pb, pl, dev, ws, s)
                         : launch_cfg<Cfg<256, false, false, 5, 32>>(pb, pl, dev, ws, s);

@@ -132,22 +132,27 @@ def test_cta_pair_path(force_env, M, N, K, macro, grid, bn):
     assert_gemm_close(out, ref, bound, f"pair{bn} {M}x{N}x{K} macro={macro} grid={grid}")
 
 
-@pytest.mark.parametrize("S,M,N,K,kind", [
-    (2, 300, 272, 1088, "plain"),    # ragged M and N, partial last K stage, 5 stages over 2
-    (4, 129, 784, 4160, "plain"),    # one row past a tile, 17 stages over 4
-    (8, 256, 512, 2048, "plain"),    # one stage per rank
-    (8, 200, 1024, 2304, "macro"),   # macro-block B scales, 9 stages over 8
-    (4, 160, 1280, 3072, "packed"),  # packed weights
-    (4, 1024, 1024, 5120, "plain"),  # the reference's small deep-K shape (default plan)
+@pytest.mark.parametrize("S,M,N,K,kind,bn", [
+    (2, 300, 272, 1088, "plain", 256),    # ragged M and N, partial last K stage, 5 stages over 2
+    (4, 129, 784, 4160, "plain", 256),    # one row past a tile, 17 stages over 4
+    (8, 256, 512, 2048, "plain", 256),    # one stage per rank
+    (8, 200, 1024, 2304, "macro", 256),   # macro-block B scales, 9 stages over 8
+    (4, 160, 1280, 3072, "packed", 256),  # packed weights
+    (4, 1024, 1024, 5120, "plain", 0),    # the reference's small deep-K shape (default plan)
+    (2, 300, 272, 1088, "plain", 128),    # 128-column tiles: a last tile of 16 columns
+    (4, 129, 784, 4160, "plain", 128),
+    (2, 200, 1024, 2304, "macro", 128),
+    (4, 1024, 1024, 5120, "plain", 128),
 ])
-def test_cluster_split_k(force_env, S, M, N, K, kind):
+def test_cluster_split_k(force_env, S, M, N, K, kind, bn):
     """Cluster split-K: the S CTAs of a cluster take S K ranges of one tile
-    and add their fp32 partials through distributed shared memory, each
-    finishing 128 / S rows."""
+    (128 x 256, or 128 x 128) and add their fp32 partials through
+    distributed shared memory, each finishing 128 / S rows."""
     import mbs_b200
-    if (M, N, K) != (1024, 1024, 5120):
-        force_env(MBS_KSPLIT=S)
-    c = Case(M, N, K, seed=M + N + S, factors=True, macro=kind == "macro", b_std=0.02 if kind == "packed" else 1.0)
+    if bn:
+        force_env(MBS_KSPLIT=S, MBS_SPLIT_BN=bn)
+    c = Case(M, N, K, seed=M + N + S + bn, factors=True, macro=kind == "macro",
+             b_std=0.02 if kind == "packed" else 1.0)
     if kind == "macro":
         out = mbs_b200.gemm_a4w4_macro(c.A, c.B, c.A_scale, c.B_scale, c.A_factor, c.B_factor)
     elif kind == "packed":
@@ -157,7 +162,7 @@ def test_cluster_split_k(force_env, S, M, N, K, kind):
         out = _gemm(c)
     torch.cuda.synchronize()
     ref, bound = c.reference()
-    assert_gemm_close(out, ref, bound, f"ksplit{S} {M}x{N}x{K} {kind}")
+    assert_gemm_close(out, ref, bound, f"ksplit{S} bn{bn} {M}x{N}x{K} {kind}")
 
 
 @pytest.mark.parametrize("M,N,K", [(384, 1024, 512), (1000, 2048, 256)])
