@@ -123,21 +123,27 @@ constexpr int QUANT_THREADS = 256;
 // registers, so the rows in flight per SM (and the MBS variant, which waits
 // for a CTA-wide row max, most of all) scale with it
 constexpr int QUANT_MIN_CTAS = 6;
+// The MBS variant: 128-thread CTAs with 8 loads in flight per thread hold a
+// K = 8192 row in half the threads, and 8 of them fit on an SM (8 rows in
+// flight per SM instead of 6), each waiting on a 4-warp row max.
+constexpr int QMBS_THREADS = 128;
+constexpr int QMBS_UNROLL = 8;
+constexpr int QMBS_MIN_CTAS = 8;
 
 // MBS = true: each row is first reduced to its max |x| (one read of the row,
 // kept in L2 for the second), its factor byte b is written to `factors`, and
 // the row is quantised as x * (1 + b/256).
-// Codes and scales of one group of QUANT_UNROLL octets per thread (octet j =
-// j0 + u * QUANT_THREADS of row r), the row already multiplied by m when MBS.
-template <bool MBS>
-__device__ __forceinline__ void quantize_group(const uint4 (&v)[QUANT_UNROLL], int j0, int oct, int limit,
+// Codes and scales of one group of UNROLL octets per thread (octet j =
+// j0 + u * NT of row r), the row already multiplied by m when MBS.
+template <bool MBS, int NT, int UNROLL>
+__device__ __forceinline__ void quantize_group(const uint4 (&v)[UNROLL], int j0, int oct, int limit,
                                                float m, int r, int K, uint32_t* __restrict__ qr,
                                                uint8_t* __restrict__ sc, int shuffled, int snp)
 {
 #pragma unroll
-    for (int u = 0; u < QUANT_UNROLL; ++u)
+    for (int u = 0; u < UNROLL; ++u)
     {
-        const int j = j0 + u * QUANT_THREADS;
+        const int j = j0 + u * NT;
         if (j - (int)(threadIdx.x & 31) >= limit) break;  // whole warp past the row end
         const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
         uint32_t am = amax_bits8(w);
@@ -169,20 +175,21 @@ __device__ __forceinline__ void quantize_group(const uint4 (&v)[QUANT_UNROLL], i
     }
 }
 
-template <int UNROLL>
+template <int NT, int UNROLL>
 __device__ __forceinline__ void load_group(const uint4* __restrict__ xr, int j0, int oct, uint4 (&v)[UNROLL],
                                            bool last_use)
 {
 #pragma unroll
     for (int u = 0; u < UNROLL; ++u)
     {
-        const int j = j0 + u * QUANT_THREADS;
+        const int j = j0 + u * NT;
         v[u] = j < oct ? (last_use ? __ldcs(xr + j) : __ldcg(xr + j)) : make_uint4(0, 0, 0, 0);
     }
 }
 
 // MBS row factor: CTA-wide max of the threads' `am`, factor byte to
 // factors[r], returns the row multiplier m = 1 + b/256.
+template <int NT>
 __device__ __forceinline__ float mbs_row_multiplier(uint32_t am, int r, uint8_t* __restrict__ factors,
                                                     uint32_t* red)
 {
@@ -191,7 +198,7 @@ __device__ __forceinline__ float mbs_row_multiplier(uint32_t am, int r, uint8_t*
     __syncthreads();
     if (threadIdx.x < 32)
     {
-        uint32_t a = threadIdx.x < QUANT_THREADS / 32 ? red[threadIdx.x] : 0u;
+        uint32_t a = threadIdx.x < NT / 32 ? red[threadIdx.x] : 0u;
         a = __reduce_max_sync(0xffffffffu, a);
         if (threadIdx.x == 0)
         {
@@ -208,60 +215,60 @@ __device__ __forceinline__ float mbs_row_multiplier(uint32_t am, int r, uint8_t*
 
 // MBS = true: each row is first reduced to its max |x|, its factor byte b is
 // written to `factors`, and the row is quantised as x * (1 + b/256).  A row
-// of up to QUANT_THREADS * QUANT_UNROLL octets (K <= 8192) stays in registers
-// between the two steps; longer rows are read twice (the second read from L2).
-template <bool MBS>
-__global__ void __launch_bounds__(QUANT_THREADS, QUANT_MIN_CTAS) quantize_1x32_kernel(const uint16_t* __restrict__ x,
+// of up to NT * UNROLL octets (K <= 8192) stays in registers between the two
+// steps; longer rows are read twice (the second read from L2).
+template <bool MBS, int NT, int UNROLL, int MIN_CTAS>
+__global__ void __launch_bounds__(NT, MIN_CTAS) quantize_1x32_kernel(const uint16_t* __restrict__ x,
                                                                       int rows, int K, int ld_x,
                                                                       uint8_t* __restrict__ q,
                                                                       uint8_t* __restrict__ sc, int shuffled,
                                                                       int snp, uint8_t* __restrict__ factors)
 {
-    __shared__ uint32_t red[QUANT_THREADS / 32];
+    __shared__ uint32_t red[NT / 32];
     const int oct = K >> 3;                 // octets in a row (multiple of 4)
     const int limit = (oct + 31) & ~31;     // whole warps
-    const bool one_pass = oct <= QUANT_THREADS * QUANT_UNROLL;
+    const bool one_pass = oct <= NT * UNROLL;
     for (int r = blockIdx.x; r < rows; r += gridDim.x)
     {
         const uint4* xr = reinterpret_cast<const uint4*>(x + (int64_t)r * ld_x);
         uint32_t* qr = reinterpret_cast<uint32_t*>(q + (int64_t)r * (K >> 1));
         if (MBS && one_pass)
         {
-            uint4 v[QUANT_UNROLL];
-            load_group<QUANT_UNROLL>(xr, threadIdx.x, oct, v, true);
+            uint4 v[UNROLL];
+            load_group<NT, UNROLL>(xr, threadIdx.x, oct, v, true);
             uint32_t am = 0;
 #pragma unroll
-            for (int u = 0; u < QUANT_UNROLL; ++u)
+            for (int u = 0; u < UNROLL; ++u)
             {
                 const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
                 am = max(am, amax_bits8(w));
             }
-            const float m = mbs_row_multiplier(am, r, factors, red);
-            quantize_group<MBS>(v, threadIdx.x, oct, limit, m, r, K, qr, sc, shuffled, snp);
+            const float m = mbs_row_multiplier<NT>(am, r, factors, red);
+            quantize_group<MBS, NT, UNROLL>(v, threadIdx.x, oct, limit, m, r, K, qr, sc, shuffled, snp);
             continue;
         }
         float m = 1.0f;
         if constexpr (MBS)
         {
             uint32_t am = 0;
-            for (int j0 = threadIdx.x; j0 < oct; j0 += QUANT_THREADS * QUANT_UNROLL)
+            for (int j0 = threadIdx.x; j0 < oct; j0 += NT * UNROLL)
             {
-                uint4 v[QUANT_UNROLL];
-                load_group<QUANT_UNROLL>(xr, j0, oct, v, false);
+                uint4 v[UNROLL];
+                load_group<NT, UNROLL>(xr, j0, oct, v, false);
 #pragma unroll
-                for (int u = 0; u < QUANT_UNROLL; ++u)
+                for (int u = 0; u < UNROLL; ++u)
                 {
                     const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
                     am = max(am, amax_bits8(w));
                 }
             }
-            m = mbs_row_multiplier(am, r, factors, red);
+            m = mbs_row_multiplier<NT>(am, r, factors, red);
         }
-        for (int j0 = threadIdx.x; j0 < limit; j0 += QUANT_THREADS * QUANT_UNROLL)
+        for (int j0 = threadIdx.x; j0 < limit; j0 += NT * UNROLL)
         {
-            uint4 v[QUANT_UNROLL];
-            load_group<QUANT_UNROLL>(xr, j0, oct, v, true);
-            quantize_group<MBS>(v, j0, oct, limit, m, r, K, qr, sc, shuffled, snp);
+            uint4 v[UNROLL];
+            load_group<NT, UNROLL>(xr, j0, oct, v, true);
+            quantize_group<MBS, NT, UNROLL>(v, j0, oct, limit, m, r, K, qr, sc, shuffled, snp);
         }
     }
 }
@@ -422,11 +429,11 @@ int quantize_1x32(const char* fn, const void* x_bf16, int rows, int K, int ld_x,
     // one CTA per row (grid-stride over rows beyond the cap)
     const int qgrid = rows < dev.num_sms * 64 ? rows : dev.num_sms * 64;
     if (factors != nullptr)
-        quantize_1x32_kernel<true><<<qgrid, QUANT_THREADS, 0, s>>>(
+        quantize_1x32_kernel<true, QMBS_THREADS, QMBS_UNROLL, QMBS_MIN_CTAS><<<qgrid, QMBS_THREADS, 0, s>>>(
             static_cast<const uint16_t*>(x_bf16), rows, K, ld_x, fp4_out, scale_out, shuffled ? 1 : 0,
             snp, factors);
     else
-        quantize_1x32_kernel<false><<<qgrid, QUANT_THREADS, 0, s>>>(
+        quantize_1x32_kernel<false, QUANT_THREADS, QUANT_UNROLL, QUANT_MIN_CTAS><<<qgrid, QUANT_THREADS, 0, s>>>(
             static_cast<const uint16_t*>(x_bf16), rows, K, ld_x, fp4_out, scale_out, shuffled ? 1 : 0,
             snp, nullptr);
     if (shuffled && ((rows % 32) != 0 || (K / 32) != snp))
