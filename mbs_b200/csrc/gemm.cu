@@ -247,6 +247,9 @@ __device__ __forceinline__ void raise_error(const Params& p, volatile int* abort
 #endif
 #if MBS_TIMING
 __device__ unsigned long long g_mbs_timing[16];
+// per CTA (single-CTA kernel): SM id, start after the dependent-launch wait,
+// last stage issued by the producer, CTA end (%globaltimer ns), stages issued
+__device__ unsigned long long g_mbs_cta[1024 * 5];
 #define MBS_TSTART() const long long _mbs_t0 = clock64()
 #define MBS_TADD(acc, b) (acc)[b] += (unsigned long long)(clock64() - _mbs_t0)
 #define MBS_TFLUSH(acc)                                              \
@@ -560,6 +563,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     griddep_launch_dependents();
 #if MBS_TIMING
     if (threadIdx.x == 0) tacc[14] = (unsigned long long)(clock64() - t_kernel0);
+    if (threadIdx.x == 0 && blockIdx.x < 1024) g_mbs_cta[blockIdx.x * 5 + 1] = globaltimer_ns();
 #endif
 
     if (warp == 0)
@@ -631,6 +635,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 }
             }
         producer_done:;
+#if MBS_TIMING
+            if (blockIdx.x < 1024)
+            {
+                unsigned smid_t;
+                asm volatile("mov.u32 %0, %%smid;" : "=r"(smid_t));
+                g_mbs_cta[blockIdx.x * 5 + 0] = smid_t;
+                g_mbs_cta[blockIdx.x * 5 + 2] = globaltimer_ns();
+                g_mbs_cta[blockIdx.x * 5 + 4] = tacc[10];
+            }
+#endif
         }
     }
     else if (warp == 1)
@@ -1141,6 +1155,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (warp == 1) tmem_dealloc(tmem_base, CF::TMEM_COLS);
 #if MBS_TIMING
     if (threadIdx.x == 0) tacc[9] = (unsigned long long)(clock64() - t_kernel0);
+    if (threadIdx.x == 0 && blockIdx.x < 1024) g_mbs_cta[blockIdx.x * 5 + 3] = globaltimer_ns();
     if (lane == 0 && (warp <= 2 || warp == EPI_WARP0)) MBS_TFLUSH(tacc);
 #else
     (void)tacc;
@@ -2578,6 +2593,18 @@ using mbs::gemm::Problem;
 
 #if MBS_TIMING
 // Debug builds only: per-role cycle buckets summed over all CTAs (see above).
+#if MBS_TIMING
+// Timing builds only: per-CTA stamps of the last single-CTA GEMM launch (5 words per CTA).
+extern "C" int mbs_timing_cta_read(unsigned long long* host, int ctas)
+{
+    if (ctas <= 0 || ctas > 1024) return MBS_ERR_INVALID_ARGUMENT;
+    return cudaMemcpyFromSymbol(host, mbs::gemm::g_mbs_cta, (size_t)ctas * 5 * sizeof(unsigned long long)) ==
+                   cudaSuccess
+               ? MBS_OK
+               : MBS_ERR_CUDA;
+}
+#endif
+
 extern "C" int mbs_timing_read(unsigned long long* host, int reset)
 {
     cudaError_t e = cudaMemcpyFromSymbol(host, mbs::gemm::g_mbs_timing, 16 * sizeof(unsigned long long));
