@@ -117,15 +117,15 @@ __device__ __forceinline__ int64_t flat_s(int r, int b, int snp)
 // QUANT_UNROLL independent 16-byte loads in flight before using them, and no
 // index needs a division.  Lanes past the row end run the shuffles with an
 // empty block.
-constexpr int QUANT_UNROLL = 4;
-constexpr int QUANT_THREADS = 256;
-// CTAs per SM the register budget must allow: each holds its row's loads in
-// registers, so the rows in flight per SM (and the MBS variant, which waits
-// for a CTA-wide row max, most of all) scale with it
-constexpr int QUANT_MIN_CTAS = 6;
-// The MBS variant: 128-thread CTAs with 8 loads in flight per thread hold a
-// K = 8192 row in half the threads, and 8 of them fit on an SM (8 rows in
-// flight per SM instead of 6), each waiting on a 4-warp row max.
+// Both variants: 128-thread CTAs with 8 loads in flight per thread (a K =
+// 8192 row in one pass) and a register budget for 8 CTAs per SM, so the rows
+// in flight per SM (and for the MBS variant, which waits for a CTA-wide row
+// max, most of all) are 8.  Against 256 threads x 4 loads at 6 CTAs per SM
+// this took 16384x8192 from 54.5 to 53.0 us (16384x4096 33.0 -> 30.0) and
+// the MBS variant from 65.5 to 60.4 us.
+constexpr int QUANT_UNROLL = 8;
+constexpr int QUANT_THREADS = 128;
+constexpr int QUANT_MIN_CTAS = 8;
 constexpr int QMBS_THREADS = 128;
 constexpr int QMBS_UNROLL = 8;
 constexpr int QMBS_MIN_CTAS = 8;
