@@ -150,7 +150,7 @@ struct Cfg
     // Cluster split-K: a CTA's buffer of S partial slices (S <= 8, each
     // 128 / S rows + 1 pad row of BN / 4 16-byte column groups) lives in the
     // idle pipeline stages.
-    static constexpr bool SPLIT_OK = !SWAP && R_ROWS == 128 && (BM + 8) * (BN / 4) * 16 <= STAGES * STAGE_BYTES;
+    static constexpr bool SPLIT_OK = !SWAP && (R_ROWS + 8) * (BN / 4) * 16 <= STAGES * STAGE_BYTES;
 };
 
 // ------------------------------------------------------------------ schedule
@@ -347,7 +347,8 @@ __device__ __forceinline__ void transpose_side(const uint8_t* raw, uint8_t* atom
 }
 
 // Cluster split-K.  Cluster rank r finishes rows [r R, (r + 1) R) of the
-// tile, R = 128 / S.  Each CTA's buffer (in its pipeline stages, idle once
+// tile, R = R_ROWS / S (R_ROWS = 128, or 32 / 64 for skinny tiles, the rows
+// that can hold outputs).  Each CTA's buffer (in its pipeline stages, idle once
 // the whole cluster holds complete accumulators) has S slots, slot s holding
 // rank s's partial of the rows this CTA finishes, stored by 16-byte column
 // group q and row: group (s, q) is R + 1 rows of 16 bytes, so
@@ -376,7 +377,8 @@ __device__ __forceinline__ void split_push(const Params& p, const uint8_t* smem,
     constexpr int BATCH = NCH < 4 ? NCH : 4;
     const int quarter = warp & 3, half = (warp - EPI_WARP0) >> 2;
     const int row = quarter * 32 + lane;  // accumulator row (TMEM lane)
-    const int S = p.ksplit, rows = BM / S;
+    if (row >= CF::R_ROWS) return;        // skinny tiles: rows past R_ROWS hold no output
+    const int S = p.ksplit, rows = CF::R_ROWS / S;
     const int rank = (int)(blockIdx.x % (unsigned)S);
     const int dst = row / rows, lr = row % rows;
     const bool local = dst == rank;
@@ -423,7 +425,7 @@ __device__ __forceinline__ void split_finish(const Params& p, const uint8_t* sme
     constexpr int U = 8;
     const int S = p.ksplit;
     const int rank = (int)(blockIdx.x % (unsigned)S);
-    const int rows = BM / S;
+    const int rows = CF::R_ROWS / S;
     const int tile = (int)(blockIdx.x / (unsigned)S);
     const int tr = tile % p.tiles_r, tc = tile / p.tiles_r;
     const int r0 = tr * BM, c0 = tc * BN;
@@ -2002,7 +2004,7 @@ Plan make_plan(int M, int N, int K, int num_sms, bool packed = false)
         int lim = num_sms;
         if (g_grid_limit > 0 && g_grid_limit < lim) lim = g_grid_limit;
         int split_bn = 256;
-        if (!pl.swap && pl.r_rows == 128 && force_split > 1)
+        if (!pl.swap && force_split > 1)
         {
             if (force_split <= pl.k_stages && force_split <= 8 && tiles * force_split < (1LL << 31))
             {
@@ -2029,6 +2031,26 @@ Plan make_plan(int M, int N, int K, int num_sms, bool packed = false)
                         pl.ksplit = S;
                         split_bn = bn;
                     }
+                }
+            }
+        }
+        else if (!pl.swap && pl.r_rows < 128 && force_split != 0 && !overridden)
+        {
+            // Skinny (decode) tiles with room for every tile's split on the SMs:
+            // the stream-K owner of a tile otherwise waits for its contributors'
+            // partials through L2 (16x8192x8192: streaming done at ~5 us, the
+            // last owner at ~15 us).  The largest S in 8, 4, 2 leaving every CTA
+            // 4 or more K stages, clusters of 8 only for up to 8 tiles (more of
+            // them do not fit at a time).  Back to back: 16x8192x8192 16.4 ->
+            // 12.6 us, 32x4096x4096 13.9 -> 9.2, 16x1024x8192 14.9 -> 9.7 (S = 8),
+            // 64x14336x4096 16.5 -> 13.0.
+            for (int S : {8, 4, 2})
+            {
+                if (S == 8 && tiles > 8) continue;
+                if (tiles * S <= lim && pl.k_stages >= 4 * S)
+                {
+                    pl.ksplit = S;
+                    break;
                 }
             }
         }

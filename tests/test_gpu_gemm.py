@@ -143,11 +143,17 @@ def test_cta_pair_path(force_env, M, N, K, macro, grid, bn):
     (4, 129, 784, 4160, "plain", 128),
     (2, 200, 1024, 2304, "macro", 128),
     (4, 1024, 1024, 5120, "plain", 128),
+    (4, 16, 784, 4160, "plain", 256),     # skinny tiles (32 rows), 17 stages over 4
+    (2, 48, 1024, 2304, "macro", 256),    # 64-row tiles, macro-block scales
+    (8, 1, 512, 2048, "plain", 256),      # M = 1, 4 rows per rank
+    (4, 24, 1280, 3072, "packed", 256),   # skinny packed weights
+    (4, 16, 8192, 8192, "plain", 0),      # skinny, default plan
 ])
 def test_cluster_split_k(force_env, S, M, N, K, kind, bn):
     """Cluster split-K: the S CTAs of a cluster take S K ranges of one tile
-    (128 x 256, or 128 x 128) and add their fp32 partials through
-    distributed shared memory, each finishing 128 / S rows."""
+    (128 x 256, 128 x 128, or a skinny tile of 32 or 64 rows by 256) and add
+    their fp32 partials through distributed shared memory, each finishing
+    1/S of the tile's rows."""
     import mbs_b200
     if bn:
         force_env(MBS_KSPLIT=S, MBS_SPLIT_BN=bn)
