@@ -16,6 +16,15 @@ inside the timed region.  Under torchrun every rank runs its own workload
 (weak scaling: replicas, no collective in the timed region) and the JSON
 line reports the max time over ranks.
 
+The default line carries three more measurements beside the headline:
+`decode` (config[1], M = 1/4/16/32: HBM GB/s per call back to back from a
+CUDA graph, eager back to back as bench_one.py:34-47 times, and one call
+after an L2 flush) and `configs` (config[0] per call, config[3] TFLOPS), both
+on one GPU only, and `sharded` on every rank count (config[4]: quantise +
+N-sharded GEMM + exchange of the C shards so every rank holds all of C;
+strong scaling, max over ranks, with parity against the oracle on each
+rank's shard and checksums of the exchanged blocks).
+
 `--impl reference` times the reference's CPU path (the dequantise-then-matmul
 oracle of test_gemm_a4w4.py:28-44, restated in oracle/) on the host cores on
 a bounded row sample of the same workload.
@@ -66,6 +75,9 @@ def parse():
                     help="--workload sharded with chunks > 1: SMs left free for the NCCL kernels")
     ap.add_argument("--skip-extras", action="store_true",
                     help="skip the e2e and CPU-baseline legs (profiling runs)")
+    ap.add_argument("--no-extra-configs", action="store_true",
+                    help="skip the decode, other-config and sharded objects of the default line")
+    ap.add_argument("--sharded-steps", type=int, default=10)
     ap.add_argument("--soak-s", type=float, default=1.5,
                     help="seconds of untimed steps right before the timed region, so the "
                          "clock sampler sees the GPU under this load")
@@ -365,19 +377,23 @@ def run_mbs(args):
     peaks, src = load_peaks()
     traffic = load_traffic(args.workload, M)
     if args.workload == "prefill":
-        peak = FP4_PER_BF16 * float(peaks["bf16_tflops"])
-        roof = {"bound": "tensor", "achieved": round(kernel_tflops, 2), "peak": round(peak, 1),
-                "unit": "TFLOP/s", "frac": round(kernel_tflops / peak, 4), "traffic": traffic,
-                "peak_source": f"4 x bf16_tflops of {src} (dense FP4:BF16 = 4:1)",
-                "kernel_ms": round(kernel_ms, 5)}
-        # the measured mxf4 tensor-pipe peak of this GPU (MMA-only probe), beside the derived one
+        # MEASURED_PEAKS.json holds no FP4 figure: the denominator is the mxf4
+        # tensor-pipe rate measured here by the probe (the prefill kernel's own
+        # instruction, operands resident, no memory traffic); 4 x the measured
+        # bf16 cuBLAS rate is reported beside it
         from mbs_b200.probe import mxf4_peak_probe
         pr = mxf4_peak_probe(groups=20000, device=dev)
-        roof["peak_probe"] = {"tflops": round(pr["tflops"], 1), "sm_mhz": round(pr["sm_mhz"], 1),
-                              "cycles_per_mma": round(pr["cycles_per_mma"], 2),
-                              "frac": round(kernel_tflops / pr["tflops"], 4),
-                              "what": "mbs_mxf4_peak_probe: back-to-back 256x256x64 pair MMAs, "
-                                      "operands resident in shared memory, no memory traffic"}
+        peak = float(pr["tflops"])
+        peak4 = FP4_PER_BF16 * float(peaks["bf16_tflops"])
+        roof = {"bound": "tensor", "achieved": round(kernel_tflops, 2), "peak": round(peak, 1),
+                "unit": "TFLOP/s", "frac": round(kernel_tflops / peak, 4), "traffic": traffic,
+                "peak_source": "measured this run: mbs_mxf4_peak_probe (back-to-back 256x256x64 "
+                               "tcgen05 kind::mxf4 pair MMAs, operands resident in shared memory)",
+                "peak_probe": {"tflops": round(peak, 1), "sm_mhz": round(pr["sm_mhz"], 1),
+                               "cycles_per_mma": round(pr["cycles_per_mma"], 2)},
+                "peak_4x_bf16": {"tflops": round(peak4, 1), "frac": round(kernel_tflops / peak4, 4),
+                                 "source": f"4 x bf16_tflops of {src} (dense FP4:BF16 = 4:1)"},
+                "kernel_ms": round(kernel_ms, 5)}
     else:
         nbytes = N * K // 2 + N * K // 32 + M * K // 2 + M * K // 32 + M * N * 2
         gbs = nbytes / (kernel_ms * 1e-3) / 1e9
@@ -408,6 +424,13 @@ def run_mbs(args):
         line["isolated_call"] = isolated
     if rank == 0 and world == 1:
         line["cpu_baseline"] = cpu_baseline(M, N, K)
+    if args.workload == "prefill" and not args.no_extra_configs:
+        del A, B, As, Bs, out, flush, flush_rd, lanes, hA, hB, hAs, hBs
+        torch.cuda.empty_cache()
+        if world == 1:
+            line["decode"] = decode_object(dev, peaks)
+            line["configs"] = configs_object(dev)
+        line["sharded"] = sharded_object(args, world, rank, dev)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -452,6 +475,278 @@ def cpu_baseline(M, N, K, budget_s=20.0):
                       f"cast), best of {len(times)}"}
 
 
+def _events(n):
+    import torch
+    return [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
+
+
+def _per_call_us(call, flush_fn, steps=20, reps=3, eager_iters=50):
+    """Three per-call times of one operator call (microseconds):
+    graph  -- `steps` calls captured in one CUDA graph, replayed back to back
+              (median of `reps` replays): the launch cost overlaps the
+              previous call, as in a serving step;
+    eager  -- bench_one.py:34-47's method: 10 warm-up calls, then events
+              around `eager_iters` back-to-back eager calls;
+    isolated -- one call after an L2 flush, events around it (median of 5)."""
+    import torch
+    stream = torch.cuda.current_stream()
+    for _ in range(10):
+        call()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(eager_iters):
+        call()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    eager = e0.elapsed_time(e1) * 1e3 / eager_iters
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for _ in range(steps):
+            call()
+    graph.replay()
+    torch.cuda.synchronize()
+    g = []
+    for _ in range(reps):
+        e0.record(stream)
+        graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        g.append(e0.elapsed_time(e1) * 1e3 / steps)
+    del graph
+    iso = []
+    for i in range(5):
+        flush_fn(i)
+        torch.cuda._sleep(100000)  # the host queues the call while the GPU is still busy
+        e0.record(stream)
+        call()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        iso.append(e0.elapsed_time(e1) * 1e3)
+    return statistics.median(g), eager, statistics.median(iso)
+
+
+def _flusher(dev):
+    import torch
+    buf = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.int32, device=dev)
+    rd = torch.zeros(L2_FLUSH_BYTES // 4, dtype=torch.int32, device=dev)
+
+    def flush(i):
+        buf.fill_(i)
+        rd.sum()
+    return flush
+
+
+def decode_object(dev, peaks):
+    """BASELINE config[1] (decode, N = 57344, K = 8192, M in {1, 4, 16, 32};
+    activations N(0,1), weights N(0,0.02), both quantised on the device).
+    HBM-bound: algorithmic bytes = weights + their scales + activations +
+    their scales + bf16 out, against the measured copy rate and 8 TB/s."""
+    import torch
+
+    import mbs_b200
+    N, K = 57344, 8192
+    g = torch.Generator(device=dev).manual_seed(4242)
+    w = (torch.randn(N, K, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    qw, sw = mbs_b200.quantize_mxfp4(w, shuffle=False)
+    del w
+    B, Bs = mbs_b200.shuffle_weight(qw), mbs_b200.shuffle_scales(sw, K)
+    del qw, sw
+    flush = _flusher(dev)
+    hbm = float(peaks["hbm_gbs"])
+    res = {"workload": "cfg1 decode N=57344 K=8192 (Llama-3-70B gate+up), MBS factors off",
+           "method": "graph: 20 calls in one CUDA graph replayed back to back (median of 3); eager: "
+                     "bench_one.py:34-47 (10 warm-up, 50 eager calls back to back); isolated: one call "
+                     "after an L2 flush (median of 5); GB/s = algorithmic bytes / per-call time",
+           "peak_measured_gbs": hbm}
+    for M in (1, 4, 16, 32):
+        x = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
+        A, As = mbs_b200.quantize_mxfp4(x, shuffle=True)
+        out = torch.empty(((M + 31) // 32 * 32, N), dtype=torch.bfloat16, device=dev)
+        nbytes = N * K // 2 + N * K // 32 + M * K // 2 + M * K // 32 + M * N * 2
+        gus, eus, ius = _per_call_us(lambda: mbs_b200.gemm_a4w4(A, B, As, Bs, out=out), flush)
+        gbs = nbytes / (gus * 1e-6) / 1e9
+        res[f"M={M}"] = {"graph_us": round(gus, 2), "eager_us": round(eus, 2), "isolated_us": round(ius, 2),
+                         "gbs": round(gbs, 1), "frac_measured": round(gbs / hbm, 4),
+                         "frac_8tbs": round(gbs / 8000.0, 4),
+                         "eager_gbs": round(nbytes / (eus * 1e-6) / 1e9, 1),
+                         "isolated_gbs": round(nbytes / (ius * 1e-6) / 1e9, 1),
+                         "algorithmic_bytes": nbytes}
+    del B, Bs
+    torch.cuda.empty_cache()
+    return res
+
+
+def configs_object(dev):
+    """The other single-GPU configs of BASELINE.json: config[0] (256x512x1024
+    with MBS factors, latency-bound) per call, and config[3] (4096x7168x18432,
+    macro-block B scales, activations with 1 % x20 outliers, MBS factors) in
+    TFLOPS with L2 flushed before every call."""
+    import torch
+
+    import mbs_b200
+    from mbs_b200 import _lib
+    flush = _flusher(dev)
+    g = torch.Generator(device=dev).manual_seed(99)
+    res = {}
+    M, N, K = 256, 512, 1024
+    x = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
+    w = torch.randn(N, K, device=dev, generator=g).to(torch.bfloat16)
+    A, As = mbs_b200.quantize_mxfp4(x, shuffle=True)
+    qw, sw = mbs_b200.quantize_mxfp4(w, shuffle=False)
+    B, Bs = mbs_b200.shuffle_weight(qw), mbs_b200.shuffle_scales(sw, K)
+    fa = torch.randint(0, 256, (M,), dtype=torch.uint8, device=dev, generator=g)
+    fb = torch.randint(0, 256, (N,), dtype=torch.uint8, device=dev, generator=g)
+    out = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+    gus, eus, ius = _per_call_us(lambda: mbs_b200.gemm_a4w4(A, B, As, Bs, fa, fb, out=out), flush)
+    res["cfg0"] = {"workload": "256x512x1024 + MBS factors", "graph_us": round(gus, 2),
+                   "eager_us": round(eus, 2), "isolated_us": round(ius, 2),
+                   "tflops_graph": round(2.0 * M * N * K / (gus * 1e-6) / 1e12, 2)}
+    M, N, K = 4096, 7168, 18432
+    x = torch.randn(M, K, device=dev, generator=g)
+    x = torch.where(torch.rand(M, K, device=dev, generator=g) < 0.01, x * 20, x).to(torch.bfloat16)
+    w = (torch.randn(N, K, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    A, As = mbs_b200.quantize_mxfp4(x, shuffle=True)
+    qw, mb = mbs_b200.quantize_mxfp4_macro(w)
+    del x, w
+    B = mbs_b200.shuffle_weight(qw)
+    fa = torch.randint(0, 256, (M,), dtype=torch.uint8, device=dev, generator=g)
+    fb = torch.randint(0, 256, (N,), dtype=torch.uint8, device=dev, generator=g)
+    out = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+
+    def call():
+        mbs_b200.gemm_a4w4_macro(A, B, As, mb, fa, fb, out=out)
+    for _ in range(3):
+        call()
+    L = _lib.lib()
+    steps = 10
+    ev, kev = _events(steps), _events(steps)
+    for a, b in kev:
+        a.record()
+        b.record()
+    torch.cuda.synchronize()
+    for i in range(steps):
+        flush(i)
+        L.mbs_set_profile_events(kev[i][0].cuda_event, kev[i][1].cuda_event)
+        ev[i][0].record()
+        call()
+        ev[i][1].record()
+    L.mbs_set_profile_events(None, None)
+    torch.cuda.synchronize()
+    ms = statistics.median(a.elapsed_time(b) for a, b in ev)
+    kms = statistics.median(a.elapsed_time(b) for a, b in kev)
+    flops = 2.0 * M * N * K
+    res["cfg3"] = {"workload": "4096x7168x18432 macro-block B scales + MBS factors, L2 flushed per call",
+                   "call_ms": round(ms, 4), "tflops": round(flops / (ms * 1e-3) / 1e12, 1),
+                   "kernel_ms": round(kms, 4), "kernel_tflops": round(flops / (kms * 1e-3) / 1e12, 1)}
+    torch.cuda.empty_cache()
+    return res
+
+
+def sharded_object(args, world, rank, dev):
+    """BASELINE config[4] on all `world` ranks: A bf16 [16384, 8192] N(0,1),
+    the same on every rank and quantised on each; the MXFP4 weight
+    [57344, 8192] (N(0,0.02)) split by output columns, N/world rows per rank;
+    each rank's GEMM writes its C shard and the shards are exchanged so every
+    rank holds all of C.  Timed with CUDA events per step, max over ranks.
+    Parity: each rank's shard against the CPU oracle on sampled rows/columns,
+    and the exchange by checksums (every block a rank received equals the
+    block its owner computed)."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import mbs_b200
+    from mbs_b200.sharded import ShardedA4W4
+    from oracle import mxfp4_oracle as O
+
+    own_group = False
+    if not dist.is_initialized():
+        import socket
+        with socket.socket() as s_:
+            s_.bind(("127.0.0.1", 0))
+            port = s_.getsockname()[1]
+        dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=0, world_size=1,
+                                device_id=dev)
+        own_group = True
+    M, N, K = 16384, 57344, 8192
+    nl = N // world
+    x = torch.randn(M, K, device=dev, generator=torch.Generator(device=dev).manual_seed(77)).to(torch.bfloat16)
+    gw = torch.Generator(device=dev).manual_seed(1000 + rank)
+    w = (torch.randn(nl, K, device=dev, generator=gw) * 0.02).to(torch.bfloat16)
+    qw, sw = mbs_b200.quantize_mxfp4(w, shuffle=False)
+    B, Bs = mbs_b200.shuffle_weight(qw), mbs_b200.shuffle_scales(sw, K)
+    del w
+    layer = ShardedA4W4(B, Bs, N, K)
+    exchange = args.exchange
+    if exchange == "auto":
+        exchange = layer.default_exchange(x)
+    chunks = args.chunks if args.chunks is not None else layer.default_chunks(exchange)
+    stream = torch.cuda.current_stream(dev)
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        dist.barrier()
+        ev = _events(args.sharded_steps)
+        for a, b in ev:
+            a.record(stream)
+            fn()
+            b.record(stream)
+        torch.cuda.synchronize()
+        dist.barrier()
+        return statistics.median(a.elapsed_time(b) for a, b in ev)
+
+    local_ms = timed(lambda: layer.local(x))
+    layer_ms = timed(lambda: layer(x, chunks=chunks, comm_sms=args.comm_sms, exchange=exchange))
+    t = torch.tensor([local_ms, layer_ms], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    local_ms, layer_ms = float(t[0]), float(t[1])
+    # parity
+    out = layer(x, chunks=chunks, comm_sms=args.comm_sms, exchange=exchange)  # [world, M, nl]
+    torch.cuda.synchronize()
+    mine = out[rank]
+    rows = np.sort(np.random.default_rng(rank).choice(M, 64, replace=False))
+    cols = np.sort(np.random.default_rng(100 + rank).choice(nl, 256, replace=False))
+    qa, sa = mbs_b200.quantize_mxfp4(x[torch.from_numpy(rows).to(dev)], shuffle=False)
+    tc = torch.from_numpy(cols).to(dev)
+    ref = O.gemm_ref(qa.cpu().numpy(), qw[tc].cpu().numpy(), sa.cpu().numpy(), sw[tc].cpu().numpy())
+    bound = O.gemm_abs_bound(qa.cpu().numpy(), qw[tc].cpu().numpy(), sa.cpu().numpy(), sw[tc].cpu().numpy())
+    got = mine[torch.from_numpy(rows).to(dev)][:, tc].float().cpu().numpy()
+    ok, ratio, nbad = O.check_gemm(got, ref, bound)
+    # exchange: int64 sums of the bf16 bit patterns, exact and order-independent
+    sums = torch.stack([out[r].view(torch.int16).sum(dtype=torch.int64) for r in range(world)])
+    owner_sums = torch.empty(world, dtype=torch.int64, device=dev)
+    dist.all_gather_into_tensor(owner_sums, sums[rank].reshape(1))
+    xchg_ok = bool(torch.equal(sums, owner_sums))
+    flags = torch.tensor([1 if ok else 0, 1 if xchg_ok else 0], device=dev)
+    dist.all_reduce(flags, op=dist.ReduceOp.MIN)
+    rat = torch.tensor([ratio], device=dev)
+    dist.all_reduce(rat, op=dist.ReduceOp.MAX)
+    flops = 2.0 * M * N * K
+    res = {"workload": "cfg4 M=16384 N=57344 K=8192: quantise A on every rank + N-sharded GEMM + exchange of "
+                       "the bf16 C shards (every rank ends with all of C)",
+           "scaling": "strong", "n_ranks": world, "layer_ms": round(layer_ms, 4),
+           "tflops": round(flops / (layer_ms * 1e-3) / 1e12, 1),
+           "quant_gemm_ms": round(local_ms, 4),
+           "quant_gemm_tflops_per_rank": round(flops / world / (local_ms * 1e-3) / 1e12, 1),
+           "exposed_exchange_ms": round(layer_ms - local_ms, 4),
+           "exchange": "none (one rank holds all of C)" if world == 1 else layer.describe_exchange(exchange, chunks),
+           "bytes_received_per_rank": (world - 1) * M * nl * 2,
+           "parity": {"oracle_sample_ok": bool(flags[0].item()), "max_ratio": round(float(rat.item()), 4),
+                      "sample": "64 rows x 256 columns of every rank's shard against the CPU oracle",
+                      "exchange_checksums_ok": bool(flags[1].item())},
+           "steps": args.sharded_steps, "timing": "median of per-step CUDA events, max over ranks"}
+    del out, mine
+    dist.barrier()
+    layer.close()
+    dist.barrier()
+    if own_group:
+        dist.destroy_process_group()
+    return res
+
+
 def run_reference(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -486,87 +781,24 @@ def run_reference(args):
 
 
 def run_sharded(args):
-    """A bf16 [16384, 8192] quantised on every rank, the
-    MXFP4 weight [57344, 8192] N-sharded across the ranks, local GEMM, then an
-    NCCL all-gather of the bf16 C shards.  Timed per step with CUDA events on
-    the current stream; max over ranks."""
+    """`--workload sharded`: BASELINE config[4] alone (the `sharded` object of
+    the default line, printed as its own line)."""
     import torch
     import torch.distributed as dist
-
-    import mbs_b200
-    from mbs_b200.sharded import ShardedA4W4
-
     world, rank, local = dist_setup(args)
     dev = torch.device("cuda", local)
-    M, N, K = 16384, 57344, 8192
-    nl = N // world
-    g = torch.Generator(device=dev).manual_seed(77 + rank)
-    x = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
-    w = (torch.randn(nl, K, device=dev, generator=g) * 0.02).to(torch.bfloat16)
-    qw, sw = mbs_b200.quantize_mxfp4(w, shuffle=False)
-    B = mbs_b200.shuffle_weight(qw)
-    Bs = mbs_b200.shuffle_scales(sw, K)
-    del w, qw, sw
-    if world == 1:
-        import torch.distributed as _d  # single-rank group so the same code path runs
-        if not _d.is_initialized():
-            os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-            os.environ.setdefault("MASTER_PORT", "29533")
-            _d.init_process_group("nccl", rank=0, world_size=1, device_id=dev)
-    layer = ShardedA4W4(B, Bs, N, K)
-    exchange = args.exchange
-    if exchange == "auto":
-        exchange = "copy" if world == 2 else "nccl"
-    chunks = args.chunks if args.chunks is not None else (4 if exchange == "copy" else 1)
-    stream = torch.cuda.current_stream(dev)
-
-    def timed(fn):
-        for _ in range(max(args.warmup, 3)):
-            fn()
-        torch.cuda.synchronize()
-        dist.barrier()
-        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-              for _ in range(args.steps)]
-        for i in range(args.steps):
-            ev[i][0].record(stream)
-            fn()
-            ev[i][1].record(stream)
-        torch.cuda.synchronize()
-        dist.barrier()
-        return sum(a.elapsed_time(b) for a, b in ev) / args.steps
-
-    local_ms = timed(lambda: layer.local(x))           # quantise + GEMM alone
-    total_ms = timed(lambda: layer(x, chunks=chunks, comm_sms=args.comm_sms,
-                                   exchange=exchange))  # the whole layer
-    t = torch.tensor([local_ms, total_ms], device=dev)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    local_ms, total_ms = float(t[0]), float(t[1])
-    flops = 2.0 * M * N * K
+    res = sharded_object(args, world, rank, dev)
     if rank == 0:
         print(json.dumps({
-            "metric": "A4W4 MXFP4 fused quant + N-sharded GEMM + all-gather TFLOPS (config[4])",
-            "value": round(flops / (total_ms * 1e-3) / 1e12, 2), "unit": "TFLOPS", "n_gpus": world,
-            "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": round(total_ms, 4),
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "e2m1 (fp32 accumulate, bf16 out)", "data": "synthetic",
-            "config": {"workload": "cfg4 M=16384 N=57344 K=8192 N-sharded", "parallelism": f"N-shards x{world}"},
-            "quant_gemm_ms": round(local_ms, 4),
-            "quant_gemm_tflops": round(flops / world / (local_ms * 1e-3) / 1e12 * world, 2),
-            "exposed_exchange_ms": round(total_ms - local_ms, 4),
-            "exchange": "none (one rank holds the whole output)" if world == 1 else
-                        ("NCCL all-gather" if chunks == 1 else
-                         f"{chunks} row chunks, NCCL send/recv overlapped with the next chunk's GEMM "
-                         f"({args.comm_sms} SMs left to NCCL)") if exchange == "nccl" else
-                        f"{chunks} row chunks pushed into the peers' buffers by copy engines (CUDA IPC), "
-                        f"overlapped with the next chunk's GEMM",
-            "bytes_received_per_rank": (world - 1) * M * nl * 2,
-        }), flush=True)
-    torch.cuda.synchronize()
-    dist.barrier()
-    if layer._peerbuf is not None:  # every rank is done with every buffer
-        layer._peerbuf.close()
-    dist.barrier()
-    dist.destroy_process_group()
+            "metric": "A4W4 MXFP4 quant + N-sharded GEMM + exchange TFLOPS (config[4])",
+            "value": res["tflops"], "unit": "TFLOPS", "n_gpus": world, "steps": args.sharded_steps,
+            "warmup": 3, "ms_per_step": res["layer_ms"], "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "e2m1 (fp32 accumulate, bf16 out)", "data": "synthetic",
+            "config": {"workload": res["workload"], "parallelism": f"N-shards x{world}"},
+            "sharded": res}), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def main():

@@ -251,6 +251,31 @@ int mbs_set_profile_events(void* before_main, void* after_main);
 int mbs_set_grid_limit(int max_ctas);
 
 /*
+ * Tuning and test hook: on this host thread, force parts of the schedule of
+ * the following GEMM calls (and of the workspace-size and kernels-per-call
+ * queries, which plan the same way), so that every schedule can be reached on
+ * small shapes.  A field at its "auto" value keeps the planner's own choice;
+ * ov == NULL clears every override.
+ *   schedule   0 auto, 1 stream-K, 2 data-parallel
+ *   grid       0 auto, else at most this many CTAs
+ *   pair       -1 auto, 0 never CTA pairs, 1 CTA pairs whenever data-parallel
+ *   swap       -1 auto, 1 weights as the 128-row operand when M <= 64
+ *   pair_bn    0 auto, 256 or 384: CTA-pair tile width
+ *   pair_wide  0 auto, else this many 384-wide column tiles, then 256-wide ones
+ *   ksplit     -1 auto, 0 off, 2, 4 or 8: cluster split-K factor
+ *   split_bn   0 auto (256), 128 or 256: split-K tile width (256 when M <= 64)
+ * Returns MBS_ERR_INVALID_ARGUMENT (and changes nothing) for a value outside
+ * these sets.  Replaces the reference's compile-time tile override
+ * (-DMBS_FORCE_TILE_ENV, kernel/gemm_a4w4.hip:1094-1102) with an explicit
+ * call, so the launch path reads no environment variable.
+ */
+typedef struct mbs_plan_override
+{
+    int schedule, grid, pair, swap, pair_bn, pair_wide, ksplit, split_bn;
+} mbs_plan_override;
+int mbs_set_plan_override(const mbs_plan_override* ov);
+
+/*
  * Peer-memory plumbing for exchanging GEMM output shards between the GPUs of
  * one node (the N-sharded layer) with copy-engine
  * transfers over NVLink instead of SM kernels:
@@ -267,6 +292,21 @@ int mbs_ipc_open(const void* handle, void** peer_ptr);
 int mbs_ipc_close(void* peer_ptr);
 int mbs_ipc_free(void* ptr);
 int mbs_copy_async(void* dst, const void* src, size_t bytes, void* stream);
+
+/*
+ * Test hook for the failure path of the kernels' bounded waits: on this host
+ * thread, while `on` != 0, the stream-K contributors of the following GEMM
+ * calls write their partial tiles but never release their completion flags
+ * (a flag that nothing sets).  The owner of each split tile then waits until
+ * its limit (2 s of %globaltimer) runs out, records MBS_ERR_DEVICE_TIMEOUT in
+ * the device error word and finishes its kernel without the partials, so the
+ * output is wrong and mbs_device_error reports the timeout.  The wait is the
+ * last step of the owner's kernel, with no copy or MMA in flight, and the
+ * flag words stay zero.  No reference counterpart (the reference's only
+ * failure path is its launcher's false return,
+ * interface/gemm_a4w4_pybind.cpp:56-61).
+ */
+int mbs_set_withhold_release(int on);
 
 /*
  * Sticky device-side error word of the current device: 0, or the code of a

@@ -39,6 +39,8 @@ SIGNATURES = {
     "mbs_device_error": (_c_int, [ctypes.POINTER(_c_int), _c_int]),
     "mbs_set_profile_events": (_c_int, [_c_void_p, _c_void_p]),
     "mbs_set_grid_limit": (_c_int, [_c_int]),
+    "mbs_set_plan_override": (_c_int, [_c_void_p]),
+    "mbs_set_withhold_release": (_c_int, [_c_int]),
     "mbs_ipc_alloc": (_c_int, [_c_size_t, ctypes.POINTER(_c_void_p), _c_void_p]),
     "mbs_ipc_open": (_c_int, [_c_void_p, ctypes.POINTER(_c_void_p)]),
     "mbs_ipc_close": (_c_int, [_c_void_p]),
@@ -51,6 +53,21 @@ SIGNATURES = {
                                                                                 _c_void_p]),
     "mbs_mxf4_peak_probe": (_c_int, [_c_int] + [ctypes.POINTER(ctypes.c_double)] * 3 + [_c_void_p]),
 }
+
+
+
+class PlanOverride(ctypes.Structure):
+    """mbs_plan_override of include/mbs_gemm_a4w4.h (field defaults = "auto")."""
+    _fields_ = [(name, _c_int) for name in ("schedule", "grid", "pair", "swap", "pair_bn", "pair_wide",
+                                            "ksplit", "split_bn")]
+    AUTO = dict(schedule=0, grid=0, pair=-1, swap=-1, pair_bn=0, pair_wide=0, ksplit=-1, split_bn=0)
+
+    def __init__(self, **kw):
+        unknown = set(kw) - set(self.AUTO)
+        if unknown:
+            raise ValueError(f"unknown plan override fields: {sorted(unknown)}")
+        super().__init__(**{**self.AUTO, **{k: int(v) for k, v in kw.items()}})
+
 
 _lock = threading.Lock()
 _lib = None

@@ -82,6 +82,7 @@ struct Params
                                   // 384 wide, the rest (up to tiles_c) 256 wide
     int img_b_blocks;             // ... 128-row blocks per K stage of the B scale images
     int ksplit;                   // single-CTA kernel, > 1: cluster split-K over clusters of ksplit CTAs
+    int withhold_release;         // test hook: stream-K contributors never release their flags
 };
 
 constexpr int align_up(int x, int a) { return (x + a - 1) / a * a; }
@@ -365,8 +366,12 @@ __device__ __forceinline__ int split_off(int s, int q, int lr, int rows, int c4)
 // The hand-over (epilogue threads, after a cluster barrier): each CTA pushes
 // its fp32 partial straight from TMEM, rows [j R, (j + 1) R) into slot r of
 // rank j's buffer; its own rows with plain shared stores (~3x the rate of
-// stores into another CTA).  With S <= 4 a warp's 32 rows have a single
-// destination, so the branch is warp-uniform.  An empty K range pushes zeros.
+// stores into another CTA).  When R = R_ROWS / S >= 32 a warp's 32 rows have a
+// single destination and the local/remote branch is warp-uniform; skinny
+// tiles (R_ROWS = 32 or 64) with a larger S spread one warp's rows over
+// several CTAs, which stays correct but diverges.  S is 2, 4 or 8 (the
+// planner accepts nothing else), so R is a whole number of rows and every row
+// has a destination rank below S.  An empty K range pushes zeros.
 template <class CF>
 __device__ __forceinline__ void split_push(const Params& p, const uint8_t* smem, uint32_t tmem_base, int warp,
                                            int lane, bool any)
@@ -381,6 +386,7 @@ __device__ __forceinline__ void split_push(const Params& p, const uint8_t* smem,
     const int S = p.ksplit, rows = CF::R_ROWS / S;
     const int rank = (int)(blockIdx.x % (unsigned)S);
     const int dst = row / rows, lr = row % rows;
+    if (dst >= S) return;  // never taken for S in {2, 4, 8}; keeps mapa inside the cluster
     const bool local = dst == rank;
     const uint32_t rbase = mapa_shared(smem_u32(smem), (uint32_t)dst);
     uint8_t* lbase = const_cast<uint8_t*>(smem);
@@ -891,7 +897,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 if (lane == 0) mbar_arrive(&acc_empty[acc]);
                 __threadfence();
                 named_bar_sync(1, NUM_EPI_THREADS);
-                if (et == 0) st_release_gpu(&p.flags[blockIdx.x], 1u);
+                // (the failure-path test withholds the release: the owner's bounded wait then runs out)
+                if (et == 0 && !p.withhold_release) st_release_gpu(&p.flags[blockIdx.x], 1u);
             }
             else
             {
@@ -1895,6 +1902,10 @@ thread_local cudaEvent_t g_ev_before = nullptr, g_ev_after = nullptr;
 // as the NCCL kernels of an overlapped all-gather.
 thread_local int g_grid_limit = 0;
 
+// Test hook (mbs_set_withhold_release): stream-K contributors of the next
+// launches from this host thread never release their completion flags.
+thread_local int g_withhold_release = 0;
+
 
 int record_before(cudaStream_t s)
 {
@@ -1915,6 +1926,13 @@ int env_int(const char* name, int dflt)
     const char* v = getenv(name);
     return (v != nullptr && *v != 0) ? atoi(v) : dflt;
 }
+
+// Schedule overrides of the following plans on this host thread
+// (mbs_set_plan_override; "auto" values keep the planner's own choice).  The
+// launch path reads no environment variable: the tests reach every schedule
+// on small shapes through this explicit, thread-local hook.
+constexpr mbs_plan_override kAutoOverride = {0, 0, -1, -1, 0, 0, -1, 0};
+thread_local mbs_plan_override g_ov = kAutoOverride;
 
 // The pair GEMM starts behind its scale-image pre-pass by programmatic
 // dependent launch; MBS_PAIR_PDL=0 launches it in plain stream order.
@@ -1954,17 +1972,17 @@ constexpr int kMaxGrid = (int)(kFlagBytes / sizeof(unsigned));
 // activation rows per stage and uses stream-K so every SM streams an equal
 // share of the weights; larger M runs data-parallel tiles (stream-K only for
 // a very deep K over few tiles).
-//   MBS_FORCE_SCHEDULE=1 (stream-K) / 2 (data-parallel), MBS_FORCE_GRID=<G>:
-//   debug overrides used by the tests to reach every schedule on small shapes.
+// The thread's plan override (mbs_set_plan_override) can force the schedule,
+// the grid, CTA pairs, the swapped form, pair tile widths and cluster split-K.
 Plan make_plan(int M, int N, int K, int num_sms, bool packed = false)
 {
     Plan pl{};
     // Skinny M keeps the weights in the N = 256 operand (one 128x256x64 MMA
     // per 8 KB of weights) and loads only the activation rows that exist;
-    // MBS_FORCE_SWAP=1 selects the swapped form (weights as the 128-row operand).
+    // An override swap = 1 selects the swapped form (weights as the 128-row operand).
+    const mbs_plan_override& ov = g_ov;
     pl.swap = false;
-    const int force_swap = env_int("MBS_FORCE_SWAP", -1);
-    if (force_swap == 1 && M <= 64 && !packed) pl.swap = true;
+    if (ov.swap == 1 && M <= 64 && !packed) pl.swap = true;
     pl.bn = pl.swap ? (M <= 32 ? 32 : 64) : 256;
     pl.r_rows = pl.swap ? 128 : (M <= 32 ? 32 : (M <= 64 ? 64 : 128));
     pl.k_stages = (K + BK - 1) / BK;
@@ -1993,23 +2011,25 @@ Plan make_plan(int M, int N, int K, int num_sms, bool packed = false)
     // 11.5 at 128 x S4; 1024x1024x2048 12.3 -> 9.3 at 128 x S2;
     // 128x7168x16384 29.4 -> 21.3 at 256 x S4).  A split needs 8 or more K
     // stages (256x512x1024, 4 stages: 8.0 -> 9.9 us at S = 2); clusters of 8
-    // fit too few at a time.  The schedule overrides below turn it off;
-    // MBS_KSPLIT=S forces S (2, 4 or 8) with MBS_SPLIT_BN=128 or 256
-    // (default 256), MBS_KSPLIT=0 turns it off.
+    // fit too few at a time.  The schedule overrides below turn it off; an
+    // override ksplit = S forces S (2, 4 or 8, checked when the override is
+    // set, so R_ROWS / S is always a whole number of rows) with split_bn = 128
+    // or 256 (256 for skinny tiles, whose configurations exist only at 256),
+    // ksplit = 0 turns it off.
     pl.ksplit = 1;
     {
-        const int force_split = env_int("MBS_KSPLIT", -1);
-        const bool overridden = env_int("MBS_FORCE_SCHEDULE", 0) != 0 || env_int("MBS_FORCE_GRID", 0) != 0 ||
-                                env_int("MBS_FORCE_PAIR", -1) == 1;
+        const int force_split = ov.ksplit;
+        const bool overridden = ov.schedule != 0 || ov.grid != 0 || ov.pair == 1;
         int lim = num_sms;
         if (g_grid_limit > 0 && g_grid_limit < lim) lim = g_grid_limit;
         int split_bn = 256;
         if (!pl.swap && force_split > 1)
         {
-            if (force_split <= pl.k_stages && force_split <= 8 && tiles * force_split < (1LL << 31))
+            if ((force_split == 2 || force_split == 4 || force_split == 8) && force_split <= pl.k_stages &&
+                tiles * force_split < (1LL << 31))
             {
                 pl.ksplit = force_split;
-                split_bn = (env_int("MBS_SPLIT_BN", 256) == 128 && !packed) ? 128 : 256;
+                split_bn = (ov.split_bn == 128 && !packed && pl.r_rows == 128) ? 128 : 256;
             }
         }
         else if (!pl.swap && pl.r_rows == 128 && force_split != 0 && !overridden && pl.k_stages >= 8)
@@ -2072,12 +2092,12 @@ Plan make_plan(int M, int N, int K, int num_sms, bool packed = false)
     // 10-30 % slower than data-parallel tiles at M in 128..2048 even when
     // those leave SMs idle.
     pl.sk = pl.swap || pl.r_rows < 128 || (tiles * 4 <= num_sms && pl.k_stages >= 64);
-    const int force = env_int("MBS_FORCE_SCHEDULE", 0);
+    const int force = ov.schedule;
     if (force == 1) pl.sk = true;
     if (force == 2) pl.sk = false;
     int G = num_sms < kMaxGrid ? num_sms : kMaxGrid;
     if (g_grid_limit > 0 && g_grid_limit < G) G = g_grid_limit;
-    const int fg = env_int("MBS_FORCE_GRID", 0);
+    const int fg = ov.grid;
     if (fg > 0 && fg < G) G = fg;
     const long long units = pl.sk ? tiles * pl.k_stages : tiles;
     // Stream-K ranges of at least 8 K-stages (16 for 128-row partials) per
@@ -2096,7 +2116,7 @@ Plan make_plan(int M, int N, int K, int num_sms, bool packed = false)
     // scale-image pre-pass (a second launch) costs more than the pair saves.
     const long long tr2 = (M + 2 * BM - 1) / (2 * BM);
     const long long t2 = tr2 * ((N + 255) / 256);
-    const int force_pair = env_int("MBS_FORCE_PAIR", -1);
+    const int force_pair = ov.pair;
     pl.pair = !packed && !pl.swap && !pl.sk && force_pair != 0 && (t2 >= 4 || force_pair == 1);
     if (pl.pair)
     {
@@ -2106,11 +2126,11 @@ Plan make_plan(int M, int N, int K, int num_sms, bool packed = false)
         // followed by 256-wide ones (5 stages of 44 KB; a 256-wide tile
         // there measures ~1.1x a 256-wide tile of the first).  Tiles go to
         // the clusters round-robin, wide ones first; take the layout whose
-        // busiest cluster has the least work.  MBS_PAIR_BN=256 / 384 forces
-        // all-256 / all-384 tiles, MBS_PAIR_WIDE=nw a given mix.
+        // busiest cluster has the least work.  An override pair_bn = 256 / 384
+        // forces all-256 / all-384 tiles, pair_wide = nw a given mix.
         const int c = G / 2;
-        const int force_bn = env_int("MBS_PAIR_BN", 0);
-        const int force_wide = env_int("MBS_PAIR_WIDE", 0);
+        const int force_bn = ov.pair_bn;
+        const int force_wide = ov.pair_wide;
         auto busiest = [&](long long T, long long A, double w_wide, double w_narrow) {
             double mx = 0;
             const long long cl = T < c ? T : c;
@@ -2445,6 +2465,7 @@ int launch_cfg(const Problem& pb, const Plan& pl, const DeviceInfo& dev, void* w
     p.packed_b = pb.packed ? pb.B : nullptr;
     p.act_rows = act_box_rows(pb, pl);
     p.ksplit = pl.ksplit;
+    p.withhold_release = g_withhold_release;
     if (pl.ksplit > 1 && !CF::SPLIT_OK) return fail(MBS_ERR_CUDA, "cluster split-K planned for a configuration without it");
 
     cudaLaunchConfig_t cfg = {};
@@ -2644,6 +2665,36 @@ extern "C" int mbs_set_grid_limit(int max_ctas)
     mbs::clear_error();
     if (max_ctas < 0) return mbs::fail(MBS_ERR_INVALID_ARGUMENT, "mbs_set_grid_limit: max_ctas < 0");
     mbs::gemm::g_grid_limit = max_ctas;
+    return MBS_OK;
+}
+
+extern "C" int mbs_set_plan_override(const mbs_plan_override* ov)
+{
+    mbs::clear_error();
+    if (ov == nullptr)
+    {
+        mbs::gemm::g_ov = mbs::gemm::kAutoOverride;
+        return MBS_OK;
+    }
+    const bool ok = (ov->schedule >= 0 && ov->schedule <= 2) && ov->grid >= 0 &&
+                    (ov->pair >= -1 && ov->pair <= 1) && (ov->swap == -1 || ov->swap == 0 || ov->swap == 1) &&
+                    (ov->pair_bn == 0 || ov->pair_bn == 256 || ov->pair_bn == 384) && ov->pair_wide >= 0 &&
+                    (ov->ksplit == -1 || ov->ksplit == 0 || ov->ksplit == 2 || ov->ksplit == 4 || ov->ksplit == 8) &&
+                    (ov->split_bn == 0 || ov->split_bn == 128 || ov->split_bn == 256);
+    if (!ok)
+        return mbs::fail(MBS_ERR_INVALID_ARGUMENT,
+                         "mbs_set_plan_override: schedule %d grid %d pair %d swap %d pair_bn %d pair_wide %d "
+                         "ksplit %d split_bn %d outside the allowed values",
+                         ov->schedule, ov->grid, ov->pair, ov->swap, ov->pair_bn, ov->pair_wide, ov->ksplit,
+                         ov->split_bn);
+    mbs::gemm::g_ov = *ov;
+    return MBS_OK;
+}
+
+extern "C" int mbs_set_withhold_release(int on)
+{
+    mbs::clear_error();
+    mbs::gemm::g_withhold_release = on != 0 ? 1 : 0;
     return MBS_OK;
 }
 

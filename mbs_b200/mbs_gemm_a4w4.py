@@ -8,8 +8,16 @@ A's device, returned as ``out[:M]``).  Two additions: the MBS factors are
 optional (the reference's 6-argument form and the 4-argument form used by
 bench_one.py:31 both work), and ``out=`` accepts a caller buffer.
 
-    import mbs_b200.mbs_gemm_a4w4 as mbs_gemm_a4w4   # or put mbs_b200/ on sys.path
+    import mbs_b200.mbs_gemm_a4w4 as mbs_gemm_a4w4
     out = mbs_gemm_a4w4.gemm_a4w4(A, B, A_scale, B_scale, A_factor, B_factor)
+
+The reference's drivers import their extension as a top-level module after
+putting its directory on the path (`sys.path.insert(0, <dir>); import
+mbs_gemm_a4w4`, bench_one.py:11,27 and test_gemm_a4w4.py:12,80).  The same
+works with this package's directory on the path: imported that way, this file
+loads the package and makes `mbs_gemm_a4w4` an alias of
+`mbs_b200.mbs_gemm_a4w4`, so both names share one module (one workspace
+cache, one library handle).
 
 Launches go to the current torch CUDA stream of A's device, asynchronously.
 """
@@ -18,13 +26,23 @@ from __future__ import annotations
 
 import contextlib
 import ctypes
+import importlib
+import os
+import sys
 import threading
 
 import torch
 
-from . import _lib
+if not __package__:
+    # top-level import from the package directory: become the package's module
+    _root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    if _root not in sys.path:
+        sys.path.insert(0, _root)
+    sys.modules[__name__] = importlib.import_module("mbs_b200.mbs_gemm_a4w4")
+else:
+    from . import _lib
 
-__all__ = ["gemm_a4w4", "gemm_a4w4_macro", "workspace_for", "device_error", "grid_limit"]
+__all__ = ["gemm_a4w4", "gemm_a4w4_macro", "workspace_for", "device_error", "grid_limit", "plan_override"]
 
 # Workspace layout of include/mbs_gemm_a4w4.h: the first WS_FLAG_BYTES bytes
 # are the stream-K flag words (zero between launches), the rest is scratch.
@@ -58,6 +76,21 @@ def grid_limit(max_ctas: int):
         yield
     finally:
         _lib.call("mbs_set_grid_limit", 0)
+
+
+@contextlib.contextmanager
+def plan_override(**fields):
+    """Force parts of the GEMM schedule for the calls made (from this thread)
+    inside the block: schedule (1 stream-K, 2 data-parallel), grid, pair,
+    swap, pair_bn, pair_wide, ksplit, split_bn -- the fields of
+    mbs_plan_override in include/mbs_gemm_a4w4.h.  A tuning and test hook; the
+    planner's own choice is restored on exit."""
+    ov = _lib.PlanOverride(**fields)
+    _lib.call("mbs_set_plan_override", ctypes.byref(ov))
+    try:
+        yield
+    finally:
+        _lib.call("mbs_set_plan_override", None)
 
 
 def cached_workspace(need: int, device: torch.device) -> torch.Tensor | None:

@@ -116,9 +116,9 @@ class ShardedA4W4:
         if exchange == "auto":
             # measured on B200 (config[4]): copy engines win at 2 ranks
             # (2.14 vs 3.73 ms), NCCL's all-gather from 4 ranks up (3.29 vs 3.65 ms)
-            exchange = "copy" if self.world == 2 and x.is_cuda else "nccl"
+            exchange = self.default_exchange(x)
             if exchange == "copy" and chunks < 2:
-                chunks = 4
+                chunks = self.default_chunks(exchange)
         if exchange == "copy" and self.world > 1:
             return self._forward_copy(x, A_factor, layout, max(1, chunks))
         if chunks > 1:
@@ -136,6 +136,30 @@ class ShardedA4W4:
         if layout == "rows":
             return gathered.permute(1, 0, 2).reshape(M, self.world * nl)
         raise ValueError(f"layout must be 'blocked' or 'rows', got {layout!r}")
+
+    def default_exchange(self, x: torch.Tensor) -> str:
+        """The exchange `forward(exchange="auto")` takes for this group size."""
+        return "copy" if self.world == 2 and x.is_cuda else "nccl"
+
+    @staticmethod
+    def default_chunks(exchange: str) -> int:
+        return 4 if exchange == "copy" else 1
+
+    def describe_exchange(self, exchange: str, chunks: int) -> str:
+        if exchange == "copy":
+            return (f"{chunks} row chunks pushed into the peers' buffers by copy engines (CUDA IPC), "
+                    f"overlapped with the next chunk's GEMM")
+        if chunks > 1:
+            return f"{chunks} row chunks, NCCL send/recv overlapped with the next chunk's GEMM"
+        return f"NCCL all-gather over {self.world} ranks after the GEMM"
+
+    def close(self):
+        """Release the peer buffers (collective: call on every rank once no
+        rank uses the layer's results any more)."""
+        if self._peerbuf is not None:
+            torch.cuda.synchronize(self.B.device)
+            self._peerbuf.close()
+            self._peerbuf = None
 
     def _global_rank(self, r: int) -> int:
         return r if self.group is None else dist.get_global_rank(self.group, r)

@@ -123,3 +123,37 @@ def test_python_layer_fails_loudly_without_library(monkeypatch, tmp_path):
     monkeypatch.setattr(_lib, "LIB_PATH", str(tmp_path / "missing.so"))
     with pytest.raises(RuntimeError, match="no non-CUDA fallback"):
         _lib.lib()
+
+
+def test_plan_override_is_validated_and_steers_the_planner(lib):
+    """mbs_set_plan_override: values outside the documented sets are refused
+    (a cluster split-K factor that does not divide the tile rows would address
+    CTAs outside the cluster); accepted ones steer the host-side planner, seen
+    through the workspace-size and kernels-per-call queries (no device needed:
+    without one the planner assumes 148 SMs)."""
+    from mbs_b200 import _lib
+
+    def setov(**kw):
+        return lib.mbs_set_plan_override(ctypes.byref(_lib.PlanOverride(**kw)))
+    try:
+        for bad in (dict(ksplit=3), dict(ksplit=5), dict(ksplit=16), dict(split_bn=64), dict(pair_bn=320),
+                    dict(schedule=3), dict(grid=-1), dict(swap=2), dict(pair=2)):
+            assert setov(**bad) == 1, bad
+        auto_ws = lib.mbs_gemm_a4w4_workspace_size(16, 57344, 8192)
+        assert auto_ws > 4096  # config[1]: stream-K with 32-row partials
+        # forced cluster split-K on a skinny tile: no workspace; split_bn 128 is
+        # ignored there (skinny configurations exist only 256 wide)
+        assert setov(ksplit=4, split_bn=128) == 0
+        assert lib.mbs_gemm_a4w4_workspace_size(16, 1024, 4096) == 0
+        assert lib.mbs_gemm_a4w4_kernels_per_call(16, 1024, 4096) == 1
+        # forced stream-K on 17 CTAs: flags + 17 partial slots of 32 x 256 fp32
+        assert setov(schedule=1, grid=17) == 0
+        assert lib.mbs_gemm_a4w4_workspace_size(16, 1024, 4096) == 4096 + 17 * 32 * 256 * 4
+        # forced CTA pairs: two launches (scale images + GEMM)
+        assert setov(schedule=2, pair=1) == 0
+        assert lib.mbs_gemm_a4w4_kernels_per_call(512, 512, 1024) == 2
+        assert setov(schedule=2, pair=0) == 0
+        assert lib.mbs_gemm_a4w4_kernels_per_call(512, 512, 1024) == 1
+    finally:
+        assert lib.mbs_set_plan_override(None) == 0
+    assert lib.mbs_gemm_a4w4_workspace_size(16, 57344, 8192) == auto_ws

@@ -2,8 +2,6 @@
 bf16 bias, on every schedule, against the oracle's
 ((c * (a_f * b_f)) * alpha + bias) -> bf16."""
 
-import os
-
 import numpy as np
 import pytest
 import torch
@@ -14,27 +12,14 @@ from tests.gpu_helpers import Case, assert_gemm_close, bf16_bits
 pytestmark = pytest.mark.gpu
 
 SCHEDULES = {
-    "pair": dict(MBS_FORCE_SCHEDULE="2", MBS_FORCE_PAIR="1", MBS_PAIR_BN="256"),  # CTA pairs
-    "pair384": dict(MBS_FORCE_SCHEDULE="2", MBS_FORCE_PAIR="1", MBS_PAIR_BN="384"),
-    "pair_mix": dict(MBS_FORCE_SCHEDULE="2", MBS_FORCE_PAIR="1", MBS_PAIR_WIDE="1"),
-    "dp_single": dict(MBS_FORCE_SCHEDULE="2", MBS_FORCE_PAIR="0"),
-    "stream_k": dict(MBS_FORCE_SCHEDULE="1", MBS_FORCE_GRID="17"),
-    "swap": dict(MBS_FORCE_SWAP="1"),
-    "ksplit": dict(MBS_KSPLIT="4"),  # cluster split-K
+    "pair": dict(schedule="2", pair="1", pair_bn="256"),  # CTA pairs
+    "pair384": dict(schedule="2", pair="1", pair_bn="384"),
+    "pair_mix": dict(schedule="2", pair="1", pair_wide="1"),
+    "dp_single": dict(schedule="2", pair="0"),
+    "stream_k": dict(schedule="1", grid="17"),
+    "swap": dict(swap="1"),
+    "ksplit": dict(ksplit="4"),  # cluster split-K
 }
-
-
-@pytest.fixture
-def env():
-    keys = ("MBS_FORCE_SCHEDULE", "MBS_FORCE_GRID", "MBS_FORCE_PAIR", "MBS_FORCE_SWAP", "MBS_PAIR_BN",
-            "MBS_PAIR_WIDE", "MBS_KSPLIT")
-    saved = {k: os.environ.get(k) for k in keys}
-    yield os.environ
-    for k, v in saved.items():
-        if v is None:
-            os.environ.pop(k, None)
-        else:
-            os.environ[k] = v
 
 
 @pytest.mark.parametrize("sched,M,N,K", [("pair", 512, 512, 1024), ("pair384", 300, 1040, 1024),
@@ -43,9 +28,9 @@ def env():
                                          ("stream_k", 40, 2048, 2048), ("swap", 24, 1024, 512),
                                          ("ksplit", 200, 768, 2048)])
 @pytest.mark.parametrize("alpha,with_bias", [(0.5, False), (-3.25, True), (1.0, True), (7.0, True)])
-def test_alpha_bias(env, sched, M, N, K, alpha, with_bias):
+def test_alpha_bias(plan, sched, M, N, K, alpha, with_bias):
     import mbs_b200
-    env.update(SCHEDULES[sched])
+    plan(**SCHEDULES[sched])
     c = Case(M, N, K, seed=M + N, factors=True)
     bias = (torch.randn(N, generator=torch.Generator().manual_seed(N)) * 4).to(torch.bfloat16)
     out = mbs_b200.gemm_a4w4(c.A, c.B, c.A_scale, c.B_scale, c.A_factor, c.B_factor,

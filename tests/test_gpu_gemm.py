@@ -6,14 +6,12 @@ where ref is the reference oracle (fp32 dequant-matmul, factor multiply, RNE
 bf16; test_gemm_a4w4.py:28-69).
 """
 
-import os
-
 import numpy as np
 import pytest
 import torch
 
 from oracle import mxfp4_oracle as O
-from tests.gpu_helpers import Case, assert_gemm_close
+from tests.gpu_helpers import Case, assert_gemm_close, full_check
 
 pytestmark = pytest.mark.gpu
 
@@ -23,22 +21,6 @@ def _gemm(case, factors=True, out=None):
     return mbs_b200.gemm_a4w4(case.A, case.B, case.A_scale, case.B_scale,
                               case.A_factor if factors else None,
                               case.B_factor if factors else None, out=out)
-
-
-@pytest.fixture
-def force_env():
-    saved = {}
-
-    def set_(**kw):
-        for k, v in kw.items():
-            saved.setdefault(k, os.environ.get(k))
-            os.environ[k] = str(v)
-    yield set_
-    for k, v in saved.items():
-        if v is None:
-            os.environ.pop(k, None)
-        else:
-            os.environ[k] = v
 
 
 @pytest.mark.parametrize("factors", [False, True])
@@ -65,8 +47,8 @@ def test_ragged_shapes_with_factors(M, N, K):
 @pytest.mark.parametrize("M,N,K", [(2, 2048, 4096), (24, 1024, 2048), (48, 4096, 1024),
                                    (512, 1024, 2048)])
 @pytest.mark.parametrize("grid", [3, 17, 148])
-def test_stream_k_splits(force_env, M, N, K, grid):
-    force_env(MBS_FORCE_SCHEDULE=1, MBS_FORCE_GRID=grid)
+def test_stream_k_splits(plan, M, N, K, grid):
+    plan(schedule=1, grid=grid)
     c = Case(M, N, K, seed=grid, factors=True)
     out = _gemm(c)
     torch.cuda.synchronize()
@@ -78,23 +60,20 @@ def test_stream_k_splits(force_env, M, N, K, grid):
     assert torch.equal(out, out2)
 
 
-def test_one_workspace_serves_every_schedule(force_env):
+def test_one_workspace_serves_every_schedule(plan):
     """Shapes and schedules in sequence on one stream share the cached
     workspace: scale images and wide stream-K partial slots written by one
     launch must never read as another schedule's completion flags."""
     seq = [
-        (dict(MBS_FORCE_PAIR=1), (512, 512, 1024)),                         # CTA pairs: scale images
+        (dict(pair=1), (512, 512, 1024)),                         # CTA pairs: scale images
         (dict(), (300, 1024, 2048)),                                        # cluster split-K: no workspace
-        (dict(MBS_FORCE_SCHEDULE=1), (300, 1024, 2048)),                    # stream-K, 128-row slots
-        (dict(MBS_FORCE_SCHEDULE=1, MBS_FORCE_GRID=17), (2, 2048, 4096)),   # 3 CTAs per tile
-        (dict(MBS_FORCE_SCHEDULE=1, MBS_FORCE_GRID=29), (48, 1024, 4096)),  # 64-row slots
-        (dict(MBS_FORCE_SCHEDULE=1, MBS_FORCE_GRID=17), (2, 2048, 4096)),
+        (dict(schedule=1), (300, 1024, 2048)),                    # stream-K, 128-row slots
+        (dict(schedule=1, grid=17), (2, 2048, 4096)),   # 3 CTAs per tile
+        (dict(schedule=1, grid=29), (48, 1024, 4096)),  # 64-row slots
+        (dict(schedule=1, grid=17), (2, 2048, 4096)),
     ]
     for i, (env, (M, N, K)) in enumerate(seq):
-        for k in ("MBS_FORCE_SCHEDULE", "MBS_FORCE_GRID", "MBS_FORCE_PAIR"):
-            force_env(**{k: ""})
-            os.environ.pop(k)
-        force_env(**env)
+        plan(**env)
         c = Case(M, N, K, seed=100 + i, factors=True)
         out = _gemm(c)
         torch.cuda.synchronize()
@@ -106,7 +85,7 @@ def test_one_workspace_serves_every_schedule(force_env):
 @pytest.mark.parametrize("M,N,K,macro,grid", [(512, 1024, 2048, False, 0), (300, 1024, 1088, False, 0),
                                               (256, 1040, 512, False, 0), (512, 1024, 2048, True, 0),
                                               (700, 768, 1600, True, 0), (1000, 2000, 768, False, 6)])
-def test_cta_pair_path(force_env, M, N, K, macro, grid, bn):
+def test_cta_pair_path(plan, M, N, K, macro, grid, bn):
     """The CTA-pair kernel with all tiles 256 columns wide, all 384 (an N=256
     plus an N=128 MMA), and mixed (one 384-wide column tile, then 256-wide
     ones in the 384-column configuration): ragged M (rows past M are computed
@@ -114,14 +93,14 @@ def test_cta_pair_path(force_env, M, N, K, macro, grid, bn):
     inside a narrow tile, a partial last K stage, both B scale layouts, and
     several tiles per cluster."""
     import mbs_b200
-    env = dict(MBS_FORCE_SCHEDULE=2, MBS_FORCE_PAIR=1)
+    env = dict(schedule=2, pair=1)
     if bn == "mix":
-        env["MBS_PAIR_WIDE"] = 1
+        env["pair_wide"] = 1
     else:
-        env["MBS_PAIR_BN"] = bn
+        env["pair_bn"] = bn
     if grid:
-        env["MBS_FORCE_GRID"] = grid
-    force_env(**env)
+        env["grid"] = grid
+    plan(**env)
     c = Case(M, N, K, seed=M + K + (1 if bn == "mix" else bn), factors=True, macro=macro)
     if macro:
         out = mbs_b200.gemm_a4w4_macro(c.A, c.B, c.A_scale, c.B_scale, c.A_factor, c.B_factor)
@@ -149,14 +128,14 @@ def test_cta_pair_path(force_env, M, N, K, macro, grid, bn):
     (4, 24, 1280, 3072, "packed", 256),   # skinny packed weights
     (4, 16, 8192, 8192, "plain", 0),      # skinny, default plan
 ])
-def test_cluster_split_k(force_env, S, M, N, K, kind, bn):
+def test_cluster_split_k(plan, S, M, N, K, kind, bn):
     """Cluster split-K: the S CTAs of a cluster take S K ranges of one tile
     (128 x 256, 128 x 128, or a skinny tile of 32 or 64 rows by 256) and add
     their fp32 partials through distributed shared memory, each finishing
     1/S of the tile's rows."""
     import mbs_b200
     if bn:
-        force_env(MBS_KSPLIT=S, MBS_SPLIT_BN=bn)
+        plan(ksplit=S, split_bn=bn)
     c = Case(M, N, K, seed=M + N + S + bn, factors=True, macro=kind == "macro",
              b_std=0.02 if kind == "packed" else 1.0)
     if kind == "macro":
@@ -172,8 +151,8 @@ def test_cluster_split_k(force_env, S, M, N, K, kind, bn):
 
 
 @pytest.mark.parametrize("M,N,K", [(384, 1024, 512), (1000, 2048, 256)])
-def test_data_parallel_schedule(force_env, M, N, K):
-    force_env(MBS_FORCE_SCHEDULE=2, MBS_FORCE_GRID=7)
+def test_data_parallel_schedule(plan, M, N, K):
+    plan(schedule=2, grid=7)
     c = Case(M, N, K, seed=3, factors=True)
     out = _gemm(c)
     torch.cuda.synchronize()
@@ -193,15 +172,15 @@ def test_output_canary_rows_untouched():
     assert_gemm_close(buf[:M], ref, bound, "canary")
 
 
-@pytest.mark.parametrize("env", [dict(MBS_FORCE_SCHEDULE=2, MBS_FORCE_PAIR=1, MBS_PAIR_BN=256),
-                                 dict(MBS_FORCE_SCHEDULE=2, MBS_FORCE_PAIR=1, MBS_PAIR_BN=384),
-                                 dict(MBS_FORCE_SCHEDULE=2, MBS_FORCE_PAIR=0),
-                                 dict(MBS_FORCE_SCHEDULE=1, MBS_FORCE_GRID=5)])
-def test_output_only_16_byte_aligned(force_env, env):
+@pytest.mark.parametrize("env", [dict(schedule=2, pair=1, pair_bn=256),
+                                 dict(schedule=2, pair=1, pair_bn=384),
+                                 dict(schedule=2, pair=0),
+                                 dict(schedule=1, grid=5)])
+def test_output_only_16_byte_aligned(plan, env):
     """The epilogues store 32 bytes per instruction when `out` is 32-byte
     aligned; an output 16 bytes past such a boundary takes the 16-byte
     stores, with the same values and nothing written outside it."""
-    force_env(**env)
+    plan(**env)
     M, N, K = 300, 1040, 512
     c = Case(M, N, K, seed=21, factors=True)
     Mpad = (M + 31) // 32 * 32
@@ -269,9 +248,10 @@ def test_device_error_word_clear():
 
 
 @pytest.mark.parametrize("M", [1, 4, 16, 32])
-def test_decode_full_size_sampled(M):
-    """Decode shape N=57344, K=8192 at full size; parity on
-    a sample of output columns (the oracle dequantises only those weight rows)."""
+def test_decode_full_size(M):
+    """Decode shape N=57344, K=8192 at full size with
+    MBS factors: every output element against the oracle (its weight rows
+    dequantised in blocks of 8192)."""
     import mbs_b200
     N, K = 57344, 8192
     g = torch.Generator(device="cuda").manual_seed(100 + M)
@@ -286,19 +266,14 @@ def test_decode_full_size_sampled(M):
     fb = torch.randint(0, 256, (N,), dtype=torch.uint8, device="cuda", generator=g)
     out = mbs_b200.gemm_a4w4(qa, B, sa_sh, B_scale, fa, fb)
     torch.cuda.synchronize()
-    cols = np.sort(np.random.default_rng(M).choice(N, 2048, replace=False))
-    tc = torch.from_numpy(cols).cuda()
-    ref = O.gemm_ref(qa.cpu().numpy(), qw[tc].cpu().numpy(), sa.cpu().numpy(), sw[tc].cpu().numpy(),
-                     fa.cpu().numpy(), fb[tc].cpu().numpy())
-    bound = O.gemm_abs_bound(qa.cpu().numpy(), qw[tc].cpu().numpy(), sa.cpu().numpy(),
-                             sw[tc].cpu().numpy())
-    assert_gemm_close(out[:, tc], ref, bound, f"decode M={M}")
+    full_check(out, qa.cpu().numpy(), sa.cpu().numpy(), qw.cpu().numpy(), sw.cpu().numpy(),
+               fa.cpu().numpy(), fb.cpu().numpy(), what=f"config[1] decode M={M}")
 
 
-def test_prefill_8192_cubed_sampled_and_scale_property():
-    """M=N=K=8192: parity on a 256x256 sample, and the
-    size-independent property that adding 1 to every B scale byte doubles
-    every output exactly."""
+def test_prefill_8192_cubed_full_and_scale_property():
+    """M=N=K=8192 on the planner's own CTA-pair layout:
+    every output element against the oracle, and the size-independent
+    property that adding 1 to every B scale byte doubles every output exactly."""
     import mbs_b200
     n = 8192
     g = torch.Generator(device="cuda").manual_seed(8192)
@@ -314,21 +289,16 @@ def test_prefill_8192_cubed_sampled_and_scale_property():
     out2 = mbs_b200.gemm_a4w4(qa, B, sa_sh, B_scale + 1)
     torch.cuda.synchronize()
     assert torch.equal(out2.float(), out.float() * 2)
-    rows = np.sort(np.random.default_rng(1).choice(n, 256, replace=False))
-    cols = np.sort(np.random.default_rng(2).choice(n, 256, replace=False))
-    tr, tcol = torch.from_numpy(rows).cuda(), torch.from_numpy(cols).cuda()
-    ref = O.gemm_ref(qa[tr].cpu().numpy(), qw[tcol].cpu().numpy(), sa[tr].cpu().numpy(),
-                     sw[tcol].cpu().numpy())
-    bound = O.gemm_abs_bound(qa[tr].cpu().numpy(), qw[tcol].cpu().numpy(), sa[tr].cpu().numpy(),
-                             sw[tcol].cpu().numpy())
-    assert_gemm_close(out[tr][:, tcol], ref, bound, "8192^3")
+    full_check(out, qa.cpu().numpy(), sa.cpu().numpy(), qw.cpu().numpy(), sw.cpu().numpy(),
+               what="config[2] 8192^3")
 
 
-def test_config3_macro_full_size_sampled():
+def test_config3_macro_full_size():
     """BASELINE config[3] at full size (4096 x 7168 x 18432; macro-block B
     scales, N(0, 0.02) weights, activations with 1 % x20 outliers, MBS
-    factors): the planner's own mixed 384/256-column CTA-pair layout, parity
-    on a 128 x 128 sample of rows and columns."""
+    factors) on the planner's own mixed 384/256-column CTA-pair layout: every
+    output element against the oracle, and adding 1 to every A scale byte
+    doubles every output exactly."""
     import mbs_b200
     M, N, K = 4096, 7168, 18432
     g = torch.Generator(device="cuda").manual_seed(33)
@@ -343,16 +313,47 @@ def test_config3_macro_full_size_sampled():
     fa = torch.randint(0, 256, (M,), dtype=torch.uint8, device="cuda", generator=g)
     fb = torch.randint(0, 256, (N,), dtype=torch.uint8, device="cuda", generator=g)
     out = mbs_b200.gemm_a4w4_macro(qa, B, sa_sh, mb, fa, fb)
+    # shuffled A scales: bytes past the real ones are padding (127), +1 keeps the ratio exact
+    # only where scales exist, so double the plain scale bytes and re-shuffle
+    sa2 = mbs_b200.shuffle_scales(sa + 1, K)
+    out2 = mbs_b200.gemm_a4w4_macro(qa, B, sa2, mb, fa, fb)
     torch.cuda.synchronize()
-    rows = np.sort(np.random.default_rng(3).choice(M, 128, replace=False))
-    cols = np.sort(np.random.default_rng(4).choice(N, 128, replace=False))
-    tr, tcol = torch.from_numpy(rows).cuda(), torch.from_numpy(cols).cuda()
-    sb = O.expand_macro_scales(mb.cpu().numpy(), N, K)[cols]
-    qa_s, qw_s, sa_s = qa[tr].cpu().numpy(), qw[tcol].cpu().numpy(), sa[tr].cpu().numpy()
-    ref = O.gemm_ref(qa_s, qw_s, sa_s, sb, fa[tr].cpu().numpy().reshape(-1, 1),
-                     fb[tcol].cpu().numpy().reshape(-1, 1))
-    bound = O.gemm_abs_bound(qa_s, qw_s, sa_s, sb)
-    assert_gemm_close(out[tr][:, tcol], ref, bound, "config[3] full size")
+    assert torch.equal(out2.float(), out.float() * 2)
+    sb = O.expand_macro_scales(mb.cpu().numpy(), N, K)
+    full_check(out, qa.cpu().numpy(), sa.cpu().numpy(), qw.cpu().numpy(), sb,
+               fa.cpu().numpy(), fb.cpu().numpy(), what="config[3] macro 4096x7168x18432")
+
+
+def test_bounded_wait_runs_out_and_the_next_launch_is_clean(plan):
+    """The failure path of a bounded device wait: with the stream-K
+    contributors' completion flags withheld (mbs_set_withhold_release, a flag
+    that nothing sets), each split tile's owner waits until its 2 s limit,
+    records MBS_ERR_DEVICE_TIMEOUT and ends its kernel.  The context stays
+    usable: after the error is read and cleared, the next launch on the same
+    workspace matches the oracle (the flag words were never set)."""
+    import ctypes
+
+    import mbs_b200
+    from mbs_b200 import _lib
+    L = _lib.lib()
+    plan(schedule=1, grid=17)  # 16 tiles x 8 K stages over 17 CTAs: every tile is split
+    c = Case(16, 4096, 2048, seed=5, factors=True)
+    assert mbs_b200.device_error(reset=True) == 0
+    assert L.mbs_set_withhold_release(1) == 0
+    try:
+        _gemm(c)
+        code = ctypes.c_int(0)
+        assert L.mbs_device_error(ctypes.byref(code), 0) == 0  # synchronises
+        assert code.value == 7, f"expected MBS_ERR_DEVICE_TIMEOUT (7), got {code.value}"
+    finally:
+        assert L.mbs_set_withhold_release(0) == 0
+    assert mbs_b200.device_error(reset=True) == 7  # read and clear (also zeroes cached flag words)
+    assert mbs_b200.device_error() == 0
+    out = _gemm(c)
+    torch.cuda.synchronize()
+    ref, bound = c.reference()
+    assert_gemm_close(out, ref, bound, "after a device timeout")
+    assert mbs_b200.device_error() == 0
 
 
 @pytest.mark.parametrize("M,N,K", [(256, 512, 1024), (33, 96, 576), (8, 256, 512)])
