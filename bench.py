@@ -68,9 +68,9 @@ def parse():
     ap.add_argument("--chunks", type=int, default=None,
                     help="--workload sharded: row chunks whose exchange overlaps the next chunk's GEMM "
                          "(default 4 on more than one GPU, 1 on one)")
-    ap.add_argument("--exchange", choices=["nccl", "copy", "auto"], default="auto",
-                    help="--workload sharded: exchange the C shards with NCCL, with copy engines "
-                         "through peer memory, or the faster of the two for the GPU count")
+    ap.add_argument("--exchange", choices=["nccl", "copy", "fused", "auto"], default="auto",
+                    help="config[4]: exchange the C shards with NCCL, with copy engines through peer "
+                         "memory, inside the GEMM's epilogue (fused), or auto (fused from 2 GPUs up)")
     ap.add_argument("--comm-sms", type=int, default=16,
                     help="--workload sharded with chunks > 1: SMs left free for the NCCL kernels")
     ap.add_argument("--skip-extras", action="store_true",
@@ -699,7 +699,9 @@ def sharded_object(args, world, rank, dev):
         return statistics.median(a.elapsed_time(b) for a, b in ev)
 
     local_ms = timed(lambda: layer.local(x))
-    layer_ms = timed(lambda: layer(x, chunks=chunks, comm_sms=args.comm_sms, exchange=exchange))
+    # one rank: the layer is the quantiser and the GEMM alone (nothing to exchange)
+    layer_ms = local_ms if world == 1 else timed(
+        lambda: layer(x, chunks=chunks, comm_sms=args.comm_sms, exchange=exchange))
     t = torch.tensor([local_ms, layer_ms], device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     local_ms, layer_ms = float(t[0]), float(t[1])

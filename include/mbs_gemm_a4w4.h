@@ -127,6 +127,50 @@ int mbs_gemm_a4w4_launch_ex(const uint8_t* A, const uint8_t* B, const uint8_t* A
                             const void* bias, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * As mbs_gemm_a4w4_launch_ex, writing every output element to n_dst (1..8)
+ * buffers at once: element (m, n) goes to out_dst[i] + m * ldc + n (bf16
+ * elements) for each i, with ldc >= N and ldc % 8 == 0; out_dst is a host
+ * array of device pointers, each 16-byte aligned.  For an N-sharded layer the
+ * pointers are this GPU's copy of the full output and the peers' copies
+ * (mapped through CUDA IPC or peer access), each offset to this rank's column
+ * block, so the exchange of the output shards happens inside the GEMM's
+ * epilogue, over NVLink, while the tensor cores work on the next tiles.  Each
+ * kernel ends with a system-scope fence: once the launch has completed on
+ * the stream (for example behind an NCCL barrier), every copy holds its
+ * data.  No reference counterpart (the reference has no multi-GPU path);
+ * replaces "GEMM, then NCCL all-gather" for BASELINE config[4].
+ */
+int mbs_gemm_a4w4_launch_multi(const uint8_t* A, const uint8_t* B, const uint8_t* AScale,
+                               const uint8_t* BScale, const uint8_t* AFactor, const uint8_t* BFactor,
+                               void* const* out_dst, int n_dst, long long ldc, int M, int N, int K,
+                               int Mpad, int scaleN_pad, float alpha, const void* bias, void* workspace,
+                               size_t workspace_bytes, void* stream);
+
+/*
+ * Dynamic-quant + GEMM in one call: bf16 activations x [M, ld_x] (row
+ * stride ld_x elements, 16-byte aligned) are quantised to MXFP4 (the
+ * per-1x32 arithmetic of mbs_quantize_mxfp4) and multiplied with the
+ * preshuffled weight B, as mbs_quantize_mxfp4(x, shuffled) followed by
+ * mbs_gemm_a4w4_launch_ws, with bit-identical results.  When the plan runs
+ * on single CTAs (skinny and small M: decode, stream-K, cluster split-K)
+ * the quantiser lives inside the GEMM kernel -- one launch: idle warps
+ * quantise A into the workspace while the producer already streams the
+ * first weight stages, and the A loads wait for it (a grid barrier, or for
+ * cluster split-K each CTA's own K range).  Large M (CTA pairs) launches the
+ * stand-alone quantiser first.  The workspace (mbs_quant_gemm_a4w4_workspace_size,
+ * 256-byte aligned) holds the quantised A and the GEMM's scratch; it must be
+ * zero-filled before first use and is left reusable (including its first
+ * MBS_GEMM_WS_FLAG_BYTES, as for mbs_gemm_a4w4_launch_ws).  Replaces the
+ * quantise-then-GEMM sequence of the reference's drivers (bench_one.py:20-31,
+ * test_gemm_a4w4.py:134-165) for BASELINE config[4]'s "fused dynamic-quant +
+ * GEMM"; the reference has no fused kernel.
+ */
+size_t mbs_quant_gemm_a4w4_workspace_size(int M, int N, int K);
+int mbs_quant_gemm_a4w4_launch(const void* x_bf16, int ld_x, const uint8_t* B, const uint8_t* BScale,
+                               const uint8_t* AFactor, const uint8_t* BFactor, void* out, int M, int N, int K,
+                               int scaleN_pad, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * Macro-block-scaling variant: B's e8m0 scales are shared by 32-row x 32-K
  * blocks and given plainly as BScaleMacro[ceil(N/32)][mb_ld] with
  * mb_ld = roundup(K/32, 16).  A and A_scale are as above.  Spec-defined

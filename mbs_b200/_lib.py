@@ -26,6 +26,12 @@ SIGNATURES = {
     "mbs_gemm_a4w4_launch_noalloc": (_c_int, [_c_void_p] * 7 + [_c_int] * 5 + [_c_void_p]),
     "mbs_gemm_a4w4_launch_ex": (_c_int, [_c_void_p] * 7 + [_c_int] * 5 + [ctypes.c_float, _c_void_p,
                                                                            _c_void_p, _c_size_t, _c_void_p]),
+    "mbs_gemm_a4w4_launch_multi": (_c_int, [_c_void_p] * 6 + [_c_void_p, _c_int, ctypes.c_longlong]
+                                   + [_c_int] * 5 + [ctypes.c_float, _c_void_p, _c_void_p, _c_size_t,
+                                                     _c_void_p]),
+    "mbs_quant_gemm_a4w4_workspace_size": (_c_size_t, [_c_int] * 3),
+    "mbs_quant_gemm_a4w4_launch": (_c_int, [_c_void_p, _c_int] + [_c_void_p] * 5 + [_c_int] * 4
+                                   + [_c_void_p, _c_size_t, _c_void_p]),
     "mbs_gemm_a4w4_macro_launch_ws": (_c_int, [_c_void_p] * 7 + [_c_int] * 6
                                       + [_c_void_p, _c_size_t, _c_void_p]),
     "mbs_quantize_mxfp4": (_c_int, [_c_void_p, _c_int, _c_int, _c_int, _c_void_p, _c_void_p, _c_int,

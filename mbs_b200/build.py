@@ -22,7 +22,7 @@ LIB_PATH = os.path.join(PKG_DIR, LIB_NAME)
 # Debug variant with per-role cycle counters (-DMBS_TIMING=1, mbs_timing_read()).
 TIMING_LIB_PATH = os.path.join(PKG_DIR, "libmbs_gemm_kernel_timing.so")
 SOURCES = ["common.cu", "quant.cu", "gemm.cu", "probe.cu", "ipc.cu"]
-HEADERS = ["common.h", "ptx.cuh"]
+HEADERS = ["common.h", "ptx.cuh", "mx_quant.cuh"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

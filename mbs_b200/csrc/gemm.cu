@@ -47,6 +47,7 @@
 #include <unordered_map>
 
 #include "common.h"
+#include "mx_quant.cuh"
 #include "ptx.cuh"
 
 namespace mbs {
@@ -61,6 +62,8 @@ constexpr int EPI_WARP0 = 4;
 constexpr int NUM_EPI_WARPS = 8;
 constexpr int NUM_EPI_THREADS = NUM_EPI_WARPS * 32;
 
+constexpr int MAX_OUT = 8;  // output copies one launch writes (this GPU's and up to 7 peers')
+
 struct Params
 {
     int M, N, K;
@@ -69,7 +72,7 @@ struct Params
     long long sk_units;
     const uint8_t* a_factor;
     const uint8_t* b_factor;
-    __nv_bfloat16* out;
+    __nv_bfloat16* out;    // == outs[0]
     float* partials;       // [G][BN][BM] fp32, stream-K only
     unsigned* flags;       // [G], stream-K only; zero between launches
     unsigned* err;         // sticky device error word
@@ -83,6 +86,22 @@ struct Params
     int img_b_blocks;             // ... 128-row blocks per K stage of the B scale images
     int ksplit;                   // single-CTA kernel, > 1: cluster split-K over clusters of ksplit CTAs
     int withhold_release;         // test hook: stream-K contributors never release their flags
+    // Output copies: element (m, n) goes to outs[d] + m * ldc + n for every d < n_out (this GPU's
+    // buffer and, for an N-sharded layer, peer GPUs' buffers reached over NVLink).
+    long long ldc;
+    int n_out;
+    __nv_bfloat16* outs[MAX_OUT];
+    // Fused activation quantiser (mbs_quant_gemm_a4w4_launch), single-CTA kernel only:
+    // qmode 0 = A given; 1 = the grid quantises bf16 qx into qa / qsa (the A and A_scale
+    // buffers the TMA maps read) behind a grid barrier (qbar); 2 = every CTA quantises
+    // the A blocks of its own tile rows and K range (cluster split-K).
+    int qmode;
+    int qx_ld;
+    const __nv_bfloat16* qx;
+    uint8_t* qa;
+    uint8_t* qsa;
+    int q_snp;
+    unsigned* qbar;  // [arrived, departed], zero between launches
 };
 
 constexpr int align_up(int x, int a) { return (x + a - 1) / a * a; }
@@ -141,8 +160,8 @@ struct Cfg
         TMEM_NEED <= 32 ? 32 : TMEM_NEED <= 64 ? 64 : TMEM_NEED <= 128 ? 128 : TMEM_NEED <= 256 ? 256 : 512;
     static_assert(TMEM_NEED <= 512, "TMEM budget");
 
-    // barriers: full, sfready, empty [STAGES]; acc_full, acc_empty [2]; tmem slot; abort
-    static constexpr int BAR_BYTES = (3 * STAGES + 4) * 8 + 16;
+    // barriers: full, sfready, empty [STAGES]; acc_full, acc_empty [2]; qready; tmem slot; abort
+    static constexpr int BAR_BYTES = (3 * STAGES + 5) * 8 + 16;
     static constexpr int EPI_BYTES = (BM + 2 * BN) * 4;  // epilogue factor + bias staging
     static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + EPI_BYTES + 1024;  // +1024 alignment slack
     static_assert(SMEM_BYTES <= 232448, "shared memory budget");
@@ -233,6 +252,31 @@ __device__ __forceinline__ void raise_error(const Params& p, volatile int* abort
     atomicExch(p.err, (unsigned)MBS_ERR_DEVICE_TIMEOUT);
 }
 
+// One 16-column (32-byte) chunk of output row m, columns [n, n + 16), into
+// every output copy.  The copy index stays a compile-time constant (the loop
+// is unrolled over MAX_OUT and cut at n_out), so the pointers come straight
+// from the parameter bank.
+__device__ __forceinline__ void store_chunk16(const Params& p, long long m, int n, const uint32_t* w)
+{
+    const long long off = m * p.ldc + n;
+#pragma unroll
+    for (int d = 0; d < MAX_OUT; ++d)
+    {
+        if (d >= p.n_out) break;
+        __nv_bfloat16* dst = p.outs[d] + off;
+        if (p.out_v8)
+        {
+            st_global_v8(dst, w[0], w[1], w[2], w[3], w[4], w[5], w[6], w[7]);
+        }
+        else
+        {
+            uint4* d4 = reinterpret_cast<uint4*>(dst);
+            d4[0] = make_uint4(w[0], w[1], w[2], w[3]);
+            d4[1] = make_uint4(w[4], w[5], w[6], w[7]);
+        }
+    }
+}
+
 // Debug instrumentation (build with -DMBS_TIMING=1): cycles per role and
 // wait site, summed per CTA into g_mbs_timing and read with mbs_timing_read.
 //   0 producer waits on `empty`      1 MMA waits on `acc_empty`
@@ -287,6 +331,52 @@ __device__ __forceinline__ long long flat_s_offset(int r, int b, int snp)
     const int r32 = r & 31, b8 = b & 7;
     return (long long)(r32 >> 4) + (long long)(b8 >> 2) * 2 + (long long)(r32 & 15) * 4 +
            (long long)(b8 & 3) * 64 + (long long)(b >> 3) * 256 + (long long)(r >> 5) * 32 * snp;
+}
+
+// Fused activation quantiser: the octets (8 consecutive K values) o in
+// [0, nrows * width) of the slice rows [r_lo, r_lo + nrows) x octets
+// [j_lo, j_lo + width), o = (r - r_lo) * width + (j - j_lo), taken 32 at a
+// time by warp wbase, wbase + wstride, ...  j_lo and width are multiples of 4,
+// so the 4 lanes of a 32-value block are 4 consecutive lanes and share the
+// block's amax through two xor-shuffles (every lane runs them).  Writes the
+// codes to qa ([M, K/2], plain) and the scale to qsa (flatS), with the same
+// arithmetic as the stand-alone quantiser (mx_quant.cuh).
+__device__ __forceinline__ void fused_quant_slice(const Params& p, int r_lo, int nrows, int j_lo, int width,
+                                                  long long wbase, long long wstride)
+{
+    const int lane = threadIdx.x & 31;
+    const long long total = (long long)nrows * width;
+    for (long long base = wbase * 32; base < total; base += wstride * 32)
+    {
+        const long long o = base + lane;
+        const bool valid = o < total;
+        int r = 0, j = 0;
+        uint32_t w[4] = {0u, 0u, 0u, 0u};
+        if (valid)
+        {
+            r = r_lo + (int)(o / width);
+            j = j_lo + (int)(o - (long long)(r - r_lo) * width);
+            const uint4 v = __ldcg(reinterpret_cast<const uint4*>(p.qx + (long long)r * p.qx_ld) + j);
+            w[0] = v.x;
+            w[1] = v.y;
+            w[2] = v.z;
+            w[3] = v.w;
+        }
+        uint32_t am = mx::amax_bits8(w);
+        am = max(am, __shfl_xor_sync(0xffffffffu, am, 1));
+        am = max(am, __shfl_xor_sync(0xffffffffu, am, 2));
+        if (!valid) continue;
+        const uint32_t sc = mx::scale_from_amax_bits(am);
+        const bool nan_block = sc == 0xFFu;
+        const float inv = __uint_as_float((254u - (nan_block ? 254u : sc)) << 23);
+        reinterpret_cast<uint32_t*>(p.qa + (long long)r * (p.K >> 1))[j] = mx::encode8(w, inv, nan_block);
+        if ((j & 3) == 0) p.qsa[flat_s_offset(r, j >> 2, p.q_snp)] = (uint8_t)sc;
+    }
+}
+
+__device__ __forceinline__ void fence_proxy_async_global()
+{
+    asm volatile("fence.proxy.async.global;" ::: "memory");
 }
 
 // One operand's raw scale bytes for one K-stage (8 groups of 32 K) ->
@@ -496,8 +586,14 @@ __device__ __forceinline__ void split_finish(const Params& p, const uint8_t* sme
             }
             __nv_bfloat162 h0 = __floats2bfloat162_rn(x[0], x[1]);
             __nv_bfloat162 h1 = __floats2bfloat162_rn(x[2], x[3]);
-            *reinterpret_cast<uint2*>(p.out + (size_t)m * p.N + n) =
-                make_uint2(*reinterpret_cast<uint32_t*>(&h0), *reinterpret_cast<uint32_t*>(&h1));
+            const uint2 v = make_uint2(*reinterpret_cast<uint32_t*>(&h0), *reinterpret_cast<uint32_t*>(&h1));
+            const long long off = (long long)m * p.ldc + n;
+#pragma unroll
+            for (int d = 0; d < MAX_OUT; ++d)
+            {
+                if (d >= p.n_out) break;
+                *reinterpret_cast<uint2*>(p.outs[d] + off) = v;
+            }
         }
     }
 }
@@ -519,7 +615,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     uint64_t* empty = sfready + STAGES;
     uint64_t* acc_full = empty + STAGES;
     uint64_t* acc_empty = acc_full + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+    uint64_t* qready = acc_empty + 2;  // fused quantiser: this CTA's share of A is written
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(qready + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     float* epi_f = reinterpret_cast<float*>(smem + STAGES * CF::STAGE_BYTES + CF::BAR_BYTES);
 
@@ -529,6 +626,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #if MBS_TIMING
     const long long t_kernel0 = clock64();
 #endif
+    constexpr int QWARPS = NUM_THREADS / 32 - 2;  // warps 2.. quantise A before their own role
 
     if (threadIdx.x == 0)
     {
@@ -543,6 +641,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             mbar_init(&acc_full[b], 1);
             mbar_init(&acc_empty[b], NUM_EPI_WARPS);
         }
+        mbar_init(qready, QWARPS);
         *abort_flag = 0;
         fence_mbar_init();
         prefetch_tmap(&tm_r);
@@ -574,6 +673,41 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (threadIdx.x == 0 && blockIdx.x < 1024) g_mbs_cta[blockIdx.x * 5 + 1] = globaltimer_ns();
 #endif
 
+    if constexpr (!CF::SWAP)
+    {
+        if (p.qmode != 0 && warp >= 2)
+        {
+            // ------------------------------------------------ fused activation quantiser
+            // Warps 2.. write A (codes + flatS scales) before taking up their own
+            // roles, while the producer already streams the first stages' weights.
+            // qmode 1: the grid shares all of A (the producer then waits on a grid
+            // barrier); qmode 2: each CTA writes the blocks of its own tile rows and
+            // K range (CTAs of other clusters may write the same blocks, with the
+            // same bytes).
+            if (p.qmode == 1)
+            {
+                fused_quant_slice(p, 0, p.M, 0, p.K >> 3, (long long)blockIdx.x * QWARPS + (warp - 2),
+                                  (long long)gridDim.x * QWARPS);
+            }
+            else
+            {
+                Work w0;
+                if (get_work(p, 0, w0))
+                {
+                    const int r_lo = (w0.tile % p.tiles_r) * BM;
+                    const int r_hi = min(p.M, r_lo + CF::R_ROWS);
+                    const int j_lo = w0.k0 * (BK / 8);
+                    const int j_hi = min(p.K >> 3, w0.k1 * (BK / 8));
+                    if (r_hi > r_lo && j_hi > j_lo)
+                        fused_quant_slice(p, r_lo, r_hi - r_lo, j_lo, j_hi - j_lo, warp - 2, QWARPS);
+                }
+            }
+            fence_proxy_async_global();  // the TMA (async proxy) reads these bytes next
+            __syncwarp();
+            if (lane == 0) mbar_arrive(qready);
+        }
+    }
+
     if (warp == 0)
     {
         // ------------------------------------------------ TMA producer
@@ -581,6 +715,37 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         {
             int slot = 0;
             uint32_t phase = 0;
+            // Fused quantiser: the first STAGES stages are armed and their weights
+            // issued at once; their A tiles (and A scales) follow once A is written.
+            int ndef = (!CF::SWAP && p.qmode != 0) ? 0 : -1;  // -1: A is ready
+            int def_slot[STAGES], def_r0[STAGES], def_ks[STAGES];
+            auto a_ready = [&]() {
+                bool ok = mbar_wait(qready, 0, nullptr);
+                if (p.qmode == 1)
+                {
+                    __threadfence();  // this CTA's share of A (seen through qready) before the arrival
+                    atomicAdd(&p.qbar[0], 1u);
+                    const unsigned long long t0 = globaltimer_ns();
+                    while (ld_acquire_gpu(&p.qbar[0]) < gridDim.x)
+                    {
+                        if (globaltimer_ns() - t0 > kWaitTimeoutNs)
+                        {
+                            ok = false;
+                            break;
+                        }
+                    }
+                    // the last CTA past the barrier leaves both words zero for the next launch
+                    if (atomicAdd(&p.qbar[1], 1u) == gridDim.x - 1)
+                    {
+                        atomicExch(&p.qbar[0], 0u);
+                        atomicExch(&p.qbar[1], 0u);
+                    }
+                }
+                // a wait that ran out is reported; the loads still go out (to valid
+                // addresses), so every armed stage completes and nothing is left in flight
+                if (!ok) atomicExch(p.err, (unsigned)MBS_ERR_DEVICE_TIMEOUT);
+                fence_proxy_async_global();
+            };
             // The weights (C, or R when swapped) are read exactly once when the
             // other operand is a single tile: stream them evict-first.
             const bool w_once = CF::SWAP ? p.tiles_c == 1 : p.tiles_r == 1;
@@ -613,7 +778,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #endif
                     uint8_t* st = smem + slot * CF::STAGE_BYTES;
                     mbar_arrive_expect_tx(&full[slot], tx_bytes);
-                    if (CF::R_PRESHUF)
+                    const bool defer = ndef >= 0;
+                    if (defer)
+                    {
+                        def_slot[ndef] = slot;
+                        def_r0[ndef] = r0;
+                        def_ks[ndef] = ks;
+                        ++ndef;
+                    }
+                    else if (CF::R_PRESHUF)
                         tma_load_3d_hint(st + CF::R_DATA_OFF, &tm_r, &full[slot], 0, r0 / 16, ks * 8, pol_r);
                     else
                         tma_load_2d_hint(st + CF::R_DATA_OFF, &tm_r, &full[slot], ks * BKB, r0, pol_r);
@@ -625,7 +798,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         tma_load_3d_hint(st + CF::C_DATA_OFF, &tm_c, &full[slot], 0, c0 / 16, ks * 8, pol_c);
                     else
                         tma_load_2d_hint(st + CF::C_DATA_OFF, &tm_c, &full[slot], ks * BKB, c0, pol_c);
-                    if (CF::R_MACRO)
+                    if (defer)
+                        ;  // A scales follow the deferred A tile
+                    else if (CF::R_MACRO)
                         tma_load_2d_hint(st + CF::R_RAW_OFF, &tm_rsf, &full[slot], 16 * (ks >> 1), r0 / 32, pol_r);
                     else
                         tma_load_3d_hint(st + CF::R_RAW_OFF, &tm_rsf, &full[slot], 0, ks, r0 / 32, pol_r);
@@ -640,7 +815,36 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         slot = 0;
                         phase ^= 1;
                     }
+                    if (ndef == STAGES)
+                    {
+                        // every slot is armed: the next stage needs a slot the MMAs free,
+                        // and they need A
+                        a_ready();
+                        for (int d = 0; d < STAGES; ++d)
+                        {
+                            uint8_t* sd = smem + def_slot[d] * CF::STAGE_BYTES;
+                            tma_load_2d_hint(sd + CF::R_DATA_OFF, &tm_r, &full[def_slot[d]], def_ks[d] * BKB,
+                                             def_r0[d], pol_r);
+                            tma_load_3d_hint(sd + CF::R_RAW_OFF, &tm_rsf, &full[def_slot[d]], 0, def_ks[d],
+                                             def_r0[d] / 32, pol_r);
+                        }
+                        ndef = -1;
+                    }
                 }
+            }
+            if (ndef >= 0)
+            {
+                // fewer stages than slots (or no work: a grid barrier still needs this CTA)
+                a_ready();
+                for (int d = 0; d < ndef; ++d)
+                {
+                    uint8_t* sd = smem + def_slot[d] * CF::STAGE_BYTES;
+                    tma_load_2d_hint(sd + CF::R_DATA_OFF, &tm_r, &full[def_slot[d]], def_ks[d] * BKB, def_r0[d],
+                                     pol_r);
+                    tma_load_3d_hint(sd + CF::R_RAW_OFF, &tm_rsf, &full[def_slot[d]], 0, def_ks[d], def_r0[d] / 32,
+                                     pol_r);
+                }
+                ndef = -1;
             }
         producer_done:;
 #if MBS_TIMING
@@ -1058,28 +1262,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     if (!CF::SWAP)
                     {
                         const int m = r0 + row;
-                        __nv_bfloat16* orow = p.out + (size_t)m * p.N;
 #pragma unroll
                         for (int ch = 0; ch < NCH; ++ch)
                         {
                             const int n = c0 + half * COLS + ch * 16;
-                            if (n < p.N)
-                            {
-                                if (p.out_v8)
-                                {
-                                    st_global_v8(orow + n, packed[ch * 8 + 0], packed[ch * 8 + 1],
-                                                 packed[ch * 8 + 2], packed[ch * 8 + 3], packed[ch * 8 + 4],
-                                                 packed[ch * 8 + 5], packed[ch * 8 + 6], packed[ch * 8 + 7]);
-                                }
-                                else
-                                {
-                                    uint4* dst = reinterpret_cast<uint4*>(orow + n);
-                                    dst[0] = make_uint4(packed[ch * 8 + 0], packed[ch * 8 + 1],
-                                                        packed[ch * 8 + 2], packed[ch * 8 + 3]);
-                                    dst[1] = make_uint4(packed[ch * 8 + 4], packed[ch * 8 + 5],
-                                                        packed[ch * 8 + 6], packed[ch * 8 + 7]);
-                                }
-                            }
+                            if (n < p.N) store_chunk16(p, m, n, packed + ch * 8);
                         }
                     }
                     else
@@ -1094,7 +1281,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                                 const uint32_t pr = packed[t >> 1];
                                 const unsigned short hbits = (t & 1) ? (unsigned short)(pr >> 16)
                                                                      : (unsigned short)(pr & 0xFFFFu);
-                                p.out[(size_t)m * p.N + n] = __ushort_as_bfloat16(hbits);
+#pragma unroll
+                                for (int d = 0; d < MAX_OUT; ++d)
+                                {
+                                    if (d >= p.n_out) break;
+                                    p.outs[d][(long long)m * p.ldc + n] = __ushort_as_bfloat16(hbits);
+                                }
                             }
                         }
                     }
@@ -1160,6 +1352,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #endif
         }
     }
+    // output copies in other GPUs' memory: make this thread's stores visible
+    // system-wide before the grid completes (a barrier on the stream follows)
+    if (p.n_out > 1) __threadfence_system();
     __syncwarp();
     if (warp == 1) tmem_dealloc(tmem_base, CF::TMEM_COLS);
 #if MBS_TIMING
@@ -1817,28 +2012,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) __cluster_dims__(2, 1, 1)
             const int m = r0 + row;
             if (m < p.M)
             {
-                __nv_bfloat16* orow = p.out + (size_t)m * p.N;
 #pragma unroll
                 for (int ch = 0; ch < NCH; ++ch)
                 {
                     const int n = c0 + half * COLS + ch * 16;
-                    if (n < p.N && n < c_end)
-                    {
-                        if (p.out_v8)
-                        {
-                            st_global_v8(orow + n, packed[ch * 8 + 0], packed[ch * 8 + 1], packed[ch * 8 + 2],
-                                         packed[ch * 8 + 3], packed[ch * 8 + 4], packed[ch * 8 + 5],
-                                         packed[ch * 8 + 6], packed[ch * 8 + 7]);
-                        }
-                        else
-                        {
-                            uint4* dst = reinterpret_cast<uint4*>(orow + n);
-                            dst[0] = make_uint4(packed[ch * 8 + 0], packed[ch * 8 + 1], packed[ch * 8 + 2],
-                                                packed[ch * 8 + 3]);
-                            dst[1] = make_uint4(packed[ch * 8 + 4], packed[ch * 8 + 5], packed[ch * 8 + 6],
-                                                packed[ch * 8 + 7]);
-                        }
-                    }
+                    if (n < p.N && n < c_end) store_chunk16(p, m, n, packed + ch * 8);
                 }
             }
             MBS_TADD(tacc, 7);
@@ -1846,6 +2024,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) __cluster_dims__(2, 1, 1)
         }
     }
 
+    if (p.n_out > 1) __threadfence_system();  // output copies in other GPUs' memory
     __syncwarp();
     tc_fence_before();
     cluster_sync();  // no remote arrive or pair MMA can still target this CTA
@@ -1878,7 +2057,35 @@ struct Problem
     bool packed = false;  // B is in the packed format (BS unused)
     float alpha = 1.0f;   // output scale
     const void* bias = nullptr;  // bf16 [N] or null
+    // extra output copies (mbs_gemm_a4w4_launch_multi): out_dst[0..n_dst) with row stride ldc;
+    // n_dst == 0 means the single buffer `out` with row stride N
+    void* const* out_dst = nullptr;
+    int n_dst = 0;
+    long long ldc = 0;
+    // fused activation quantiser (mbs_quant_gemm_a4w4_launch): A / AS point into the
+    // workspace and are written by the GEMM itself from bf16 qx [M, qx_ld]
+    const void* qx = nullptr;
+    int qx_ld = 0;
+    unsigned* qbar = nullptr;
 };
+
+// The output copies of a launch: `out` alone with row stride N, or the
+// caller's list (validated by run()).
+void set_outputs(Params& p, const Problem& pb)
+{
+    const int n = pb.n_dst > 0 ? pb.n_dst : 1;
+    p.n_out = n;
+    p.ldc = pb.n_dst > 0 ? pb.ldc : pb.N;
+    bool v8 = (p.ldc * 2) % 32 == 0;
+    for (int d = 0; d < MAX_OUT; ++d)
+    {
+        void* ptr = d < n ? (pb.n_dst > 0 ? pb.out_dst[d] : pb.out) : nullptr;
+        p.outs[d] = static_cast<__nv_bfloat16*>(ptr);
+        if (d < n && (reinterpret_cast<uintptr_t>(ptr) & 31) != 0) v8 = false;
+    }
+    p.out = p.outs[0];
+    p.out_v8 = v8 ? 1 : 0;  // every copy's rows start 32-byte aligned: 32-byte stores
+}
 
 struct Plan
 {
@@ -1966,7 +2173,10 @@ size_t sk_partial_bytes(const Plan& pl);
 // that no schedule's scratch (partials, scale images) ever lands on another
 // schedule's flags when one workspace serves several shapes.
 constexpr size_t kFlagBytes = MBS_GEMM_WS_FLAG_BYTES;
-constexpr int kMaxGrid = (int)(kFlagBytes / sizeof(unsigned));
+// stream-K flag words [0, kMaxGrid); the last two words are the fused
+// quantiser's grid barrier (arrived, departed)
+constexpr int kMaxGrid = (int)(kFlagBytes / sizeof(unsigned)) - 2;
+constexpr int kQuantBarrierWord = kMaxGrid;
 
 // Path and schedule choice.  Skinny M (decode) loads only its 32 or 64
 // activation rows per stage and uses stream-K so every SM streams an equal
@@ -2219,6 +2429,22 @@ int validate(const Problem& pb)
     if (!aligned16(pb.A) || !aligned16(pb.B) || !aligned16(pb.AS) || (!pb.packed && !aligned16(pb.BS)) ||
         !aligned16(pb.out))
         return fail(MBS_ERR_MISALIGNED, "gemm_a4w4: A, B, scales and out must be 16-byte aligned");
+    if (pb.n_dst > 0)
+    {
+        if (pb.n_dst > MAX_OUT)
+            return fail(MBS_ERR_INVALID_ARGUMENT, "gemm_a4w4: at most %d output copies, got %d", MAX_OUT,
+                        pb.n_dst);
+        if (pb.ldc < pb.N || pb.ldc % 8 != 0 || pb.ldc > (1LL << 40))
+            return fail(MBS_ERR_INVALID_ARGUMENT,
+                        "gemm_a4w4: ldc (%lld) must be a multiple of 8 and at least N (%d)", pb.ldc, pb.N);
+        for (int d = 0; d < pb.n_dst; ++d)
+        {
+            if (pb.out_dst[d] == nullptr)
+                return fail(MBS_ERR_INVALID_ARGUMENT, "gemm_a4w4: output copy %d is NULL", d);
+            if (!aligned16(pb.out_dst[d]))
+                return fail(MBS_ERR_MISALIGNED, "gemm_a4w4: output copy %d is not 16-byte aligned", d);
+        }
+    }
     return MBS_OK;
 }
 
@@ -2392,8 +2618,7 @@ int launch_pair(const Problem& pb, const Plan& pl, const DeviceInfo& dev, void* 
     p.k_stages = pl.k_stages;
     p.a_factor = pb.AF;
     p.b_factor = pb.BF;
-    p.out = static_cast<__nv_bfloat16*>(pb.out);
-    p.out_v8 = (reinterpret_cast<uintptr_t>(pb.out) & 31) == 0 ? 1 : 0;  // rows are N * 2 bytes, N % 16 == 0
+    set_outputs(p, pb);
     p.alpha = pb.alpha;
     p.bias = static_cast<const __nv_bfloat16*>(pb.bias);
     p.tiles_c = pl.pair_tiles_c;
@@ -2451,8 +2676,7 @@ int launch_cfg(const Problem& pb, const Plan& pl, const DeviceInfo& dev, void* w
     p.sk_units = (long long)p.num_tiles * pl.k_stages;
     p.a_factor = pb.AF;
     p.b_factor = pb.BF;
-    p.out = static_cast<__nv_bfloat16*>(pb.out);
-    p.out_v8 = (reinterpret_cast<uintptr_t>(pb.out) & 31) == 0 ? 1 : 0;  // rows are N * 2 bytes, N % 16 == 0
+    set_outputs(p, pb);
     p.alpha = pb.alpha;
     p.bias = static_cast<const __nv_bfloat16*>(pb.bias);
     if (pl.sk)
@@ -2466,6 +2690,17 @@ int launch_cfg(const Problem& pb, const Plan& pl, const DeviceInfo& dev, void* w
     p.act_rows = act_box_rows(pb, pl);
     p.ksplit = pl.ksplit;
     p.withhold_release = g_withhold_release;
+    if (pb.qx != nullptr)
+    {
+        // the GEMM writes A and its scales itself (TMA maps above point at them)
+        p.qmode = pl.ksplit > 1 ? 2 : 1;
+        p.qx = static_cast<const __nv_bfloat16*>(pb.qx);
+        p.qx_ld = pb.qx_ld;
+        p.qa = const_cast<uint8_t*>(pb.A);
+        p.qsa = const_cast<uint8_t*>(pb.AS);
+        p.q_snp = pb.snp;
+        p.qbar = pb.qbar;
+    }
     if (pl.ksplit > 1 && !CF::SPLIT_OK) return fail(MBS_ERR_CUDA, "cluster split-K planned for a configuration without it");
 
     cudaLaunchConfig_t cfg = {};
@@ -2486,8 +2721,9 @@ int launch_cfg(const Problem& pb, const Plan& pl, const DeviceInfo& dev, void* w
     }
     else
     {
-        attr[na].id = cudaLaunchAttributeCooperative;  // stream-K owners wait on other CTAs
-        attr[na].val.cooperative = pl.sk ? 1 : 0;
+        // stream-K owners wait on other CTAs, and so does the fused quantiser's grid barrier
+        attr[na].id = cudaLaunchAttributeCooperative;
+        attr[na].val.cooperative = (pl.sk || p.qmode == 1) ? 1 : 0;
         ++na;
     }
     // may start while the previous kernel in the stream finishes (the kernel
@@ -2775,6 +3011,121 @@ extern "C" int mbs_gemm_a4w4_launch_ex(const uint8_t* A, const uint8_t* B, const
     pb.bias = bias;
     return mbs::gemm::run(pb, workspace, workspace_bytes, workspace == nullptr,
                           reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int mbs_gemm_a4w4_launch_multi(const uint8_t* A, const uint8_t* B, const uint8_t* AScale,
+                                          const uint8_t* BScale, const uint8_t* AFactor,
+                                          const uint8_t* BFactor, void* const* out_dst, int n_dst,
+                                          long long ldc, int M, int N, int K, int Mpad, int scaleN_pad,
+                                          float alpha, const void* bias, void* workspace,
+                                          size_t workspace_bytes, void* stream)
+{
+    mbs::clear_error();
+    if (out_dst == nullptr || n_dst < 1)
+        return mbs::fail(MBS_ERR_INVALID_ARGUMENT, "mbs_gemm_a4w4_launch_multi: no output copies");
+    Problem pb{A, B, AScale, BScale, AFactor, BFactor, out_dst[0], M, N, K, Mpad, scaleN_pad, 0, false};
+    pb.alpha = alpha;
+    pb.bias = bias;
+    pb.out_dst = out_dst;
+    pb.n_dst = n_dst;
+    pb.ldc = ldc;
+    return mbs::gemm::run(pb, workspace, workspace_bytes, workspace == nullptr,
+                          reinterpret_cast<cudaStream_t>(stream));
+}
+
+namespace mbs {
+namespace gemm {
+namespace {
+
+// Workspace of mbs_quant_gemm_a4w4_launch: [the GEMM's own workspace (at
+// least the flag words, whose last two are the quantiser's grid barrier)]
+// [quantised A: M x K/2][its flatS scales: Mpad x scaleN_pad], each part
+// 256-byte aligned.
+struct QuantLayout
+{
+    size_t gemm, a, s, total;
+};
+
+QuantLayout quant_layout(const Plan& pl, int M, int K)
+{
+    auto up = [](size_t x) { return (x + 255) / 256 * 256; };
+    QuantLayout q;
+    q.gemm = up(pl.ws_bytes > kFlagBytes ? pl.ws_bytes : kFlagBytes);
+    q.a = q.gemm;
+    q.s = q.a + up((size_t)M * (K / 2));
+    q.total = q.s + up((size_t)round_up(M, 32) * scale_n_pad(K));
+    return q;
+}
+
+int num_sms_or_default()
+{
+    int num_sms = 148, dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess)
+    {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && n > 0) num_sms = n;
+    }
+    else
+    {
+        cudaGetLastError();
+    }
+    return num_sms;
+}
+
+}  // namespace
+}  // namespace gemm
+}  // namespace mbs
+
+extern "C" size_t mbs_quant_gemm_a4w4_workspace_size(int M, int N, int K)
+{
+    using namespace mbs::gemm;
+    if (M <= 0 || N <= 0 || K <= 0) return 0;
+    return quant_layout(make_plan(M, N, K, num_sms_or_default()), M, K).total;
+}
+
+extern "C" int mbs_quant_gemm_a4w4_launch(const void* x_bf16, int ld_x, const uint8_t* B, const uint8_t* BScale,
+                                          const uint8_t* AFactor, const uint8_t* BFactor, void* out, int M, int N,
+                                          int K, int scaleN_pad, void* workspace, size_t workspace_bytes,
+                                          void* stream)
+{
+    using namespace mbs::gemm;
+    mbs::clear_error();
+    if (x_bf16 == nullptr || workspace == nullptr)
+        return mbs::fail(MBS_ERR_INVALID_ARGUMENT, "mbs_quant_gemm_a4w4_launch: x and workspace must be non-NULL");
+    if (M <= 0 || K <= 0 || ld_x < K || ld_x % 8 != 0 || !mbs::aligned16(x_bf16))
+        return mbs::fail(MBS_ERR_INVALID_ARGUMENT,
+                         "mbs_quant_gemm_a4w4_launch: x must be 16-byte aligned bf16 [M, ld_x], ld_x >= K, "
+                         "ld_x %% 8 == 0 (M=%d K=%d ld_x=%d)", M, K, ld_x);
+    if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+        return mbs::fail(MBS_ERR_MISALIGNED, "mbs_quant_gemm_a4w4_launch: workspace must be 256-byte aligned");
+    mbs::DeviceInfo dev;
+    int st = mbs::current_device(&dev);
+    if (st) return st;
+    const Plan pl = make_plan(M, N, K, dev.num_sms);
+    const QuantLayout q = quant_layout(pl, M, K);
+    if (workspace_bytes < q.total)
+        return mbs::fail(MBS_ERR_WORKSPACE, "mbs_quant_gemm_a4w4_launch: workspace of %zu bytes needed, %zu given",
+                         q.total, workspace_bytes);
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    uint8_t* qa = ws + q.a;
+    uint8_t* qs = ws + q.s;
+    Problem pb{qa, B, qs, BScale, AFactor, BFactor, out, M, N, K, mbs::round_up(M, 32), scaleN_pad, 0, false};
+    st = validate(pb);
+    if (st) return st;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    if (pl.pair || pl.swap)
+    {
+        // CTA pairs (large M: the quantiser is a small share of the call) and the
+        // swapped form take A from the stand-alone quantiser, on the same stream
+        st = mbs_quantize_mxfp4(x_bf16, M, K, ld_x, qa, qs, 1, stream);
+        if (st) return st;
+        mbs::clear_error();
+        return dispatch(pb, pl, dev, ws, s);
+    }
+    pb.qx = x_bf16;
+    pb.qx_ld = ld_x;
+    pb.qbar = reinterpret_cast<unsigned*>(ws) + kQuantBarrierWord;
+    return dispatch(pb, pl, dev, ws, s);
 }
 
 extern "C" size_t mbs_packed_weight_bytes(int N, int K)

@@ -109,9 +109,32 @@ def shuffle_scales(s: torch.Tensor, K: int | None = None) -> torch.Tensor:
 
 def quant_gemm_a4w4(x: torch.Tensor, B: torch.Tensor, B_scale: torch.Tensor,
                     A_factor=None, B_factor=None, out=None) -> torch.Tensor:
-    """Dynamic-quant + GEMM: bf16 activations x [M, K] against a preshuffled
-    MXFP4 weight B [N, K/2] with shuffled scales.  Quantises x on the device
-    (shuffled scales) and runs the GEMM on the same stream."""
-    from .mbs_gemm_a4w4 import gemm_a4w4
-    q, s = quantize_mxfp4(x, shuffle=True)
-    return gemm_a4w4(q, B, s, B_scale, A_factor, B_factor, out=out)
+    """Dynamic-quant + GEMM in one call (mbs_quant_gemm_a4w4_launch): bf16
+    activations x [M, K] against a preshuffled MXFP4 weight B [N, K/2] with
+    shuffled scales.  Bit-identical to quantize_mxfp4(x, shuffle=True)
+    followed by gemm_a4w4; for skinny and small M the quantiser runs inside
+    the GEMM kernel (one launch)."""
+    from .mbs_gemm_a4w4 import _bytes, _out_buffer, _ptr, cached_workspace
+    x, M, K = _check_x(x)
+    Bu, Bsc = _bytes(B), _bytes(B_scale)
+    N = int(Bu.size(0))
+    if int(Bu.size(1)) * 2 != K:
+        raise RuntimeError(f"quant_gemm_a4w4: B must be [N, K/2] = [{N}, {K // 2}], got {tuple(Bu.shape)}")
+    if N % 16 != 0:
+        raise RuntimeError(f"quant_gemm_a4w4: N must be a multiple of 16, got {N}")
+    snp = scale_n_pad(K)
+    if Bsc.numel() < _round_up(N, 32) * snp:
+        raise RuntimeError(f"quant_gemm_a4w4: B_scale must hold {_round_up(N, 32) * snp} bytes")
+    fa = None if A_factor is None else _bytes(A_factor)
+    fb = None if B_factor is None else _bytes(B_factor)
+    if fa is not None and fa.numel() != M:
+        raise RuntimeError(f"quant_gemm_a4w4: A_factor must hold M = {M} bytes")
+    if fb is not None and fb.numel() != N:
+        raise RuntimeError(f"quant_gemm_a4w4: B_factor must hold N = {N} bytes")
+    o = _out_buffer(out, _round_up(M, 32), M, N, x.device)
+    with torch.cuda.device(x.device):
+        need = int(_lib.lib().mbs_quant_gemm_a4w4_workspace_size(M, N, K))
+        ws = cached_workspace(need, x.device)
+        _lib.call("mbs_quant_gemm_a4w4_launch", x.data_ptr(), int(x.stride(0)), Bu.data_ptr(), Bsc.data_ptr(),
+                  _ptr(fa), _ptr(fb), o.data_ptr(), M, N, K, snp, ws.data_ptr(), ws.numel(), _stream(x.device))
+    return o.narrow(0, 0, M)

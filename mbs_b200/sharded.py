@@ -20,6 +20,16 @@ the next chunk's GEMM runs on all SMs; one-word NCCL all-reduces serve as
 device-side barriers.  With layout="blocked" the result is the layer's
 exchange buffer and stays valid until the next forward call.
 
+`exchange="fused"` (CUDA GPUs; the default from 2 ranks up) takes the
+exchange into the GEMM itself: every rank maps its peers' copies of the full
+output [M, N] through CUDA IPC and launches one GEMM whose epilogue writes
+each finished tile into all of them (mbs_gemm_a4w4_launch_multi), so the
+NVLink traffic runs beside the tensor-core work of the following tiles and
+no copy or collective kernel follows the GEMM; two one-word NCCL
+all-reduces serve as the device-side barriers around it.  The result is
+row-major [M, N] on every rank (layout="blocked" views it as
+[world, M, N/world]) and stays valid until the next forward call.
+
 `chunks > 1` (with exchange="nccl") pipelines the exchange with the compute: A is processed in
 row chunks, each chunk's GEMM writes straight into this rank's block of the
 output, and its rows are exchanged with every peer by NCCL point-to-point
@@ -111,14 +121,16 @@ class ShardedA4W4:
                 exchange: str = "nccl") -> torch.Tensor:
         if layout not in ("blocked", "rows"):
             raise ValueError(f"layout must be 'blocked' or 'rows', got {layout!r}")
-        if exchange not in ("nccl", "copy", "auto"):
-            raise ValueError(f"exchange must be 'nccl', 'copy' or 'auto', got {exchange!r}")
+        if exchange not in ("nccl", "copy", "fused", "auto"):
+            raise ValueError(f"exchange must be 'nccl', 'copy', 'fused' or 'auto', got {exchange!r}")
         if exchange == "auto":
             # measured on B200 (config[4]): copy engines win at 2 ranks
             # (2.14 vs 3.73 ms), NCCL's all-gather from 4 ranks up (3.29 vs 3.65 ms)
             exchange = self.default_exchange(x)
             if exchange == "copy" and chunks < 2:
                 chunks = self.default_chunks(exchange)
+        if exchange == "fused" and self.world > 1:
+            return self._forward_fused(x, A_factor, layout)
         if exchange == "copy" and self.world > 1:
             return self._forward_copy(x, A_factor, layout, max(1, chunks))
         if chunks > 1:
@@ -138,14 +150,18 @@ class ShardedA4W4:
         raise ValueError(f"layout must be 'blocked' or 'rows', got {layout!r}")
 
     def default_exchange(self, x: torch.Tensor) -> str:
-        """The exchange `forward(exchange="auto")` takes for this group size."""
-        return "copy" if self.world == 2 and x.is_cuda else "nccl"
+        """The exchange `forward(exchange="auto")` takes: the GEMM-fused one on
+        CUDA tensors with peers to exchange with, NCCL otherwise."""
+        return "fused" if self.world > 1 and x.is_cuda and self._default_gemm else "nccl"
 
     @staticmethod
     def default_chunks(exchange: str) -> int:
         return 4 if exchange == "copy" else 1
 
     def describe_exchange(self, exchange: str, chunks: int) -> str:
+        if exchange == "fused":
+            return (f"fused into the GEMM: the epilogue stores every output tile into all {self.world} ranks' "
+                    f"copies of C (CUDA IPC peer memory over NVLink); NCCL one-word barriers before and after")
         if exchange == "copy":
             return (f"{chunks} row chunks pushed into the peers' buffers by copy engines (CUDA IPC), "
                     f"overlapped with the next chunk's GEMM")
@@ -202,21 +218,64 @@ class ShardedA4W4:
             self._flag = torch.zeros(1, dtype=torch.int32, device=self.B.device)
         dist.all_reduce(self._flag, group=self.group)
 
+    def _peer_buffer(self, nbytes: int, device: torch.device):
+        """The layer's IPC-shared buffer on every rank, (re)allocated collectively."""
+        from .peer import PeerBuffer
+        if self._peerbuf is None or self._peerbuf.nbytes < nbytes:
+            if self._peerbuf is not None:
+                torch.cuda.synchronize(device)
+                self._barrier()
+                torch.cuda.synchronize(device)
+                self._peerbuf.close()
+            self._peerbuf = PeerBuffer(nbytes, device, self.group)
+        return self._peerbuf
+
+    def _forward_fused(self, x, A_factor, layout):
+        """One GEMM writes this rank's column block of C into every rank's copy
+        of C (its own first, then the peers in rank order after its own, so the
+        ranks spread their traffic over different links)."""
+        import ctypes
+
+        from . import _lib
+        from .mbs_gemm_a4w4 import scale_n_pad, workspace_for
+        if not x.is_cuda or not self._default_gemm:
+            raise ValueError("exchange='fused' needs CUDA tensors and this package's GEMM")
+        M = int(x.shape[0])
+        nl = self.n1 - self.n0
+        buf = self._peer_buffer(M * self.N * 2, x.device)
+        out = buf.tensor((M, self.N))
+        q, s = self._quant(x)
+        qu, su = q.view(torch.uint8).contiguous(), s.view(torch.uint8).contiguous()
+        fa = None if A_factor is None else A_factor.view(torch.uint8).contiguous()
+        fb = None if self.B_factor is None else self.B_factor.view(torch.uint8).contiguous()
+        order = [(self.rank + i) % self.world for i in range(self.world)]
+        dst = (ctypes.c_void_p * self.world)(*[buf.ptrs[r] + self.n0 * 2 for r in order])
+        K = self.K
+        Mpad = (M + 31) // 32 * 32
+        ws = workspace_for(M, nl, K, x.device)
+        # nobody may write into a rank's copy of C before that rank is done with
+        # the previous result (anything it queued before this call)
+        self._barrier()
+        stream = torch.cuda.current_stream(x.device).cuda_stream
+        _lib.call("mbs_gemm_a4w4_launch_multi", qu.data_ptr(), self.B.data_ptr(), su.data_ptr(),
+                  self.B_scale.data_ptr(), None if fa is None else fa.data_ptr(),
+                  None if fb is None else fb.data_ptr(), dst, self.world, self.N, M, nl, K, Mpad,
+                  scale_n_pad(K), 1.0, None, None if ws is None else ws.data_ptr(),
+                  0 if ws is None else ws.numel(), stream)
+        self._barrier()  # every rank's GEMM (and with it every store into every copy) has completed
+        if layout == "rows":
+            return out
+        return out.view(M, self.world, nl).permute(1, 0, 2)
+
     def _forward_copy(self, x, A_factor, layout, chunks):
         """Copy-engine exchange: every chunk's rows go straight into each peer's
         copy of the gathered output (CUDA IPC mapping, cudaMemcpyAsync on a side
         stream), beside the next chunk's GEMM, which keeps every SM."""
-        from .peer import PeerBuffer
         M = int(x.shape[0])
         nl = self.n1 - self.n0
         nbytes = self.world * M * nl * 2
-        if self._peerbuf is None or self._peerbuf.nbytes < nbytes:
-            if self._peerbuf is not None:
-                torch.cuda.synchronize(x.device)
-                self._barrier()
-                torch.cuda.synchronize(x.device)
-                self._peerbuf.close()
-            self._peerbuf = PeerBuffer(nbytes, x.device, self.group)
+        self._peer_buffer(nbytes, x.device)
+        if self._side is None:
             # one side stream: copies to different peers issued on separate
             # streams measured slower at 4 GPUs (4.15 vs 3.65 ms)
             self._side = torch.cuda.Stream(x.device)

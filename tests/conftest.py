@@ -46,8 +46,10 @@ def pytest_terminal_summary(terminalreporter):
     tr = terminalreporter
     tr.section("GEMM parity: observed tolerance use")
     worst = max(e for _, e in helpers.OBSERVED.values())
+    worst_ratio = max(r for r, _ in helpers.OBSERVED.values())
     tr.write_line(f"slack allowed 2^{math.log2(O.GEMM_SLACK):.0f}; largest needed "
-                  f"{'0' if worst == 0 else f'2^{math.log2(worst):.1f}'} over {len(helpers.OBSERVED)} checks")
+                  f"{'0' if worst == 0 else f'2^{math.log2(worst):.1f}'}, largest tolerance ratio "
+                  f"{worst_ratio:.3g}, over {len(helpers.OBSERVED)} checks")
     for what, (ratio, ex) in sorted(helpers.OBSERVED.items(), key=lambda kv: -kv[1][1])[:12]:
         tr.write_line(f"  {what}: max ratio {ratio:.3g}, slack needed "
                       f"{'0' if ex == 0 else f'2^{math.log2(ex):.1f}'}")

@@ -1,8 +1,10 @@
 """torchrun worker for tests/test_sharded.py: one rank per GPU, NCCL.
 
 Builds a seeded weight, shards it, runs the sharded forward (quantise A on
-each rank, local GEMM, all-gather) and checks the gathered C against the CPU
-oracle on a sample of columns from every shard.  Prints SHARDED_OK per rank.
+each rank, local GEMM, exchange of the C shards: NCCL all-gather, NCCL
+send/recv, copy engines, or stores into the peers' copies from the GEMM's
+epilogue) and checks the gathered C against the CPU oracle on a sample of
+columns from every shard.  Prints SHARDED_OK per rank.
 """
 
 import os
@@ -42,9 +44,11 @@ def main():
         cols = np.concatenate([np.arange(r * N // world, r * N // world + 64) for r in range(world)])
         ref = O.gemm_ref(xq, wq[cols], xs, ws[cols])
         bound = O.gemm_abs_bound(xq, wq[cols], xs, ws[cols])
-        # one all-gather, the pipelined point-to-point exchange, and the copy-engine
-        # exchange through peer memory (twice, reusing its buffer)
-        for exchange, chunks in (("nccl", 1), ("nccl", 3), ("copy", 1), ("copy", 3), ("copy", 3)):
+        # one all-gather, the pipelined point-to-point exchange, the copy-engine
+        # exchange through peer memory (twice, reusing its buffer) and the exchange
+        # fused into the GEMM's epilogue (twice, reusing its buffer)
+        for exchange, chunks in (("nccl", 1), ("nccl", 3), ("copy", 1), ("copy", 3), ("copy", 3),
+                                 ("fused", 1), ("fused", 1)):
             out = layer(x.cuda(), layout="rows", chunks=chunks, exchange=exchange)
             torch.cuda.synchronize()
             got = out[:, torch.from_numpy(cols).cuda()].float().cpu().numpy()

@@ -34,9 +34,10 @@ def _args(c, out):
 
 # (8, 4096, 1024) and (48, 2048, 1024) take the stream-K schedule (too few K
 # stages for cluster split-K), so their scratch lives in the static buffer;
-# (4096, 4096, 512) the data-parallel one, which needs no scratch.
+# (512, 512, 1024) the CTA-pair schedule, whose scale images live there too;
+# (256, 512, 1024) data-parallel single CTAs, which need no scratch.
 @pytest.mark.parametrize("M,N,K,needs_scratch", [(8, 4096, 1024, True), (48, 2048, 1024, True),
-                                                 (4096, 4096, 512, False)])
+                                                 (512, 512, 1024, True), (256, 512, 1024, False)])
 def test_noalloc_matches_oracle_and_workspace_entry_point(M, N, K, needs_scratch):
     from mbs_b200 import _lib
     L = _lib.lib()
