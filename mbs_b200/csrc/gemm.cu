@@ -1553,9 +1553,13 @@ __global__ void __launch_bounds__(256) scale_image_kernel(const uint8_t* __restr
     }
 }
 
-template <int STAGES_, int BN_>
+template <int STAGES_, int BN_, bool XCHG_ = false>
 struct CfgPair
 {
+    // XCHG: the output goes to several copies (mbs_gemm_a4w4_launch_multi, other GPUs'
+    // memory among them); each epilogue warp stages 32 rows x 64 columns at a time in
+    // shared memory and writes them out as 128-byte row segments
+    static constexpr bool XCHG = XCHG_;
     static constexpr int BN = BN_;           // pair tile columns
     static constexpr int N2 = BN - 256;      // columns of the second MMA (0 or 128)
     static_assert(N2 == 0 || N2 == 128, "pair tiles are 256 or 384 columns wide");
@@ -1586,8 +1590,12 @@ struct CfgPair
     // full, sfready, empty [STAGES]; acc_full, acc_empty; tmem slot; abort
     static constexpr int BAR_BYTES = (3 * STAGES + 2) * 8 + 16;
     static constexpr int EPI_BYTES = (BM + 2 * BN) * 4;  // factor + bias staging
-    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + EPI_BYTES + 1024;
+    static constexpr int XCHG_WARP_BYTES = 32 * 64 * 2;   // 32 rows x 64 bf16 columns
+    static constexpr int XCHG_OFF = align_up(STAGES * STAGE_BYTES + BAR_BYTES + EPI_BYTES, 128);
+    static constexpr int XCHG_BYTES = XCHG ? NUM_EPI_WARPS * XCHG_WARP_BYTES : 0;
+    static constexpr int SMEM_BYTES = XCHG_OFF + XCHG_BYTES + 1024;
     static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+    static_assert(XCHG_OFF % 16 == 0, "staging alignment");
 };
 
 template <class CF>
@@ -2010,7 +2018,49 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) __cluster_dims__(2, 1, 1)
                     mbar_arrive_cluster(acc_empty0);
             }
             const int m = r0 + row;
-            if (m < p.M)
+            if constexpr (CF::XCHG)
+            {
+                // 64 columns at a time: each thread puts its row's eight 16-byte pieces
+                // into the warp's staging block (piece q of row r at slot q ^ (r & 7), so
+                // 8 consecutive lanes hit 8 different bank groups), then lane l writes
+                // piece l & 7 of row 4i + (l >> 3): 8 lanes cover 128 contiguous bytes
+                // of one output row, which is what NVLink moves efficiently (32-byte
+                // pieces scattered over 32 rows ran ~4x slower to another GPU).
+                uint4* stg = reinterpret_cast<uint4*>(smem + CF::XCHG_OFF + e * CF::XCHG_WARP_BYTES);
+#pragma unroll
+                for (int grp = 0; grp < COLS / 64; ++grp)
+                {
+                    __syncwarp();
+#pragma unroll
+                    for (int q = 0; q < 8; ++q)
+                    {
+                        const uint32_t* w = packed + grp * 32 + q * 4;
+                        stg[lane * 8 + (q ^ (lane & 7))] = make_uint4(w[0], w[1], w[2], w[3]);
+                    }
+                    __syncwarp();
+                    const int q = lane & 7;
+                    const int n = c0 + half * COLS + grp * 64 + q * 8;
+                    const bool col_ok = n < p.N && n < c_end;
+#pragma unroll
+                    for (int i = 0; i < 8; ++i)
+                    {
+                        const int rr = 4 * i + (lane >> 3);  // row of the warp's 32
+                        const uint4 v = stg[rr * 8 + (q ^ (rr & 7))];
+                        const long long mm = (long long)r0 + quarter * 32 + rr;
+                        if (col_ok && mm < p.M)
+                        {
+                            const long long off = mm * p.ldc + n;
+#pragma unroll
+                            for (int d = 0; d < MAX_OUT; ++d)
+                            {
+                                if (d >= p.n_out) break;
+                                *reinterpret_cast<uint4*>(p.outs[d] + off) = v;
+                            }
+                        }
+                    }
+                }
+            }
+            else if (m < p.M)
             {
 #pragma unroll
                 for (int ch = 0; ch < NCH; ++ch)
@@ -2752,8 +2802,15 @@ int dispatch(const Problem& pb, const Plan& pl, const DeviceInfo& dev, void* ws,
         return launch_cfg<Cfg<256, false, false, 4, 128, true>>(pb, pl, dev, ws, s);
     }
     if (pl.pair)
+    {
+        // several output copies (other GPUs' memory among them): the staged
+        // epilogue, with one pipeline stage fewer to make room for its buffers
+        if (pb.n_dst > 1)
+            return pl.pair_bn == 384 ? launch_pair<CfgPair<4, 384, true>>(pb, pl, dev, ws, s)
+                                     : launch_pair<CfgPair<5, 256, true>>(pb, pl, dev, ws, s);
         return pl.pair_bn == 384 ? launch_pair<CfgPair<5, 384>>(pb, pl, dev, ws, s)
                                  : launch_pair<CfgPair<6, 256>>(pb, pl, dev, ws, s);
+    }
     if (pl.swap)
     {
         if (pl.bn == 32)
