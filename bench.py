@@ -457,6 +457,24 @@ def _cpu_sample(M, N, K, rows, seed=0):
     return qa, qb, sa, sb
 
 
+def _cpu_call_s(M, N, K, rows, cols, reps=2):
+    """Host seconds one full-size call of the oracle port (the reference's CPU
+    path) takes, timed on a sample of `rows` rows of A against `cols` rows of
+    B (best of `reps`) and scaled by (M / rows) * (N / cols): the dequantise
+    and matmul costs are linear in both.  Returns (seconds, sample text)."""
+    from oracle import mxfp4_oracle as O
+    rows, cols = min(M, rows), min(N, cols)
+    qa, qb, sa, sb = _cpu_sample(M, cols, K, rows)
+    best = None
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        O.gemm_ref(qa, qb, sa, sb)
+        dt = time.perf_counter() - t0
+        best = dt if best is None else min(best, dt)
+    scale = (M / rows) * (N / cols)
+    return best * scale, f"{rows} of {M} rows x {cols} of {N} columns, scaled x{scale:.0f}, best of {reps}"
+
+
 def cpu_baseline(M, N, K, budget_s=20.0):
     """The oracle's dequantise-then-matmul on the host cores, on a row sample of A."""
     from oracle import mxfp4_oracle as O
@@ -537,6 +555,11 @@ def _flusher(dev):
     return flush
 
 
+def _two_calls(mbs_b200, x, B, Bs, out):
+    q, s = mbs_b200.quantize_mxfp4(x, shuffle=True)
+    return mbs_b200.gemm_a4w4(q, B, s, Bs, out=out)
+
+
 def decode_object(dev, peaks):
     """BASELINE config[1] (decode, N = 57344, K = 8192, M in {1, 4, 16, 32};
     activations N(0,1), weights N(0,0.02), both quantised on the device).
@@ -559,20 +582,35 @@ def decode_object(dev, peaks):
                      "bench_one.py:34-47 (10 warm-up, 50 eager calls back to back); isolated: one call "
                      "after an L2 flush (median of 5); GB/s = algorithmic bytes / per-call time",
            "peak_measured_gbs": hbm}
+    packed = mbs_b200.pack_weight(B, Bs)  # the optional one-time re-layout of static weights
     for M in (1, 4, 16, 32):
         x = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
         A, As = mbs_b200.quantize_mxfp4(x, shuffle=True)
         out = torch.empty(((M + 31) // 32 * 32, N), dtype=torch.bfloat16, device=dev)
         nbytes = N * K // 2 + N * K // 32 + M * K // 2 + M * K // 32 + M * N * 2
         gus, eus, ius = _per_call_us(lambda: mbs_b200.gemm_a4w4(A, B, As, Bs, out=out), flush)
+        # activations in bf16: quantise + GEMM as two calls, and fused in one launch
+        q2_us = _per_call_us(lambda: _two_calls(mbs_b200, x, B, Bs, out), flush)
+        qf_us = _per_call_us(lambda: mbs_b200.quant_gemm_a4w4(x, B, Bs, out=out), flush)
+        pk_us = _per_call_us(lambda: mbs_b200.gemm_a4w4_packed(A, packed, As, out=out), flush)
         gbs = nbytes / (gus * 1e-6) / 1e9
+        cpu_s, cpu_sample = _cpu_call_s(M, N, K, rows=M, cols=2048)
         res[f"M={M}"] = {"graph_us": round(gus, 2), "eager_us": round(eus, 2), "isolated_us": round(ius, 2),
                          "gbs": round(gbs, 1), "frac_measured": round(gbs / hbm, 4),
                          "frac_8tbs": round(gbs / 8000.0, 4),
                          "eager_gbs": round(nbytes / (eus * 1e-6) / 1e9, 1),
                          "isolated_gbs": round(nbytes / (ius * 1e-6) / 1e9, 1),
-                         "algorithmic_bytes": nbytes}
-    del B, Bs
+                         "algorithmic_bytes": nbytes,
+                         "quant_gemm": {"two_calls_us": [round(v, 2) for v in q2_us],
+                                        "fused_us": [round(v, 2) for v in qf_us],
+                                        "what": "bf16 activations: quantize_mxfp4 + gemm_a4w4 vs quant_gemm_a4w4 "
+                                                "(one launch); [graph, eager, isolated] per call"},
+                         "packed_weights": {"us": [round(v, 2) for v in pk_us],
+                                            "gbs_graph": round(nbytes / (pk_us[0] * 1e-6) / 1e9, 1),
+                                            "what": "gemm_a4w4_packed on the one-time packed weight layout; "
+                                                    "[graph, eager, isolated] per call"},
+                         "cpu_baseline_us": round(cpu_s * 1e6, 1), "cpu_sample": cpu_sample}
+    del B, Bs, packed
     torch.cuda.empty_cache()
     return res
 
@@ -599,9 +637,11 @@ def configs_object(dev):
     fb = torch.randint(0, 256, (N,), dtype=torch.uint8, device=dev, generator=g)
     out = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
     gus, eus, ius = _per_call_us(lambda: mbs_b200.gemm_a4w4(A, B, As, Bs, fa, fb, out=out), flush)
+    cpu_s, cpu_sample = _cpu_call_s(M, N, K, rows=M, cols=N, reps=3)
     res["cfg0"] = {"workload": "256x512x1024 + MBS factors", "graph_us": round(gus, 2),
                    "eager_us": round(eus, 2), "isolated_us": round(ius, 2),
-                   "tflops_graph": round(2.0 * M * N * K / (gus * 1e-6) / 1e12, 2)}
+                   "tflops_graph": round(2.0 * M * N * K / (gus * 1e-6) / 1e12, 2),
+                   "cpu_baseline_us": round(cpu_s * 1e6, 1), "cpu_sample": cpu_sample}
     M, N, K = 4096, 7168, 18432
     x = torch.randn(M, K, device=dev, generator=g)
     x = torch.where(torch.rand(M, K, device=dev, generator=g) < 0.01, x * 20, x).to(torch.bfloat16)
@@ -636,9 +676,11 @@ def configs_object(dev):
     ms = statistics.median(a.elapsed_time(b) for a, b in ev)
     kms = statistics.median(a.elapsed_time(b) for a, b in kev)
     flops = 2.0 * M * N * K
+    cpu_s, cpu_sample = _cpu_call_s(M, N, K, rows=128, cols=1024)
     res["cfg3"] = {"workload": "4096x7168x18432 macro-block B scales + MBS factors, L2 flushed per call",
                    "call_ms": round(ms, 4), "tflops": round(flops / (ms * 1e-3) / 1e12, 1),
-                   "kernel_ms": round(kms, 4), "kernel_tflops": round(flops / (kms * 1e-3) / 1e12, 1)}
+                   "kernel_ms": round(kms, 4), "kernel_tflops": round(flops / (kms * 1e-3) / 1e12, 1),
+                   "cpu_baseline_ms": round(cpu_s * 1e3, 1), "cpu_sample": cpu_sample + " (per-row block scales)"}
     torch.cuda.empty_cache()
     return res
 
@@ -740,6 +782,10 @@ def sharded_object(args, world, rank, dev):
                       "sample": "64 rows x 256 columns of every rank's shard against the CPU oracle",
                       "exchange_checksums_ok": bool(flags[1].item())},
            "steps": args.sharded_steps, "timing": "median of per-step CUDA events, max over ranks"}
+    if rank == 0 and world == 1:
+        cpu_s, cpu_sample = _cpu_call_s(M, N, K, rows=64, cols=4096)
+        res["cpu_baseline_ms"] = round(cpu_s * 1e3, 1)
+        res["cpu_sample"] = cpu_sample + " (GEMM only, activations already quantised)"
     del out, mine
     dist.barrier()
     layer.close()
