@@ -105,9 +105,70 @@ unsigned* device_error_word(int device)
     return ptrs[device];
 }
 
+// A calling thread usually launches the same operands again and again (a
+// serving loop, a benchmark): encoded maps are kept in a small per-thread
+// direct-mapped cache keyed by every input of the encoding, so a repeated
+// launch skips the driver call.  A map depends on nothing else.
+namespace {
+struct TmapKey
+{
+    uint64_t v[16];
+    bool operator==(const TmapKey& o) const
+    {
+        for (int i = 0; i < 16; ++i)
+            if (v[i] != o.v[i]) return false;
+        return true;
+    }
+};
+struct TmapEntry
+{
+    TmapKey key;
+    CUtensorMap map;
+    bool valid;
+};
+constexpr int kTmapCacheSlots = 64;
+thread_local TmapEntry g_tmap_cache[kTmapCacheSlots];
+}  // namespace
+
+int encode_tmap_uncached(CUtensorMap* map, CUtensorMapDataType dtype, int rank, void* base,
+                         const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
+                         CUtensorMapSwizzle swizzle);
+
 int encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, void* base,
                 const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
                 CUtensorMapSwizzle swizzle)
+{
+    if (rank < 1 || rank > 5) return encode_tmap_uncached(map, dtype, rank, base, dims, strides_bytes, box, swizzle);
+    TmapKey k{};
+    k.v[0] = ((uint64_t)dtype << 32) | ((uint64_t)rank << 16) | (uint64_t)swizzle;
+    k.v[1] = reinterpret_cast<uintptr_t>(base);
+    for (int i = 0; i < rank; ++i)
+    {
+        k.v[2 + i] = dims[i];
+        k.v[7 + i] = box[i];
+    }
+    for (int i = 0; i + 1 < rank; ++i) k.v[12 + i] = strides_bytes[i];
+    uint64_t h = 1469598103934665603ull;
+    for (int i = 0; i < 16; ++i) h = (h ^ k.v[i]) * 1099511628211ull;
+    TmapEntry& e = g_tmap_cache[(h >> 17) % kTmapCacheSlots];
+    if (e.valid && e.key == k)
+    {
+        *map = e.map;
+        return MBS_OK;
+    }
+    const int st = encode_tmap_uncached(map, dtype, rank, base, dims, strides_bytes, box, swizzle);
+    if (st == MBS_OK)
+    {
+        e.key = k;
+        e.map = *map;
+        e.valid = true;
+    }
+    return st;
+}
+
+int encode_tmap_uncached(CUtensorMap* map, CUtensorMapDataType dtype, int rank, void* base,
+                         const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
+                         CUtensorMapSwizzle swizzle)
 {
     EncodeTiledFn fn = get_encode_fn();
     if (fn == nullptr) return fail(MBS_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");

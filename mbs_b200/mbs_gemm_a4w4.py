@@ -62,8 +62,33 @@ def scale_n_pad(K: int) -> int:
 
 
 def _bytes(t: torch.Tensor) -> torch.Tensor:
-    # .view(kByte).contiguous() as in interface/gemm_a4w4_pybind.cpp:25-30
-    return t.view(torch.uint8).contiguous()
+    # .view(kByte).contiguous() as in interface/gemm_a4w4_pybind.cpp:25-30 (each torch
+    # call costs a few microseconds of host time per launch, so skip the no-op ones)
+    if t.dtype != torch.uint8:
+        t = t.view(torch.uint8)
+    return t if t.is_contiguous() else t.contiguous()
+
+
+class _on_device:
+    """`with torch.cuda.device(dev)` only when dev is not already current
+    (switching costs host time on every launch)."""
+    __slots__ = ("idx", "prev")
+
+    def __init__(self, device: torch.device):
+        self.idx = device.index if device.index is not None else torch.cuda.current_device()
+        self.prev = None
+
+    def __enter__(self):
+        cur = torch.cuda.current_device()
+        if cur != self.idx:
+            self.prev = cur
+            torch.cuda.set_device(self.idx)
+        return self
+
+    def __exit__(self, *exc):
+        if self.prev is not None:
+            torch.cuda.set_device(self.prev)
+        return False
 
 
 @contextlib.contextmanager
@@ -111,9 +136,52 @@ def cached_workspace(need: int, device: torch.device) -> torch.Tensor | None:
     return buf
 
 
+_ws_size_cache: dict = {}
+
+
 def workspace_for(M: int, N: int, K: int, device: torch.device) -> torch.Tensor | None:
     """Workspace for a drop-in launch of this shape on the current stream."""
-    return cached_workspace(int(_lib.lib().mbs_gemm_a4w4_workspace_size(M, N, K)), device)
+    return _remembered_workspace(M, N, K, device, fresh=True)
+
+
+def _remembered_workspace(M: int, N: int, K: int, device: torch.device, fresh: bool = False):
+    """As workspace_for with the size remembered per (shape, device), which
+    saves a library call per launch.  The plan behind a size can change with
+    this thread's plan override or grid limit, so a launch that reports
+    MBS_ERR_WORKSPACE asks again with fresh=True (see _launch)."""
+    key = (M, N, K, device.index)
+    need = None if fresh else _ws_size_cache.get(key)
+    if need is None:
+        need = int(_lib.lib().mbs_gemm_a4w4_workspace_size(M, N, K))
+        _ws_size_cache[key] = need
+    return cached_workspace(need, device)
+
+
+def _stream_ptr(device: torch.device) -> int:
+    """Raw handle of the current stream of `device` (the cheap accessor when
+    this torch build has it)."""
+    raw = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+    if raw is not None:
+        return raw(device.index if device.index is not None else torch.cuda.current_device())
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _launch(func: str, args_before_ws: tuple, M: int, N: int, K: int, device: torch.device,
+            ws_fn=None) -> None:
+    """Launch `func` with the cached workspace of the shape; on MBS_ERR_WORKSPACE
+    (a cached size from before a plan override or grid limit) size it afresh once."""
+    ws_fn = ws_fn or _remembered_workspace
+    fn = getattr(_lib.lib(), func)
+    stream = _stream_ptr(device)
+    for fresh in (False, True):
+        ws = ws_fn(M, N, K, device, fresh=fresh)
+        st = fn(*args_before_ws, None if ws is None else ws.data_ptr(), 0 if ws is None else ws.numel(), stream)
+        if st != MBS_ERR_WORKSPACE or fresh:
+            _lib.check(func, st)
+            return
+
+
+MBS_ERR_WORKSPACE = 5
 
 
 def device_error(reset: bool = False) -> int:
@@ -201,14 +269,12 @@ def gemm_a4w4(A: torch.Tensor, B: torch.Tensor, A_scale: torch.Tensor, B_scale: 
     if Bsc.numel() < _round_up(N, 32) * snp:
         raise RuntimeError(f"gemm_a4w4: B_scale must hold roundup(N,32)*scaleN_pad = "
                            f"{_round_up(N, 32) * snp} bytes, got {Bsc.numel()}")
-    o = _out_buffer(out, Mpad, M, N, A.device)
-    with torch.cuda.device(A.device):
-        ws = workspace_for(M, N, K, A.device)
-        stream = torch.cuda.current_stream(A.device).cuda_stream
-        _lib.call("mbs_gemm_a4w4_launch_ws", _ptr(Au), _ptr(Bu), _ptr(Asc), _ptr(Bsc), _ptr(Afc),
-                  _ptr(Bfc), o.data_ptr(), M, N, K, Mpad, snp, _ptr(ws),
-                  0 if ws is None else ws.numel(), stream)
-    return o.narrow(0, 0, M)
+    dev = A.device
+    o = _out_buffer(out, Mpad, M, N, dev)
+    with _on_device(dev):
+        _launch("mbs_gemm_a4w4_launch_ws", (_ptr(Au), _ptr(Bu), _ptr(Asc), _ptr(Bsc), _ptr(Afc), _ptr(Bfc),
+                                            o.data_ptr(), M, N, K, Mpad, snp), M, N, K, dev)
+    return o if o.size(0) == M else o.narrow(0, 0, M)
 
 
 def _gemm_ex(A, B, A_scale, B_scale, A_factor, B_factor, out, alpha, bias):
@@ -224,14 +290,12 @@ def _gemm_ex(A, B, A_scale, B_scale, A_factor, B_factor, out, alpha, bias):
         if bias.dtype != torch.bfloat16 or bias.numel() != N:
             raise RuntimeError(f"gemm_a4w4: bias must be bf16 with N = {N} elements")
         bias_t = bias.contiguous()
-    o = _out_buffer(out, Mpad, M, N, A.device)
-    with torch.cuda.device(A.device):
-        ws = workspace_for(M, N, K, A.device)
-        stream = torch.cuda.current_stream(A.device).cuda_stream
-        _lib.call("mbs_gemm_a4w4_launch_ex", _ptr(Au), _ptr(Bu), _ptr(Asc), _ptr(Bsc), _ptr(Afc),
-                  _ptr(Bfc), o.data_ptr(), M, N, K, Mpad, snp, alpha, _ptr(bias_t), _ptr(ws),
-                  0 if ws is None else ws.numel(), stream)
-    return o.narrow(0, 0, M)
+    dev = A.device
+    o = _out_buffer(out, Mpad, M, N, dev)
+    with _on_device(dev):
+        _launch("mbs_gemm_a4w4_launch_ex", (_ptr(Au), _ptr(Bu), _ptr(Asc), _ptr(Bsc), _ptr(Afc), _ptr(Bfc),
+                                            o.data_ptr(), M, N, K, Mpad, snp, alpha, _ptr(bias_t)), M, N, K, dev)
+    return o if o.size(0) == M else o.narrow(0, 0, M)
 
 
 def gemm_a4w4_macro(A: torch.Tensor, B: torch.Tensor, A_scale: torch.Tensor,

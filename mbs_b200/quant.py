@@ -107,6 +107,9 @@ def shuffle_scales(s: torch.Tensor, K: int | None = None) -> torch.Tensor:
     return out
 
 
+_qws_size_cache: dict = {}
+
+
 def quant_gemm_a4w4(x: torch.Tensor, B: torch.Tensor, B_scale: torch.Tensor,
                     A_factor=None, B_factor=None, out=None) -> torch.Tensor:
     """Dynamic-quant + GEMM in one call (mbs_quant_gemm_a4w4_launch): bf16
@@ -114,7 +117,7 @@ def quant_gemm_a4w4(x: torch.Tensor, B: torch.Tensor, B_scale: torch.Tensor,
     shuffled scales.  Bit-identical to quantize_mxfp4(x, shuffle=True)
     followed by gemm_a4w4; for skinny and small M the quantiser runs inside
     the GEMM kernel (one launch)."""
-    from .mbs_gemm_a4w4 import _bytes, _out_buffer, _ptr, cached_workspace
+    from .mbs_gemm_a4w4 import _bytes, _launch, _on_device, _out_buffer, _ptr, cached_workspace
     x, M, K = _check_x(x)
     Bu, Bsc = _bytes(B), _bytes(B_scale)
     N = int(Bu.size(0))
@@ -132,9 +135,19 @@ def quant_gemm_a4w4(x: torch.Tensor, B: torch.Tensor, B_scale: torch.Tensor,
     if fb is not None and fb.numel() != N:
         raise RuntimeError(f"quant_gemm_a4w4: B_factor must hold N = {N} bytes")
     o = _out_buffer(out, _round_up(M, 32), M, N, x.device)
-    with torch.cuda.device(x.device):
+    with _on_device(x.device):
+        _launch("mbs_quant_gemm_a4w4_launch", (x.data_ptr(), int(x.stride(0)), Bu.data_ptr(), Bsc.data_ptr(),
+                                               _ptr(fa), _ptr(fb), o.data_ptr(), M, N, K, snp),
+                M, N, K, x.device, ws_fn=_quant_gemm_workspace)
+    return o if o.size(0) == M else o.narrow(0, 0, M)
+
+
+def _quant_gemm_workspace(M, N, K, device, fresh=False):
+    from .mbs_gemm_a4w4 import cached_workspace
+    key = (M, N, K, device.index)
+    need = None if fresh else _qws_size_cache.get(key)
+    if need is None:
         need = int(_lib.lib().mbs_quant_gemm_a4w4_workspace_size(M, N, K))
-        ws = cached_workspace(need, x.device)
-        _lib.call("mbs_quant_gemm_a4w4_launch", x.data_ptr(), int(x.stride(0)), Bu.data_ptr(), Bsc.data_ptr(),
-                  _ptr(fa), _ptr(fb), o.data_ptr(), M, N, K, snp, ws.data_ptr(), ws.numel(), _stream(x.device))
-    return o.narrow(0, 0, M)
+        _qws_size_cache[key] = need
+    # the fused call always needs a workspace (at least its barrier words)
+    return cached_workspace(max(need, 1), device)
