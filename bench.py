@@ -62,7 +62,9 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["mbs", "reference"], default="mbs")
-    ap.add_argument("--workload", choices=["prefill", "decode", "sharded"], default="prefill")
+    ap.add_argument("--workload", choices=["prefill", "decode", "decode-fused", "sharded"], default="prefill",
+                    help="decode-fused: config[1] from bf16 activations, quantised inside the GEMM "
+                         "(quant_gemm_a4w4)")
     ap.add_argument("--m", type=int, default=None, help="M for --workload decode (default 16)")
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--chunks", type=int, default=None,
@@ -88,6 +90,10 @@ def workload_shape(args):
     if args.workload == "decode":
         M = args.m or 16
         return M, 57344, 8192, f"cfg1 decode M={M} N=57344 K=8192 (Llama-3-70B gate+up)"
+    if args.workload == "decode-fused":
+        M = args.m or 16
+        return M, 57344, 8192, (f"cfg1 decode M={M} N=57344 K=8192 from bf16 activations, quantised inside "
+                                "the GEMM (quant_gemm_a4w4)")
     return 8192, 8192, 8192, "cfg2 prefill M=N=K=8192"
 
 
@@ -158,8 +164,8 @@ def load_traffic(workload, M):
     try:
         with open(os.path.join(REPO, "profiles", "traffic.json")) as f:
             d = json.load(f)
-        key = "prefill_8192" if workload == "prefill" else f"decode_m{M}"
-        return d.get(key)
+        key = {"prefill": "prefill_8192", "decode": f"decode_m{M}", "decode-fused": f"decode_fused_m{M}"}.get(workload)
+        return d.get(key) if key else None
     except (OSError, ValueError):
         return None
 
@@ -208,6 +214,10 @@ def run_mbs(args):
     dev = torch.device("cuda", local)
     M, N, K, wl_name = workload_shape(args)
     A, B, As, Bs = make_inputs(M, N, K, seed=1234 + rank, device=dev)
+    x_bf16 = None
+    if args.workload == "decode-fused":
+        x_bf16 = torch.randn(M, K, device=dev, generator=torch.Generator(device=dev).manual_seed(5)).to(
+            torch.bfloat16)
     out = torch.empty(((M + 31) // 32 * 32, N), dtype=torch.bfloat16, device=dev)
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.int32, device=dev)
     flush_rd = torch.zeros(L2_FLUSH_BYTES // 4, dtype=torch.int32, device=dev)
@@ -220,7 +230,10 @@ def run_mbs(args):
     stream = torch.cuda.current_stream(dev)
 
     def step():
-        mbs_b200.gemm_a4w4(A, B, As, Bs, out=out)
+        if x_bf16 is not None:
+            mbs_b200.quant_gemm_a4w4(x_bf16, B, Bs, out=out)
+        else:
+            mbs_b200.gemm_a4w4(A, B, As, Bs, out=out)
 
     # Decode: the weights alone are larger than L2, so steps run back to back
     # with events around all of them (the reference's bench_one.py:34-47 times
@@ -395,7 +408,9 @@ def run_mbs(args):
                                  "source": f"4 x bf16_tflops of {src} (dense FP4:BF16 = 4:1)"},
                 "kernel_ms": round(kernel_ms, 5)}
     else:
-        nbytes = N * K // 2 + N * K // 32 + M * K // 2 + M * K // 32 + M * N * 2
+        # weights + their scales + activations (fp4 + scales, or bf16 when quantised in the GEMM) + bf16 out
+        a_bytes = M * K * 2 if args.workload == "decode-fused" else M * K // 2 + M * K // 32
+        nbytes = N * K // 2 + N * K // 32 + a_bytes + M * N * 2
         gbs = nbytes / (kernel_ms * 1e-3) / 1e9
         roof = {"bound": "hbm", "achieved": round(gbs, 1), "peak": float(peaks["hbm_gbs"]),
                 "unit": "GB/s", "frac": round(gbs / float(peaks["hbm_gbs"]), 4), "traffic": traffic,
@@ -587,7 +602,9 @@ def decode_object(dev, peaks):
         x = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
         A, As = mbs_b200.quantize_mxfp4(x, shuffle=True)
         out = torch.empty(((M + 31) // 32 * 32, N), dtype=torch.bfloat16, device=dev)
-        nbytes = N * K // 2 + N * K // 32 + M * K // 2 + M * K // 32 + M * N * 2
+        # weights + their scales + activations (fp4 + scales, or bf16 when quantised in the GEMM) + bf16 out
+        a_bytes = M * K * 2 if args.workload == "decode-fused" else M * K // 2 + M * K // 32
+        nbytes = N * K // 2 + N * K // 32 + a_bytes + M * N * 2
         gus, eus, ius = _per_call_us(lambda: mbs_b200.gemm_a4w4(A, B, As, Bs, out=out), flush)
         # activations in bf16: quantise + GEMM as two calls, and fused in one launch
         q2_us = _per_call_us(lambda: _two_calls(mbs_b200, x, B, Bs, out), flush)
