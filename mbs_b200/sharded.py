@@ -212,11 +212,18 @@ class ShardedA4W4:
         return out.permute(1, 0, 2).reshape(M, self.world * nl)
 
     def _barrier(self):
-        """Device-side barrier on the current stream: a one-word NCCL all-reduce
-        completes on a rank only after every rank's stream has reached it."""
-        if self._flag is None:
-            self._flag = torch.zeros(1, dtype=torch.int32, device=self.B.device)
-        dist.all_reduce(self._flag, group=self.group)
+        """Barrier between the ranks' streams: on an NCCL group a one-word
+        all-reduce, which completes on a rank only after every rank's stream
+        has reached it (no host synchronisation); on other groups (gloo: ranks
+        that share a GPU, as in the single-GPU tests) the host waits for this
+        device's work and then for the other ranks."""
+        if dist.get_backend(self.group) == "nccl":
+            if self._flag is None:
+                self._flag = torch.zeros(1, dtype=torch.int32, device=self.B.device)
+            dist.all_reduce(self._flag, group=self.group)
+        else:
+            torch.cuda.synchronize(self.B.device)
+            dist.barrier(group=self.group)
 
     def _peer_buffer(self, nbytes: int, device: torch.device):
         """The layer's IPC-shared buffer on every rank, (re)allocated collectively."""
