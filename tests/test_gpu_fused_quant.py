@@ -86,3 +86,28 @@ def test_one_workspace_across_shapes_and_strided_x():
         torch.cuda.synchronize()
         assert torch.equal(got, ref2), f"step {i} {M}x{N}x{K}"
     assert mbs_b200.device_error() == 0
+
+
+@pytest.mark.parametrize("sched", ["auto", "stream_k", "ksplit", "dp_single"])
+def test_fused_special_values_bit_identical(plan, sched):
+    """Blocks holding Inf or NaN (scale 0xFF, codes 0), all-zero blocks, -0,
+    and values near the bf16 maximum: the in-kernel quantiser writes the same
+    bytes as the stand-alone one, so the outputs agree bit for bit (NaN
+    patterns included)."""
+    import mbs_b200
+    M, N, K = 40, 2048, 2048
+    qw, sw, B, Bs = _weights(N, K, seed=9)
+    x = seeded_bf16(M, K, seed=3).cuda()
+    x[0, 5] = float("inf")
+    x[1, 40] = float("-inf")
+    x[2, 77] = float("nan")
+    x[3, :64] = 0.0
+    x[4, 64:96] = -0.0
+    x[5, 96:128] = 3.0e38
+    x[6, 128:160] = -1.0e-38
+    plan(**PLANS[sched])
+    ref2 = _two_call(x, B, Bs, None, None)
+    got = mbs_b200.quant_gemm_a4w4(x, B, Bs)
+    torch.cuda.synchronize()
+    assert torch.equal(got.view(torch.int16), ref2.view(torch.int16))
+    assert mbs_b200.device_error() == 0

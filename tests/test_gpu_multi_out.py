@@ -80,3 +80,33 @@ def test_multi_output_rejects_bad_arguments():
     assert call(1, 200) == 1                               # ldc < N
     assert call(1, 260) == 1                               # ldc not a multiple of 8
     assert call(2, 512, [buf.data_ptr(), buf.data_ptr() + 2]) == 3  # misaligned copy
+
+
+@pytest.mark.parametrize("sched", ["pair384", "pair_mix", "dp_single", "stream_k"])
+def test_multi_output_with_alpha_and_bias(plan, sched):
+    """The alpha/bias epilogue on the multi-copy path (the staged pair
+    epilogue included): every copy equals the single-output
+    mbs_gemm_a4w4_launch_ex result bit for bit."""
+    import mbs_b200
+    from mbs_b200 import _lib
+    from mbs_b200.mbs_gemm_a4w4 import scale_n_pad, workspace_for
+    L = _lib.lib()
+    M, N, K = 300, 1040, 1024
+    c = Case(M, N, K, seed=77, factors=True)
+    bias = (torch.randn(N, generator=torch.Generator().manual_seed(5)) * 3).to(torch.bfloat16).cuda()
+    plan(**PLANS[sched])
+    single = mbs_b200.gemm_a4w4(c.A, c.B, c.A_scale, c.B_scale, c.A_factor, c.B_factor, alpha=-1.75, bias=bias)
+    copies, col0, ldc = 3, 32, N + 96
+    bufs = [torch.full((M + 8, ldc), 9.0, dtype=torch.bfloat16, device="cuda") for _ in range(copies)]
+    dst = (ctypes.c_void_p * copies)(*[b.data_ptr() + col0 * 2 for b in bufs])
+    ws = workspace_for(M, N, K, torch.device("cuda"))
+    st = L.mbs_gemm_a4w4_launch_multi(
+        c.A.data_ptr(), c.B.data_ptr(), c.A_scale.data_ptr(), c.B_scale.data_ptr(), c.A_factor.data_ptr(),
+        c.B_factor.data_ptr(), dst, copies, ldc, M, N, K, (M + 31) // 32 * 32, scale_n_pad(K),
+        ctypes.c_float(-1.75), bias.data_ptr(), None if ws is None else ws.data_ptr(),
+        0 if ws is None else ws.numel(), torch.cuda.current_stream().cuda_stream)
+    assert st == 0, L.mbs_last_error_message()
+    torch.cuda.synchronize()
+    for d, b in enumerate(bufs):
+        assert torch.equal(b[:M, col0:col0 + N], single), f"copy {d} differs from launch_ex"
+        assert torch.all(b[:, :col0] == 9.0) and torch.all(b[:, col0 + N:] == 9.0) and torch.all(b[M:] == 9.0)
