@@ -602,9 +602,7 @@ def decode_object(dev, peaks):
         x = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
         A, As = mbs_b200.quantize_mxfp4(x, shuffle=True)
         out = torch.empty(((M + 31) // 32 * 32, N), dtype=torch.bfloat16, device=dev)
-        # weights + their scales + activations (fp4 + scales, or bf16 when quantised in the GEMM) + bf16 out
-        a_bytes = M * K * 2 if args.workload == "decode-fused" else M * K // 2 + M * K // 32
-        nbytes = N * K // 2 + N * K // 32 + a_bytes + M * N * 2
+        nbytes = N * K // 2 + N * K // 32 + M * K // 2 + M * K // 32 + M * N * 2
         gus, eus, ius = _per_call_us(lambda: mbs_b200.gemm_a4w4(A, B, As, Bs, out=out), flush)
         # activations in bf16: quantise + GEMM as two calls, and fused in one launch
         q2_us = _per_call_us(lambda: _two_calls(mbs_b200, x, B, Bs, out), flush)

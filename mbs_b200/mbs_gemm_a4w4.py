@@ -126,8 +126,11 @@ def cached_workspace(need: int, device: torch.device) -> torch.Tensor | None:
     """
     if need == 0:
         return None
-    stream = torch.cuda.current_stream(device)
-    key = (device.index, stream.cuda_stream)
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    key = (idx, _stream_ptr(device))
+    buf = _ws_cache.get(key)
+    if buf is not None and buf.numel() >= need:
+        return buf
     with _ws_lock:
         buf = _ws_cache.get(key)
         if buf is None or buf.numel() < need:
@@ -226,7 +229,7 @@ def _check_inputs(A, B, A_scale, B_scale, A_factor, B_factor):
         if not (Bfc.is_cuda and Bfc.numel() == N):
             raise RuntimeError(f"gemm_a4w4: B_factor must hold N = {N} bytes on device, got {Bfc.numel()}")
     for name, t in (("A_scale", Asc), ("B_scale", Bsc)):
-        if not t.is_cuda or t.device != A.device:
+        if not t.is_cuda or t.get_device() != A.get_device():
             raise RuntimeError(f"gemm_a4w4: {name} must be on A's device")
     return Au, Bu, Asc, Bsc, Afc, Bfc, M, N, K
 
@@ -234,8 +237,9 @@ def _check_inputs(A, B, A_scale, B_scale, A_factor, B_factor):
 def _out_buffer(out, Mpad, M, N, device):
     if out is None:
         return torch.empty((Mpad, N), dtype=torch.bfloat16, device=device)
-    if out.dtype != torch.bfloat16 or out.device != device or not out.is_contiguous() \
-            or out.dim() != 2 or out.size(0) < M or out.size(1) != N:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    if out.dtype != torch.bfloat16 or not out.is_cuda or out.get_device() != idx \
+            or not out.is_contiguous() or out.dim() != 2 or out.size(0) < M or out.size(1) != N:
         raise RuntimeError(f"gemm_a4w4: out must be a contiguous bf16 [>= {M}, {N}] tensor on {device}")
     return out
 
