@@ -793,6 +793,10 @@ def sharded_object(args, world, rank, dev):
            "exposed_exchange_ms": round(layer_ms - local_ms, 4),
            "exchange": "none (one rank holds all of C)" if world == 1 else layer.describe_exchange(exchange, chunks),
            "bytes_received_per_rank": (world - 1) * M * nl * 2,
+           # what bounds the layer: the exchange volume at the pool's peer-copy rate
+           # (770 GB/s per direction) against quantise + GEMM alone
+           "nvlink_bound_ms": round((world - 1) * M * nl * 2 / 770e9 * 1e3, 4),
+           "layer_over_bound": round(layer_ms / max(local_ms, (world - 1) * M * nl * 2 / 770e9 * 1e3), 3),
            "parity": {"oracle_sample_ok": bool(flags[0].item()), "max_ratio": round(float(rat.item()), 4),
                       "sample": "64 rows x 256 columns of every rank's shard against the CPU oracle",
                       "exchange_checksums_ok": bool(flags[1].item())},
