@@ -114,9 +114,17 @@ constexpr int align_up(int x, int a) { return (x + a - 1) / a * a; }
 // weight format (pack_weight_kernel): per 256-row tile and K stage one
 // contiguous block = the 32 KB tile in shared-memory order followed by its
 // 2 KB of tcgen05.cp-ready scale blocks, loaded with one bulk copy.
+// R_QUANT_: the activation rows (at most XQ_ROWS = 8 of them) arrive as bf16
+// (a plain box of rows x BK values, 512 B per row, in the space the A tile
+// otherwise takes) and warp 2 quantises them in shared memory: the e2m1
+// codes go over the start of that staging, in the 128-byte-swizzled layout
+// the MMA reads, the scales straight into the tcgen05.cp blocks (no raw
+// activation scales, no global A).
 constexpr int PACK_STAGE_BYTES = 256 * BKB + 4 * 512;
+constexpr int XQ_ROWS = 8;
 
-template <int BN_, bool SWAP_, bool W_MACRO_, int STAGES_, int R_ROWS_ = 128, bool C_PACKED_ = false>
+template <int BN_, bool SWAP_, bool W_MACRO_, int STAGES_, int R_ROWS_ = 128, bool C_PACKED_ = false,
+          bool R_QUANT_ = false>
 struct Cfg
 {
     static constexpr int BN = BN_;
@@ -124,8 +132,11 @@ struct Cfg
     static constexpr int STAGES = STAGES_;
     static constexpr int R_ROWS = R_ROWS_;
     static constexpr bool C_PACKED = C_PACKED_;
+    static constexpr bool R_QUANT = R_QUANT_;
     static_assert(R_ROWS == 128 || (!SWAP_ && (R_ROWS == 32 || R_ROWS == 64)), "R rows");
     static_assert(!C_PACKED || (!SWAP_ && !W_MACRO_ && BN_ == 256), "packed weights: non-swapped, BN 256");
+    static_assert(!R_QUANT || (!SWAP_ && !W_MACRO_ && !C_PACKED_ && R_ROWS_ == 32),
+                  "in-stage quantiser: 32-row non-swapped tiles, plain weights");
     static constexpr bool R_PRESHUF = SWAP;   // weights are the preshuffled operand
     static constexpr bool C_PRESHUF = !SWAP;
     static constexpr bool R_MACRO = SWAP && W_MACRO_;
@@ -133,8 +144,11 @@ struct Cfg
     static constexpr int C_RB = BN >= 128 ? BN / 128 : 1;  // 128-row scale blocks of C
 
     static constexpr int R_DATA = R_ROWS * BKB;
+    static constexpr int R_ROW_TX = R_QUANT ? BK * 2 : BKB;  // bytes the TMA brings per activation row
+    static_assert(XQ_ROWS * BK * 2 <= R_DATA, "in-stage quantiser: the bf16 rows fit the A tile's space");
+    static constexpr int R_SPAN = R_DATA;                     // R data (or bf16 staging + codes)
     static constexpr int C_DATA = BN * BKB;
-    static constexpr int R_RAW = R_MACRO ? (R_ROWS / 32) * 16 : (R_ROWS / 32) * 256;
+    static constexpr int R_RAW = R_QUANT ? 0 : R_MACRO ? (R_ROWS / 32) * 16 : (R_ROWS / 32) * 256;
     static constexpr int C_RAW = C_PACKED ? 0 : (C_MACRO ? (BN / 32) * 16 : (BN / 32) * 256);
     static constexpr int R_ATOM = 2 * 512;
     static constexpr int C_ATOM = 2 * C_RB * 512;
@@ -142,14 +156,14 @@ struct Cfg
     // packed: [R data][C data][C atoms][R raw][R atoms] (C data + atoms contiguous)
     // else:   [R data][C data][R raw][C raw][R atoms][C atoms]
     static constexpr int R_DATA_OFF = 0;
-    static constexpr int C_DATA_OFF = R_DATA_OFF + R_DATA;
+    static constexpr int C_DATA_OFF = R_DATA_OFF + R_SPAN;
     static constexpr int R_RAW_OFF = C_PACKED ? C_DATA_OFF + C_DATA + C_ATOM : C_DATA_OFF + C_DATA;
     static constexpr int C_RAW_OFF = R_RAW_OFF + align_up(R_RAW, 128);
     static constexpr int R_ATOM_OFF = C_RAW_OFF + align_up(C_RAW, 128);
     static constexpr int C_ATOM_OFF = C_PACKED ? C_DATA_OFF + C_DATA : R_ATOM_OFF + R_ATOM;
     static constexpr int STAGE_END = C_PACKED ? R_ATOM_OFF + R_ATOM : C_ATOM_OFF + C_ATOM;
     static constexpr int STAGE_BYTES = align_up(STAGE_END, 1024);
-    static constexpr uint32_t TX_BYTES = R_DATA + C_DATA + R_RAW + C_RAW + (C_PACKED ? C_ATOM : 0);
+    static constexpr uint32_t TX_BYTES = R_SPAN + C_DATA + R_RAW + C_RAW + (C_PACKED ? C_ATOM : 0);
     static_assert(!C_PACKED || C_DATA + C_ATOM == PACK_STAGE_BYTES, "packed stage");
 
     static constexpr int SF_STAGE_COLS = 8 + 8 * C_RB;
@@ -160,8 +174,10 @@ struct Cfg
         TMEM_NEED <= 32 ? 32 : TMEM_NEED <= 64 ? 64 : TMEM_NEED <= 128 ? 128 : TMEM_NEED <= 256 ? 256 : 512;
     static_assert(TMEM_NEED <= 512, "TMEM budget");
 
-    // barriers: full, sfready, empty [STAGES]; acc_full, acc_empty [2]; qready; tmem slot; abort
-    static constexpr int BAR_BYTES = (3 * STAGES + 5) * 8 + 16;
+    // barriers: full, sfready, empty [STAGES]; acc_full, acc_empty [2]; qready; xfull [STAGES when
+    // R_QUANT]; tmem slot; abort
+    static constexpr int XBARS = R_QUANT ? STAGES : 0;
+    static constexpr int BAR_BYTES = (3 * STAGES + 5 + XBARS) * 8 + 16;
     static constexpr int EPI_BYTES = (BM + 2 * BN) * 4;  // epilogue factor + bias staging
     static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + EPI_BYTES + 1024;  // +1024 alignment slack
     static_assert(SMEM_BYTES <= 232448, "shared memory budget");
@@ -437,6 +453,81 @@ __device__ __forceinline__ void transpose_side(const uint8_t* raw, uint8_t* atom
     }
 }
 
+// In-stage activation quantiser (R_QUANT configurations), run by warp 2 on
+// every stage once its bf16 rows landed (their own `xfull` barrier, so this
+// runs ahead of the stage's weights, which warp 3 still waits for).  The
+// n <= XQ_ROWS bf16 rows were staged by TMA as n x 512 B (row r's BK = 256
+// values at r * 512).  Each row becomes 128 B of e2m1 codes over the start
+// of the same buffer -- row r at r * 128, its 16-byte chunk b (32 values,
+// one scale block) at b ^ (r % 8): the 128-byte swizzle of the MMA's K-major
+// operand -- and 8 e8m0 scales written straight into the tcgen05.cp blocks,
+// scale (r, b) at (b / 4) * 512 + (r % 32) * 16 + (r / 32) * 4 + b % 4 (the
+// transpose_side<32> output).  The arithmetic is the stand-alone
+// quantiser's (mx_quant.cuh).
+// Lane l takes whole blocks: block l % 8 of rows l / 8 + 4i, i < NI (its
+// amax needs no other lane), and loads all of them before converting any;
+// the codes land over staging rows below 2 only after every lane's reads.
+// One warp converts ~8 rows per stage within the time the stage's weights
+// take to stream in (more rows take the grid-shared quantiser instead).
+template <int NI>
+__device__ __forceinline__ void quantise_rows(uint8_t* xs, uint8_t* atoms, int n, int lane)
+{
+    const int q = lane >> 3, b = lane & 7;
+    uint4 v[NI][4];
+#pragma unroll
+    for (int i = 0; i < NI; ++i)
+    {
+        const int r = min(q + 4 * i, n - 1);  // rows past n: any staged row (not stored)
+        const uint4* src = reinterpret_cast<const uint4*>(xs + r * 512 + b * 64);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v[i][j] = src[j];
+    }
+    uint4 code[NI];
+    uint32_t sc[NI];
+#pragma unroll
+    for (int i = 0; i < NI; ++i)
+    {
+        uint32_t w[4][4];
+        uint32_t am = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+        {
+            w[j][0] = v[i][j].x;
+            w[j][1] = v[i][j].y;
+            w[j][2] = v[i][j].z;
+            w[j][3] = v[i][j].w;
+            am = max(am, mx::amax_bits8(w[j]));
+        }
+        const uint32_t e = mx::scale_from_amax_bits(am);
+        const bool nan_block = e == 0xFFu;
+        const float inv = __uint_as_float((254u - (nan_block ? 254u : e)) << 23);
+        code[i].x = mx::encode8(w[0], inv, nan_block);
+        code[i].y = mx::encode8(w[1], inv, nan_block);
+        code[i].z = mx::encode8(w[2], inv, nan_block);
+        code[i].w = mx::encode8(w[3], inv, nan_block);
+        sc[i] = e;
+    }
+    __syncwarp();  // every lane's reads before any lane's writes
+#pragma unroll
+    for (int i = 0; i < NI; ++i)
+    {
+        const int r = q + 4 * i;
+        if (r < n)
+        {
+            *reinterpret_cast<uint4*>(xs + r * 128 + ((b ^ (r & 7)) << 4)) = code[i];
+            atoms[(b >> 2) * 512 + (r & 31) * 16 + (r >> 5) * 4 + (b & 3)] = (uint8_t)sc[i];
+        }
+    }
+}
+
+__device__ __forceinline__ void quantise_stage(uint8_t* xs, uint8_t* atoms, int n, int lane)
+{
+    if (n > 4)
+        quantise_rows<2>(xs, atoms, n, lane);
+    else
+        quantise_rows<1>(xs, atoms, n, lane);
+}
+
 // Cluster split-K.  Cluster rank r finishes rows [r R, (r + 1) R) of the
 // tile, R = R_ROWS / S (R_ROWS = 128, or 32 / 64 for skinny tiles, the rows
 // that can hold outputs).  Each CTA's buffer (in its pipeline stages, idle once
@@ -616,7 +707,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     uint64_t* acc_full = empty + STAGES;
     uint64_t* acc_empty = acc_full + 2;
     uint64_t* qready = acc_empty + 2;  // fused quantiser: this CTA's share of A is written
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(qready + 1);
+    uint64_t* xfull = qready + 1;      // in-stage quantiser: the stage's bf16 rows landed
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xfull + CF::XBARS);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     float* epi_f = reinterpret_cast<float*>(smem + STAGES * CF::STAGE_BYTES + CF::BAR_BYTES);
 
@@ -642,6 +734,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             mbar_init(&acc_empty[b], NUM_EPI_WARPS);
         }
         mbar_init(qready, QWARPS);
+        for (int s = 0; s < CF::XBARS; ++s) mbar_init(&xfull[s], 1);
         *abort_flag = 0;
         fence_mbar_init();
         prefetch_tmap(&tm_r);
@@ -673,7 +766,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (threadIdx.x == 0 && blockIdx.x < 1024) g_mbs_cta[blockIdx.x * 5 + 1] = globaltimer_ns();
 #endif
 
-    if constexpr (!CF::SWAP)
+    if constexpr (!CF::SWAP && !CF::R_QUANT)
     {
         if (p.qmode != 0 && warp >= 2)
         {
@@ -717,7 +810,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             uint32_t phase = 0;
             // Fused quantiser: the first STAGES stages are armed and their weights
             // issued at once; their A tiles (and A scales) follow once A is written.
-            int ndef = (!CF::SWAP && p.qmode != 0) ? 0 : -1;  // -1: A is ready
+            int ndef = (!CF::SWAP && !CF::R_QUANT && p.qmode != 0) ? 0 : -1;  // -1: A is ready
             int def_slot[STAGES], def_r0[STAGES], def_ks[STAGES];
             auto a_ready = [&]() {
                 bool ok = mbar_wait(qready, 0, nullptr);
@@ -754,7 +847,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             const uint64_t pol_c = CF::SWAP ? l2_policy_evict_normal() : pol_w;
             // A box of activation rows stops at M when one tile covers them all, so no
             // stage pays for out-of-bounds fill; expect only the bytes it brings.
-            const uint32_t tx_bytes = CF::TX_BYTES - (uint32_t)((CF::SWAP ? BN : CF::R_ROWS) - p.act_rows) * BKB;
+            // In-stage quantiser: the bf16 rows complete `xfull`, the rest `full`.
+            const uint32_t tx_bytes = CF::TX_BYTES - (CF::R_QUANT ? (uint32_t)CF::R_SPAN
+                                                                  : (uint32_t)((CF::SWAP ? BN : CF::R_ROWS) -
+                                                                               p.act_rows) * BKB);
+            const uint32_t x_tx = (uint32_t)p.act_rows * CF::R_ROW_TX;
             Work w;
             for (int i = 0; get_work(p, i, w); ++i)
             {
@@ -777,6 +874,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     tacc[10] += 1;
 #endif
                     uint8_t* st = smem + slot * CF::STAGE_BYTES;
+                    if constexpr (CF::R_QUANT)
+                    {
+                        // bf16 activations (tm_r is their map): {BK values, rows}
+                        mbar_arrive_expect_tx(&xfull[slot], x_tx);
+                        tma_load_2d_hint(st + CF::R_DATA_OFF, &tm_r, &xfull[slot], ks * BK, r0, pol_r);
+                    }
                     mbar_arrive_expect_tx(&full[slot], tx_bytes);
                     const bool defer = ndef >= 0;
                     if (defer)
@@ -788,6 +891,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     }
                     else if (CF::R_PRESHUF)
                         tma_load_3d_hint(st + CF::R_DATA_OFF, &tm_r, &full[slot], 0, r0 / 16, ks * 8, pol_r);
+                    else if (CF::R_QUANT)
+                        ;  // loaded above
                     else
                         tma_load_2d_hint(st + CF::R_DATA_OFF, &tm_r, &full[slot], ks * BKB, r0, pol_r);
                     if (CF::C_PACKED)
@@ -798,8 +903,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         tma_load_3d_hint(st + CF::C_DATA_OFF, &tm_c, &full[slot], 0, c0 / 16, ks * 8, pol_c);
                     else
                         tma_load_2d_hint(st + CF::C_DATA_OFF, &tm_c, &full[slot], ks * BKB, c0, pol_c);
-                    if (defer)
-                        ;  // A scales follow the deferred A tile
+                    if (defer || CF::R_QUANT)
+                        ;  // A scales follow the deferred A tile, or come from the quantiser warps
                     else if (CF::R_MACRO)
                         tma_load_2d_hint(st + CF::R_RAW_OFF, &tm_rsf, &full[slot], 16 * (ks >> 1), r0 / 32, pol_r);
                     else
@@ -889,8 +994,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 {
                     // `sfready` implies `full`: both transposer warps arrive on it
                     // only after their own wait on this stage's `full` (release /
-                    // acquire through the two barriers), so one barrier test per
-                    // stage suffices here.
+                    // acquire through the two barriers; with the in-stage quantiser
+                    // warp 3 still waits for `full`), so one barrier test per stage
+                    // suffices here.
                     bool ok_sf;
                     {
                         MBS_TSTART();
@@ -961,7 +1067,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     else if (warp == 2 || warp == 3)
     {
         // ------------------------------------------------ scale transposers
-        // warp 2 rewrites the R operand's scales, warp 3 the C operand's.
+        // warp 2 rewrites the R operand's scales, warp 3 the C operand's; with
+        // the in-stage quantiser warp 2 quantises the activation rows instead.
         const bool r_side = warp == 2;
         int slot = 0;
         uint32_t phase = 0;
@@ -971,28 +1078,54 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             bool ok = true;
             for (int ks = w.k0; ks < w.k1; ++ks)
             {
-                bool ok_full;
+                if (CF::R_QUANT && r_side)
                 {
+                    // the stage's activation rows, quantised as soon as they land
+                    bool ok_x;
+                    {
+                        MBS_TSTART();
+                        ok_x = mbar_wait(&xfull[slot], phase, abort_flag);
+                        MBS_TADD(tacc, 4);
+                    }
+                    if (!ok_x)
+                    {
+                        if (lane == 0) raise_error(p, abort_flag);
+                        ok = false;
+                        break;
+                    }
                     MBS_TSTART();
-                    ok_full = mbar_wait(&full[slot], phase, abort_flag);
-                    MBS_TADD(tacc, 4);
+                    uint8_t* st = smem + slot * CF::STAGE_BYTES;
+                    quantise_stage(st + CF::R_DATA_OFF, st + CF::R_ATOM_OFF, p.act_rows, lane);
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&sfready[slot]);
+                    MBS_TADD(tacc, 5);
                 }
-                if (!ok_full)
+                else
                 {
-                    if (lane == 0) raise_error(p, abort_flag);
-                    ok = false;
-                    break;
+                    bool ok_full;
+                    {
+                        MBS_TSTART();
+                        ok_full = mbar_wait(&full[slot], phase, abort_flag);
+                        MBS_TADD(tacc, 4);
+                    }
+                    if (!ok_full)
+                    {
+                        if (lane == 0) raise_error(p, abort_flag);
+                        ok = false;
+                        break;
+                    }
+                    MBS_TSTART();
+                    uint8_t* st = smem + slot * CF::STAGE_BYTES;
+                    if (r_side && !CF::R_QUANT)
+                        transpose_side<CF::R_ROWS, CF::R_MACRO>(st + CF::R_RAW_OFF, st + CF::R_ATOM_OFF, ks, lane);
+                    else if (!CF::C_PACKED)
+                        transpose_side<BN, CF::C_MACRO>(st + CF::C_RAW_OFF, st + CF::C_ATOM_OFF, ks, lane);
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&sfready[slot]);
+                    MBS_TADD(tacc, 5);
                 }
-                MBS_TSTART();
-                uint8_t* st = smem + slot * CF::STAGE_BYTES;
-                if (r_side)
-                    transpose_side<CF::R_ROWS, CF::R_MACRO>(st + CF::R_RAW_OFF, st + CF::R_ATOM_OFF, ks, lane);
-                else if (!CF::C_PACKED)
-                    transpose_side<BN, CF::C_MACRO>(st + CF::C_RAW_OFF, st + CF::C_ATOM_OFF, ks, lane);
-                fence_proxy_async_smem();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&sfready[slot]);
-                MBS_TADD(tacc, 5);
                 if (++slot == STAGES)
                 {
                     slot = 0;
@@ -2503,6 +2636,14 @@ int validate(const Problem& pb)
 // M when a single tile holds them all (TMA zero-fill of the rows past M costs
 // stream time; those shared-memory rows only feed accumulator rows that are
 // never stored).
+// The bf16 activations go through the GEMM's in-stage quantiser: 32-row
+// tiles of at most XQ_ROWS rows (every larger M quantises A in global memory).
+bool in_stage_quant(const Problem& pb, const Plan& pl)
+{
+    return pb.qx != nullptr && !pl.swap && !pl.pair && !pb.packed && !pb.macro && pl.r_rows == 32 &&
+           pl.bn == 256 && pb.M <= XQ_ROWS;
+}
+
 int act_box_rows(const Problem& pb, const Plan& pl)
 {
     const int tile_rows = pl.swap ? pl.bn : pl.r_rows;
@@ -2510,7 +2651,7 @@ int act_box_rows(const Problem& pb, const Plan& pl)
 }
 
 int make_maps(const Problem& pb, const Plan& pl, CUtensorMap* tm_r, CUtensorMap* tm_c,
-              CUtensorMap* tm_rsf, CUtensorMap* tm_csf)
+              CUtensorMap* tm_rsf, CUtensorMap* tm_csf, bool x_in_stage = false)
 {
     const int r_rows = pl.swap ? BM : pl.r_rows, c_rows = pl.bn;
     const int act_rows = pl.swap ? c_rows : r_rows;
@@ -2521,6 +2662,18 @@ int make_maps(const Problem& pb, const Plan& pl, CUtensorMap* tm_r, CUtensorMap*
     CUtensorMap* w_sf = pl.swap ? tm_rsf : tm_csf;
     const uint64_t Kp = (uint64_t)pb.K / 2;
     int st;
+    if (x_in_stage)
+    {  // bf16 activations [M, K] (row stride qx_ld) for the in-stage quantiser:
+       // plain boxes of {BK values, rows}; values past K read as zero
+        const uint64_t dims[2] = {(uint64_t)pb.K, (uint64_t)pb.M};
+        const uint64_t strides[1] = {(uint64_t)pb.qx_ld * 2};
+        const uint32_t box[2] = {BK, (uint32_t)act_box_rows(pb, pl)};
+        st = encode_tmap(act_map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (void*)pb.qx, dims, strides, box,
+                         CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (st) return st;
+        memset(act_sf, 0, sizeof(CUtensorMap));  // the scales come from the quantiser warps
+    }
+    else
     {  // activations: plain [M, K/2], 128-byte swizzled boxes of {128 B, rows}
         const uint64_t dims[2] = {Kp, (uint64_t)pb.M};
         const uint64_t strides[1] = {Kp};
@@ -2543,6 +2696,7 @@ int make_maps(const Problem& pb, const Plan& pl, CUtensorMap* tm_r, CUtensorMap*
                          CU_TENSOR_MAP_SWIZZLE_NONE);
         if (st) return st;
     }
+    if (!x_in_stage)
     {  // activation scales: flatS as {256 B chunk, K-stage, 32-row group}
         const uint64_t dims[3] = {256, (uint64_t)pb.snp / 8, (uint64_t)pb.Mpad / 32};
         const uint64_t strides[2] = {256, (uint64_t)pb.snp * 32};
@@ -2712,7 +2866,7 @@ int launch_cfg(const Problem& pb, const Plan& pl, const DeviceInfo& dev, void* w
         }
     }
     CUtensorMap tm_r, tm_c, tm_rsf, tm_csf;
-    int st = make_maps(pb, pl, &tm_r, &tm_c, &tm_rsf, &tm_csf);
+    int st = make_maps(pb, pl, &tm_r, &tm_c, &tm_rsf, &tm_csf, CF::R_QUANT);
     if (st) return st;
     Params p{};
     p.M = pb.M;
@@ -2740,7 +2894,13 @@ int launch_cfg(const Problem& pb, const Plan& pl, const DeviceInfo& dev, void* w
     p.act_rows = act_box_rows(pb, pl);
     p.ksplit = pl.ksplit;
     p.withhold_release = g_withhold_release;
-    if (pb.qx != nullptr)
+    if (CF::R_QUANT != in_stage_quant(pb, pl)) return fail(MBS_ERR_CUDA, "in-stage quantiser configuration mismatch");
+    if (CF::R_QUANT)
+    {
+        // warps 2-3 quantise the bf16 rows each stage brings (tm_r maps them)
+        p.qmode = 3;
+    }
+    else if (pb.qx != nullptr)
     {
         // the GEMM writes A and its scales itself (TMA maps above point at them)
         p.qmode = pl.ksplit > 1 ? 2 : 1;
@@ -2819,6 +2979,7 @@ int dispatch(const Problem& pb, const Plan& pl, const DeviceInfo& dev, void* ws,
         return pb.macro ? launch_cfg<Cfg<64, true, true, 8>>(pb, pl, dev, ws, s)
                         : launch_cfg<Cfg<64, true, false, 8>>(pb, pl, dev, ws, s);
     }
+    if (in_stage_quant(pb, pl)) return launch_cfg<Cfg<256, false, false, 5, 32, false, true>>(pb, pl, dev, ws, s);
     if (pl.bn == 128)
         return pb.macro ? launch_cfg<Cfg<128, false, true, 6>>(pb, pl, dev, ws, s)
                         : launch_cfg<Cfg<128, false, false, 6>>(pb, pl, dev, ws, s);

@@ -1,11 +1,13 @@
 """Dynamic-quant + GEMM in one call (mbs_quant_gemm_a4w4_launch, Python
 quant_gemm_a4w4) against the two-call sequence it replaces
 (bench_one.py:20-31: quantise with shuffled scales, then gemm_a4w4): the
-outputs must be bit-identical, on every schedule -- the in-kernel quantiser
-behind a grid barrier (stream-K, data-parallel single CTAs), per CTA (cluster
-split-K), and the stand-alone quantiser in front of the CTA-pair GEMM --
-and one workspace serves a sequence of shapes (the grid barrier words are
-left zero)."""
+outputs must be bit-identical, on every schedule -- up to 8 rows quantised
+in shared memory from the bf16 rows each pipeline stage brings (stream-K,
+data-parallel, cluster split-K; 1, 4, 5 and 8 rows, a K tail shorter than a
+stage), more rows quantising A in global memory behind a grid barrier
+(stream-K, data-parallel single CTAs) or per CTA (cluster split-K), and the
+stand-alone quantiser in front of the CTA-pair GEMM -- and one workspace
+serves a sequence of shapes (the grid barrier words are left zero)."""
 
 import numpy as np
 import pytest
@@ -48,6 +50,13 @@ def _weights(N, K, seed):
     ("dp_single", 200, 768, 512), ("dp_single", 33, 96, 576),
     ("ksplit", 129, 784, 4160), ("ksplit", 24, 1280, 3072),
     ("pair", 300, 1040, 1024),
+    # in-stage quantiser (M <= 8): one and two blocks per lane, K tails, every schedule
+    ("auto", 4, 57344, 8192), ("auto", 8, 57344, 8192), ("auto", 5, 8192, 8192),
+    ("stream_k", 5, 1024, 1088), ("dp_single", 1, 256, 64), ("dp_single", 7, 272, 320),
+    ("ksplit", 8, 2048, 4096), ("stream_k", 3, 4096, 576),
+    # the grid-shared quantiser just past that: 9 to 64 rows
+    ("auto", 9, 57344, 1024), ("auto", 64, 4096, 2048), ("stream_k", 63, 1024, 1088),
+    ("dp_single", 31, 272, 320), ("ksplit", 48, 2048, 4096),
 ])
 def test_fused_matches_two_calls(plan, sched, M, N, K):
     import mbs_b200
@@ -88,14 +97,15 @@ def test_one_workspace_across_shapes_and_strided_x():
     assert mbs_b200.device_error() == 0
 
 
+@pytest.mark.parametrize("M", [40, 7])
 @pytest.mark.parametrize("sched", ["auto", "stream_k", "ksplit", "dp_single"])
-def test_fused_special_values_bit_identical(plan, sched):
+def test_fused_special_values_bit_identical(plan, sched, M):
     """Blocks holding Inf or NaN (scale 0xFF, codes 0), all-zero blocks, -0,
     and values near the bf16 maximum: the in-kernel quantiser writes the same
     bytes as the stand-alone one, so the outputs agree bit for bit (NaN
     patterns included)."""
     import mbs_b200
-    M, N, K = 40, 2048, 2048
+    N, K = 2048, 2048
     qw, sw, B, Bs = _weights(N, K, seed=9)
     x = seeded_bf16(M, K, seed=3).cuda()
     x[0, 5] = float("inf")
