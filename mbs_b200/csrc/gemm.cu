@@ -94,7 +94,8 @@ struct Params
     // Fused activation quantiser (mbs_quant_gemm_a4w4_launch), single-CTA kernel only:
     // qmode 0 = A given; 1 = the grid quantises bf16 qx into qa / qsa (the A and A_scale
     // buffers the TMA maps read) behind a grid barrier (qbar); 2 = every CTA quantises
-    // the A blocks of its own tile rows and K range (cluster split-K).
+    // the A blocks of its own tile rows and K range (cluster split-K); 3 = each stage's
+    // bf16 rows are quantised in shared memory (R_QUANT configurations).
     int qmode;
     int qx_ld;
     const __nv_bfloat16* qx;
@@ -146,7 +147,6 @@ struct Cfg
     static constexpr int R_DATA = R_ROWS * BKB;
     static constexpr int R_ROW_TX = R_QUANT ? BK * 2 : BKB;  // bytes the TMA brings per activation row
     static_assert(XQ_ROWS * BK * 2 <= R_DATA, "in-stage quantiser: the bf16 rows fit the A tile's space");
-    static constexpr int R_SPAN = R_DATA;                     // R data (or bf16 staging + codes)
     static constexpr int C_DATA = BN * BKB;
     static constexpr int R_RAW = R_QUANT ? 0 : R_MACRO ? (R_ROWS / 32) * 16 : (R_ROWS / 32) * 256;
     static constexpr int C_RAW = C_PACKED ? 0 : (C_MACRO ? (BN / 32) * 16 : (BN / 32) * 256);
@@ -156,14 +156,14 @@ struct Cfg
     // packed: [R data][C data][C atoms][R raw][R atoms] (C data + atoms contiguous)
     // else:   [R data][C data][R raw][C raw][R atoms][C atoms]
     static constexpr int R_DATA_OFF = 0;
-    static constexpr int C_DATA_OFF = R_DATA_OFF + R_SPAN;
+    static constexpr int C_DATA_OFF = R_DATA_OFF + R_DATA;  // (R_QUANT: bf16 staging + codes)
     static constexpr int R_RAW_OFF = C_PACKED ? C_DATA_OFF + C_DATA + C_ATOM : C_DATA_OFF + C_DATA;
     static constexpr int C_RAW_OFF = R_RAW_OFF + align_up(R_RAW, 128);
     static constexpr int R_ATOM_OFF = C_RAW_OFF + align_up(C_RAW, 128);
     static constexpr int C_ATOM_OFF = C_PACKED ? C_DATA_OFF + C_DATA : R_ATOM_OFF + R_ATOM;
     static constexpr int STAGE_END = C_PACKED ? R_ATOM_OFF + R_ATOM : C_ATOM_OFF + C_ATOM;
     static constexpr int STAGE_BYTES = align_up(STAGE_END, 1024);
-    static constexpr uint32_t TX_BYTES = R_SPAN + C_DATA + R_RAW + C_RAW + (C_PACKED ? C_ATOM : 0);
+    static constexpr uint32_t TX_BYTES = R_DATA + C_DATA + R_RAW + C_RAW + (C_PACKED ? C_ATOM : 0);
     static_assert(!C_PACKED || C_DATA + C_ATOM == PACK_STAGE_BYTES, "packed stage");
 
     static constexpr int SF_STAGE_COLS = 8 + 8 * C_RB;
@@ -848,7 +848,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             // A box of activation rows stops at M when one tile covers them all, so no
             // stage pays for out-of-bounds fill; expect only the bytes it brings.
             // In-stage quantiser: the bf16 rows complete `xfull`, the rest `full`.
-            const uint32_t tx_bytes = CF::TX_BYTES - (CF::R_QUANT ? (uint32_t)CF::R_SPAN
+            const uint32_t tx_bytes = CF::TX_BYTES - (CF::R_QUANT ? (uint32_t)CF::R_DATA
                                                                   : (uint32_t)((CF::SWAP ? BN : CF::R_ROWS) -
                                                                                p.act_rows) * BKB);
             const uint32_t x_tx = (uint32_t)p.act_rows * CF::R_ROW_TX;
@@ -2631,11 +2631,6 @@ int validate(const Problem& pb)
     return MBS_OK;
 }
 
-// TMA descriptors for the four operands of one launch.
-// Rows per activation TMA box: the activation operand's rows per tile, cut to
-// M when a single tile holds them all (TMA zero-fill of the rows past M costs
-// stream time; those shared-memory rows only feed accumulator rows that are
-// never stored).
 // The bf16 activations go through the GEMM's in-stage quantiser: 32-row
 // tiles of at most XQ_ROWS rows (every larger M quantises A in global memory).
 bool in_stage_quant(const Problem& pb, const Plan& pl)
@@ -2644,12 +2639,19 @@ bool in_stage_quant(const Problem& pb, const Plan& pl)
            pl.bn == 256 && pb.M <= XQ_ROWS;
 }
 
+// Rows per activation TMA box: the activation operand's rows per tile, cut to
+// M when a single tile holds them all (TMA zero-fill of the rows past M costs
+// stream time; those shared-memory rows only feed accumulator rows that are
+// never stored).
 int act_box_rows(const Problem& pb, const Plan& pl)
 {
     const int tile_rows = pl.swap ? pl.bn : pl.r_rows;
     return pb.M < tile_rows ? pb.M : tile_rows;
 }
 
+// TMA descriptors for the four operands of one launch (with the in-stage
+// quantiser, tm_r maps the bf16 activations and the activation-scale map is
+// unused).
 int make_maps(const Problem& pb, const Plan& pl, CUtensorMap* tm_r, CUtensorMap* tm_c,
               CUtensorMap* tm_rsf, CUtensorMap* tm_csf, bool x_in_stage = false)
 {
@@ -2897,7 +2899,7 @@ int launch_cfg(const Problem& pb, const Plan& pl, const DeviceInfo& dev, void* w
     if (CF::R_QUANT != in_stage_quant(pb, pl)) return fail(MBS_ERR_CUDA, "in-stage quantiser configuration mismatch");
     if (CF::R_QUANT)
     {
-        // warps 2-3 quantise the bf16 rows each stage brings (tm_r maps them)
+        // warp 2 quantises the bf16 rows each stage brings (tm_r maps them)
         p.qmode = 3;
     }
     else if (pb.qx != nullptr)
