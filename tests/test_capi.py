@@ -78,6 +78,33 @@ def test_quant_and_shuffle_validation_without_device(lib):
     assert lib.mbs_quantize_mxfp4_macro(1024, 4, 40, 64, 1024, 1024, None) == 2
 
 
+def test_multi_output_and_fused_quant_validation_without_device(lib):
+    """The several-copies entry point and the dynamic-quant entry point reject
+    bad arguments in host-side validation, before any CUDA call."""
+    def multi(dsts, n=None, ldc=16):
+        arr = None if dsts is None else (ctypes.c_void_p * max(1, len(dsts)))(*dsts)
+        n = len(dsts) if n is None and dsts is not None else (n or 0)
+        return lib.mbs_gemm_a4w4_launch_multi(1024, 1024, 1024, 1024, None, None, arr, n, ldc,
+                                              8, 16, 64, 32, 8, 1.0, None, None, 0, None)
+    assert multi(None) == 1                                   # no output copies
+    assert multi([4096], n=0) == 1
+    assert multi([4096] * 9) == 1 and b"at most 8" in lib.mbs_last_error_message()
+    assert multi([4096], ldc=8) == 1 and b"ldc" in lib.mbs_last_error_message()   # ldc < N
+    assert multi([4096], ldc=20) == 1                         # ldc % 8
+    assert multi([4096, None]) == 1 and b"copy 1 is NULL" in lib.mbs_last_error_message()
+    assert multi([4096, 4096 + 8]) == 3                       # misaligned copy
+
+    def qg(x=4096, ld_x=64, K=64, ws=8192):
+        return lib.mbs_quant_gemm_a4w4_launch(x, ld_x, 1024, 1024, None, None, 2048, 8, 16, K, 8, ws,
+                                              1 << 20, None)
+    assert qg(x=None) == 1
+    assert qg(ws=None) == 1
+    assert qg(ld_x=32) == 1 and b"ld_x" in lib.mbs_last_error_message()  # ld_x < K
+    assert qg(ld_x=68) == 1                                   # ld_x % 8
+    assert qg(x=4096 + 2) == 1                                # x not 16-byte aligned
+    assert qg(ws=8192 + 16) == 3                              # workspace not 256-byte aligned
+
+
 def test_workspace_size_is_host_only(lib):
     lib.mbs_gemm_a4w4_workspace_size.restype = ctypes.c_size_t
     # decode shapes use stream-K partials; a large prefill runs on CTA pairs
