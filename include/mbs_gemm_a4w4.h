@@ -153,11 +153,13 @@ int mbs_gemm_a4w4_launch_multi(const uint8_t* A, const uint8_t* B, const uint8_t
  * preshuffled weight B, as mbs_quantize_mxfp4(x, shuffled) followed by
  * mbs_gemm_a4w4_launch_ws, with bit-identical results.  When the plan runs
  * on single CTAs (skinny and small M: decode, stream-K, cluster split-K)
- * the quantiser lives inside the GEMM kernel -- one launch: idle warps
- * quantise A into the workspace while the producer already streams the
- * first weight stages, and the A loads wait for it (a grid barrier, or for
- * cluster split-K each CTA's own K range).  Large M (CTA pairs) launches the
- * stand-alone quantiser first.  The workspace (mbs_quant_gemm_a4w4_workspace_size,
+ * the quantiser lives inside the GEMM kernel -- one launch.  Up to 8 rows,
+ * each pipeline stage brings its bf16 rows and one warp converts them in
+ * shared memory while the stage's weights stream in (no global A); more
+ * rows are quantised by idle warps into the workspace while the producer
+ * already streams the first weight stages, and the A loads wait for it (a
+ * grid barrier, or for cluster split-K each CTA's own K range).  Large M
+ * (CTA pairs) launches the stand-alone quantiser first.  The workspace (mbs_quant_gemm_a4w4_workspace_size,
  * 256-byte aligned) holds the quantised A and the GEMM's scratch; it must be
  * zero-filled before first use and is left reusable (including its first
  * MBS_GEMM_WS_FLAG_BYTES, as for mbs_gemm_a4w4_launch_ws).  Replaces the
