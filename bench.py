@@ -608,6 +608,7 @@ def decode_object(dev, peaks):
         q2_us = _per_call_us(lambda: _two_calls(mbs_b200, x, B, Bs, out), flush)
         qf_us = _per_call_us(lambda: mbs_b200.quant_gemm_a4w4(x, B, Bs, out=out), flush)
         pk_us = _per_call_us(lambda: mbs_b200.gemm_a4w4_packed(A, packed, As, out=out), flush)
+        pkq_us = _per_call_us(lambda: mbs_b200.quant_gemm_a4w4_packed(x, packed, out=out), flush)
         gbs = nbytes / (gus * 1e-6) / 1e9
         cpu_s, cpu_sample = _cpu_call_s(M, N, K, rows=M, cols=2048)
         res[f"M={M}"] = {"graph_us": round(gus, 2), "eager_us": round(eus, 2), "isolated_us": round(ius, 2),
@@ -622,8 +623,10 @@ def decode_object(dev, peaks):
                                                 "(one launch); [graph, eager, isolated] per call"},
                          "packed_weights": {"us": [round(v, 2) for v in pk_us],
                                             "gbs_graph": round(nbytes / (pk_us[0] * 1e-6) / 1e9, 1),
-                                            "what": "gemm_a4w4_packed on the one-time packed weight layout; "
-                                                    "[graph, eager, isolated] per call"},
+                                            "from_bf16_us": [round(v, 2) for v in pkq_us],
+                                            "what": "gemm_a4w4_packed on the one-time packed weight layout, "
+                                                    "and quant_gemm_a4w4_packed from bf16 activations (one "
+                                                    "launch up to 16 rows); [graph, eager, isolated] per call"},
                          "cpu_baseline_us": round(cpu_s * 1e6, 1), "cpu_sample": cpu_sample}
     del B, Bs, packed
     torch.cuda.empty_cache()

@@ -220,6 +220,14 @@ int mbs_gemm_a4w4_launch_noalloc(const uint8_t* A, const uint8_t* B, const uint8
  * mbs_gemm_a4w4_packed_launch_ws: as mbs_gemm_a4w4_launch_ws with the packed
  *   weight in place of B/BScale; workspace size from
  *   mbs_gemm_a4w4_packed_workspace_size.
+ * mbs_quant_gemm_a4w4_packed_launch: dynamic quant + GEMM with the packed
+ *   weight, as mbs_quant_gemm_a4w4_launch (bf16 x [M, ld_x], bit-identical
+ *   to mbs_quantize_mxfp4 + mbs_gemm_a4w4_packed_launch_ws).  Up to 16 rows
+ *   each pipeline stage converts its bf16 rows in shared memory (the packed
+ *   scale blocks need no transpose, which frees a second converting warp);
+ *   more rows run the stand-alone quantiser first.  Workspace (256-byte
+ *   aligned, zero-filled before first use, left reusable) from
+ *   mbs_quant_gemm_a4w4_packed_workspace_size.
  */
 size_t mbs_packed_weight_bytes(int N, int K);
 int mbs_pack_weight(const uint8_t* B, const uint8_t* BScale, int N, int K, int scaleN_pad,
@@ -229,6 +237,10 @@ int mbs_gemm_a4w4_packed_launch_ws(const uint8_t* A, const uint8_t* packedB, con
                                    const uint8_t* AFactor, const uint8_t* BFactor, void* out, int M,
                                    int N, int K, int Mpad, int scaleN_pad, void* workspace,
                                    size_t workspace_bytes, void* stream);
+size_t mbs_quant_gemm_a4w4_packed_workspace_size(int M, int N, int K);
+int mbs_quant_gemm_a4w4_packed_launch(const void* x_bf16, int ld_x, const uint8_t* packedB,
+                                      const uint8_t* AFactor, const uint8_t* BFactor, void* out, int M,
+                                      int N, int K, void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---- quantiser and layout kernels ------------------------------------ */
 

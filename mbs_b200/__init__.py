@@ -7,10 +7,11 @@ N-sharded multi-GPU wrapper.
 """
 
 from .mbs_gemm_a4w4 import device_error, gemm_a4w4, gemm_a4w4_macro  # noqa: F401
-from .packed import PackedWeight, gemm_a4w4_packed, pack_weight  # noqa: F401
+from .packed import PackedWeight, gemm_a4w4_packed, pack_weight, quant_gemm_a4w4_packed  # noqa: F401
 from .quant import (quant_gemm_a4w4, quantize_mxfp4, quantize_mxfp4_macro,  # noqa: F401
                     quantize_mxfp4_mbs, shuffle_scales, shuffle_weight)
 
 __all__ = ["gemm_a4w4", "gemm_a4w4_macro", "quantize_mxfp4", "quantize_mxfp4_macro",
            "shuffle_weight", "shuffle_scales", "quant_gemm_a4w4", "pack_weight",
-           "gemm_a4w4_packed", "PackedWeight", "device_error", "quantize_mxfp4_mbs"]
+           "gemm_a4w4_packed", "quant_gemm_a4w4_packed", "PackedWeight", "device_error",
+           "quantize_mxfp4_mbs"]

@@ -30,6 +30,9 @@ SIGNATURES = {
                                    + [_c_int] * 5 + [ctypes.c_float, _c_void_p, _c_void_p, _c_size_t,
                                                      _c_void_p]),
     "mbs_quant_gemm_a4w4_workspace_size": (_c_size_t, [_c_int] * 3),
+    "mbs_quant_gemm_a4w4_packed_workspace_size": (_c_size_t, [_c_int] * 3),
+    "mbs_quant_gemm_a4w4_packed_launch": (_c_int, [_c_void_p, _c_int] + [_c_void_p] * 4 + [_c_int] * 3
+                                          + [_c_void_p, _c_size_t, _c_void_p]),
     "mbs_quant_gemm_a4w4_launch": (_c_int, [_c_void_p, _c_int] + [_c_void_p] * 5 + [_c_int] * 4
                                    + [_c_void_p, _c_size_t, _c_void_p]),
     "mbs_gemm_a4w4_macro_launch_ws": (_c_int, [_c_void_p] * 7 + [_c_int] * 6

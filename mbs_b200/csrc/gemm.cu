@@ -115,17 +115,17 @@ constexpr int align_up(int x, int a) { return (x + a - 1) / a * a; }
 // weight format (pack_weight_kernel): per 256-row tile and K stage one
 // contiguous block = the 32 KB tile in shared-memory order followed by its
 // 2 KB of tcgen05.cp-ready scale blocks, loaded with one bulk copy.
-// R_QUANT_: the activation rows (at most XQ_ROWS = 8 of them) arrive as bf16
-// (a plain box of rows x BK values, 512 B per row, in the space the A tile
-// otherwise takes) and warp 2 quantises them in shared memory: the e2m1
-// codes go over the start of that staging, in the 128-byte-swizzled layout
-// the MMA reads, the scales straight into the tcgen05.cp blocks (no raw
-// activation scales, no global A).
+// XQ_ (8 or 16; 0 = off): the activation rows (at most XQ_ of them) arrive
+// as bf16 (a plain box of rows x BK values, 512 B per row, over the space of
+// the A tile) and are quantised there in shared memory: the e2m1 codes go
+// over the start of that staging, in the 128-byte-swizzled layout the MMA
+// reads, the scales straight into the tcgen05.cp blocks (no raw activation
+// scales, no global A).  XQ_ = 8: warp 2 converts; XQ_ = 16 (packed weights,
+// whose scale blocks need no transpose): warps 2 and 3 convert 8 rows each.
 constexpr int PACK_STAGE_BYTES = 256 * BKB + 4 * 512;
-constexpr int XQ_ROWS = 8;
 
 template <int BN_, bool SWAP_, bool W_MACRO_, int STAGES_, int R_ROWS_ = 128, bool C_PACKED_ = false,
-          bool R_QUANT_ = false>
+          int XQ_ = 0>
 struct Cfg
 {
     static constexpr int BN = BN_;
@@ -133,11 +133,12 @@ struct Cfg
     static constexpr int STAGES = STAGES_;
     static constexpr int R_ROWS = R_ROWS_;
     static constexpr bool C_PACKED = C_PACKED_;
-    static constexpr bool R_QUANT = R_QUANT_;
+    static constexpr int XQ = XQ_;
+    static constexpr bool R_QUANT = XQ_ > 0;
     static_assert(R_ROWS == 128 || (!SWAP_ && (R_ROWS == 32 || R_ROWS == 64)), "R rows");
     static_assert(!C_PACKED || (!SWAP_ && !W_MACRO_ && BN_ == 256), "packed weights: non-swapped, BN 256");
-    static_assert(!R_QUANT || (!SWAP_ && !W_MACRO_ && !C_PACKED_ && R_ROWS_ == 32),
-                  "in-stage quantiser: 32-row non-swapped tiles, plain weights");
+    static_assert(XQ_ == 0 || ((XQ_ == 8 || (XQ_ == 16 && C_PACKED_)) && !SWAP_ && !W_MACRO_ && R_ROWS_ == 32),
+                  "in-stage quantiser: 8 rows, or 16 with packed weights, on 32-row non-swapped tiles");
     static constexpr bool R_PRESHUF = SWAP;   // weights are the preshuffled operand
     static constexpr bool C_PRESHUF = !SWAP;
     static constexpr bool R_MACRO = SWAP && W_MACRO_;
@@ -146,7 +147,8 @@ struct Cfg
 
     static constexpr int R_DATA = R_ROWS * BKB;
     static constexpr int R_ROW_TX = R_QUANT ? BK * 2 : BKB;  // bytes the TMA brings per activation row
-    static_assert(XQ_ROWS * BK * 2 <= R_DATA, "in-stage quantiser: the bf16 rows fit the A tile's space");
+    // the A tile's space: its codes, or with the in-stage quantiser the bf16 rows they overwrite
+    static constexpr int R_SPAN = XQ * BK * 2 > R_DATA ? XQ * BK * 2 : R_DATA;
     static constexpr int C_DATA = BN * BKB;
     static constexpr int R_RAW = R_QUANT ? 0 : R_MACRO ? (R_ROWS / 32) * 16 : (R_ROWS / 32) * 256;
     static constexpr int C_RAW = C_PACKED ? 0 : (C_MACRO ? (BN / 32) * 16 : (BN / 32) * 256);
@@ -156,7 +158,7 @@ struct Cfg
     // packed: [R data][C data][C atoms][R raw][R atoms] (C data + atoms contiguous)
     // else:   [R data][C data][R raw][C raw][R atoms][C atoms]
     static constexpr int R_DATA_OFF = 0;
-    static constexpr int C_DATA_OFF = R_DATA_OFF + R_DATA;  // (R_QUANT: bf16 staging + codes)
+    static constexpr int C_DATA_OFF = R_DATA_OFF + R_SPAN;
     static constexpr int R_RAW_OFF = C_PACKED ? C_DATA_OFF + C_DATA + C_ATOM : C_DATA_OFF + C_DATA;
     static constexpr int C_RAW_OFF = R_RAW_OFF + align_up(R_RAW, 128);
     static constexpr int R_ATOM_OFF = C_RAW_OFF + align_up(C_RAW, 128);
@@ -453,31 +455,33 @@ __device__ __forceinline__ void transpose_side(const uint8_t* raw, uint8_t* atom
     }
 }
 
-// In-stage activation quantiser (R_QUANT configurations), run by warp 2 on
-// every stage once its bf16 rows landed (their own `xfull` barrier, so this
-// runs ahead of the stage's weights, which warp 3 still waits for).  The
-// n <= XQ_ROWS bf16 rows were staged by TMA as n x 512 B (row r's BK = 256
-// values at r * 512).  Each row becomes 128 B of e2m1 codes over the start
-// of the same buffer -- row r at r * 128, its 16-byte chunk b (32 values,
-// one scale block) at b ^ (r % 8): the 128-byte swizzle of the MMA's K-major
-// operand -- and 8 e8m0 scales written straight into the tcgen05.cp blocks,
-// scale (r, b) at (b / 4) * 512 + (r % 32) * 16 + (r / 32) * 4 + b % 4 (the
+// In-stage activation quantiser (R_QUANT configurations), run on every
+// stage once its bf16 rows landed (their own `xfull` barrier, so this runs
+// ahead of the stage's weights).  The n <= XQ bf16 rows were staged by TMA
+// as n x 512 B over the A tile's space (row r's BK = 256 values at r * 512).
+// Each row becomes 128 B of e2m1 codes over the start of the same buffer --
+// row r at r * 128, its 16-byte chunk b (32 values, one scale block) at
+// b ^ (r % 8): the 128-byte swizzle of the MMA's K-major operand -- and 8
+// e8m0 scales written straight into the tcgen05.cp blocks, scale (r, b) at
+// (b / 4) * 512 + (r % 32) * 16 + (r / 32) * 4 + b % 4 (the
 // transpose_side<32> output).  The arithmetic is the stand-alone
 // quantiser's (mx_quant.cuh).
-// Lane l takes whole blocks: block l % 8 of rows l / 8 + 4i, i < NI (its
-// amax needs no other lane), and loads all of them before converting any;
-// the codes land over staging rows below 2 only after every lane's reads.
-// One warp converts ~8 rows per stage within the time the stage's weights
-// take to stream in (more rows take the grid-shared quantiser instead).
-template <int NI>
-__device__ __forceinline__ void quantise_rows(uint8_t* xs, uint8_t* atoms, int n, int lane)
+// Lane l takes whole blocks: block l % 8 of rows r0 + l / 8 + 4i, i < NI
+// (its amax needs no other lane), and loads all of them before converting
+// any.  The codes (rows below 4 of the staging) are written only after every
+// reader is done: this warp's lanes (__syncwarp), or with two converting
+// warps both warps (named barrier 2, which also ANDs their `ok`).  One warp
+// converts ~8 rows per stage within the time the stage's weights take to
+// stream in.
+template <int NI, bool TWO_WARPS>
+__device__ __forceinline__ bool quantise_rows(uint8_t* xs, uint8_t* atoms, int n, int r0, int lane, bool ok)
 {
     const int q = lane >> 3, b = lane & 7;
     uint4 v[NI][4];
 #pragma unroll
     for (int i = 0; i < NI; ++i)
     {
-        const int r = min(q + 4 * i, n - 1);  // rows past n: any staged row (not stored)
+        const int r = min(r0 + q + 4 * i, n - 1);  // rows past n: any staged row (not stored)
         const uint4* src = reinterpret_cast<const uint4*>(xs + r * 512 + b * 64);
 #pragma unroll
         for (int j = 0; j < 4; ++j) v[i][j] = src[j];
@@ -507,25 +511,31 @@ __device__ __forceinline__ void quantise_rows(uint8_t* xs, uint8_t* atoms, int n
         code[i].w = mx::encode8(w[3], inv, nan_block);
         sc[i] = e;
     }
-    __syncwarp();  // every lane's reads before any lane's writes
+    if constexpr (TWO_WARPS)
+        ok = named_bar_and(2, 64, ok);  // both warps' reads before either's writes
+    else
+        __syncwarp();                   // every lane's reads before any lane's writes
+    if (!ok) return false;
 #pragma unroll
     for (int i = 0; i < NI; ++i)
     {
-        const int r = q + 4 * i;
+        const int r = r0 + q + 4 * i;
         if (r < n)
         {
             *reinterpret_cast<uint4*>(xs + r * 128 + ((b ^ (r & 7)) << 4)) = code[i];
             atoms[(b >> 2) * 512 + (r & 31) * 16 + (r >> 5) * 4 + (b & 3)] = (uint8_t)sc[i];
         }
     }
+    return true;
 }
 
+// XQ 8: all n <= 8 rows by one warp
 __device__ __forceinline__ void quantise_stage(uint8_t* xs, uint8_t* atoms, int n, int lane)
 {
     if (n > 4)
-        quantise_rows<2>(xs, atoms, n, lane);
+        quantise_rows<2, false>(xs, atoms, n, 0, lane, true);
     else
-        quantise_rows<1>(xs, atoms, n, lane);
+        quantise_rows<1, false>(xs, atoms, n, 0, lane, true);
 }
 
 // Cluster split-K.  Cluster rank r finishes rows [r R, (r + 1) R) of the
@@ -1001,6 +1011,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     {
                         MBS_TSTART();
                         ok_sf = mbar_wait(&sfready[slot], phase, abort_flag);
+                        // 16-row in-stage quantiser: its warps arrive on `sfready` without
+                        // waiting for the stage's weights, so this thread tests `full` too
+                        if (CF::XQ == 16) ok_sf = mbar_wait(&full[slot], phase, abort_flag) && ok_sf;
                         MBS_TADD(tacc, 3);
                     }
                     if (!ok_sf)
@@ -1064,11 +1077,53 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             }
         }
     }
+    else if (CF::XQ == 16 && (warp == 2 || warp == 3))
+    {
+        // ------------------------------------------------ in-stage quantiser, 16 rows
+        // (packed weights: their scale blocks arrive ready, nothing to transpose)
+        // Warps 2 and 3 each convert 8 of the activation rows of every stage as
+        // soon as they land, and arrive on `sfready`; a failed wait in either
+        // warp reaches the other at the stage's barrier, so both stop together.
+        const int h = warp - 2;
+        int slot = 0;
+        uint32_t phase = 0;
+        bool ok = true;
+        Work w;
+        for (int i = 0; ok && get_work(p, i, w); ++i)
+        {
+            for (int ks = w.k0; ks < w.k1; ++ks)
+            {
+                bool ok_x;
+                {
+                    MBS_TSTART();
+                    ok_x = mbar_wait(&xfull[slot], phase, abort_flag);
+                    MBS_TADD(tacc, 4);
+                }
+                MBS_TSTART();
+                uint8_t* st = smem + slot * CF::STAGE_BYTES;
+                if (!quantise_rows<2, true>(st + CF::R_DATA_OFF, st + CF::R_ATOM_OFF, p.act_rows, 8 * h, lane, ok_x))
+                {
+                    if (lane == 0) raise_error(p, abort_flag);
+                    ok = false;
+                    break;
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&sfready[slot]);
+                MBS_TADD(tacc, 5);
+                if (++slot == STAGES)
+                {
+                    slot = 0;
+                    phase ^= 1;
+                }
+            }
+        }
+    }
     else if (warp == 2 || warp == 3)
     {
         // ------------------------------------------------ scale transposers
         // warp 2 rewrites the R operand's scales, warp 3 the C operand's; with
-        // the in-stage quantiser warp 2 quantises the activation rows instead.
+        // the 8-row in-stage quantiser warp 2 quantises the activation rows instead.
         const bool r_side = warp == 2;
         int slot = 0;
         uint32_t phase = 0;
@@ -2631,12 +2686,15 @@ int validate(const Problem& pb)
     return MBS_OK;
 }
 
-// The bf16 activations go through the GEMM's in-stage quantiser: 32-row
-// tiles of at most XQ_ROWS rows (every larger M quantises A in global memory).
-bool in_stage_quant(const Problem& pb, const Plan& pl)
+// Row capacity of the GEMM's in-stage quantiser for these bf16 activations:
+// 8 (one converting warp), 16 (two, with packed weights), or 0 (A is
+// quantised in global memory: by the GEMM's idle warps or, for packed
+// weights, by the stand-alone quantiser first).
+int in_stage_quant(const Problem& pb, const Plan& pl)
 {
-    return pb.qx != nullptr && !pl.swap && !pl.pair && !pb.packed && !pb.macro && pl.r_rows == 32 &&
-           pl.bn == 256 && pb.M <= XQ_ROWS;
+    if (pb.qx == nullptr || pl.swap || pl.pair || pb.macro || pl.r_rows != 32 || pl.bn != 256) return 0;
+    if (pb.M <= 8) return 8;
+    return pb.packed && pb.M <= 16 ? 16 : 0;
 }
 
 // Rows per activation TMA box: the activation operand's rows per tile, cut to
@@ -2896,10 +2954,10 @@ int launch_cfg(const Problem& pb, const Plan& pl, const DeviceInfo& dev, void* w
     p.act_rows = act_box_rows(pb, pl);
     p.ksplit = pl.ksplit;
     p.withhold_release = g_withhold_release;
-    if (CF::R_QUANT != in_stage_quant(pb, pl)) return fail(MBS_ERR_CUDA, "in-stage quantiser configuration mismatch");
+    if (CF::XQ != in_stage_quant(pb, pl)) return fail(MBS_ERR_CUDA, "in-stage quantiser configuration mismatch");
     if (CF::R_QUANT)
     {
-        // warp 2 quantises the bf16 rows each stage brings (tm_r maps them)
+        // warp 2 (and 3) quantise the bf16 rows each stage brings (tm_r maps them)
         p.qmode = 3;
     }
     else if (pb.qx != nullptr)
@@ -2959,6 +3017,9 @@ int dispatch(const Problem& pb, const Plan& pl, const DeviceInfo& dev, void* ws,
 {
     if (pb.packed)
     {
+        // bf16 activations quantised inside each stage: 8 rows by one warp, 16 by two
+        if (in_stage_quant(pb, pl) == 8) return launch_cfg<Cfg<256, false, false, 5, 32, true, 8>>(pb, pl, dev, ws, s);
+        if (in_stage_quant(pb, pl) == 16) return launch_cfg<Cfg<256, false, false, 5, 32, true, 16>>(pb, pl, dev, ws, s);
         if (pl.r_rows == 32) return launch_cfg<Cfg<256, false, false, 5, 32, true>>(pb, pl, dev, ws, s);
         if (pl.r_rows == 64) return launch_cfg<Cfg<256, false, false, 5, 64, true>>(pb, pl, dev, ws, s);
         return launch_cfg<Cfg<256, false, false, 4, 128, true>>(pb, pl, dev, ws, s);
@@ -2981,7 +3042,7 @@ int dispatch(const Problem& pb, const Plan& pl, const DeviceInfo& dev, void* ws,
         return pb.macro ? launch_cfg<Cfg<64, true, true, 8>>(pb, pl, dev, ws, s)
                         : launch_cfg<Cfg<64, true, false, 8>>(pb, pl, dev, ws, s);
     }
-    if (in_stage_quant(pb, pl)) return launch_cfg<Cfg<256, false, false, 5, 32, false, true>>(pb, pl, dev, ws, s);
+    if (in_stage_quant(pb, pl) == 8) return launch_cfg<Cfg<256, false, false, 5, 32, false, 8>>(pb, pl, dev, ws, s);
     if (pl.bn == 128)
         return pb.macro ? launch_cfg<Cfg<128, false, true, 6>>(pb, pl, dev, ws, s)
                         : launch_cfg<Cfg<128, false, false, 6>>(pb, pl, dev, ws, s);
@@ -3408,6 +3469,63 @@ extern "C" int mbs_gemm_a4w4_packed_launch_ws(const uint8_t* A, const uint8_t* p
     Problem pb{A, packedB, AScale, nullptr, AFactor, BFactor, out, M, N, K, Mpad, scaleN_pad, 0, false};
     pb.packed = true;
     return mbs::gemm::run(pb, workspace, workspace_bytes, false, reinterpret_cast<cudaStream_t>(stream));
+}
+
+// Workspace of mbs_quant_gemm_a4w4_packed_launch: the packed GEMM's own
+// workspace followed by room for the quantised A and its scales (used when
+// the rows exceed the in-stage quantiser), as for mbs_quant_gemm_a4w4_launch.
+extern "C" size_t mbs_quant_gemm_a4w4_packed_workspace_size(int M, int N, int K)
+{
+    using namespace mbs::gemm;
+    if (M <= 0 || N <= 0 || K <= 0) return 0;
+    return quant_layout(make_plan(M, N, K, num_sms_or_default(), true), M, K).total;
+}
+
+extern "C" int mbs_quant_gemm_a4w4_packed_launch(const void* x_bf16, int ld_x, const uint8_t* packedB,
+                                                 const uint8_t* AFactor, const uint8_t* BFactor, void* out,
+                                                 int M, int N, int K, void* workspace, size_t workspace_bytes,
+                                                 void* stream)
+{
+    using namespace mbs::gemm;
+    mbs::clear_error();
+    if (x_bf16 == nullptr || workspace == nullptr)
+        return mbs::fail(MBS_ERR_INVALID_ARGUMENT,
+                         "mbs_quant_gemm_a4w4_packed_launch: x and workspace must be non-NULL");
+    if (M <= 0 || K <= 0 || ld_x < K || ld_x % 8 != 0 || !mbs::aligned16(x_bf16))
+        return mbs::fail(MBS_ERR_INVALID_ARGUMENT,
+                         "mbs_quant_gemm_a4w4_packed_launch: x must be 16-byte aligned bf16 [M, ld_x], "
+                         "ld_x >= K, ld_x %% 8 == 0 (M=%d K=%d ld_x=%d)", M, K, ld_x);
+    if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+        return mbs::fail(MBS_ERR_MISALIGNED, "mbs_quant_gemm_a4w4_packed_launch: workspace must be 256-byte aligned");
+    mbs::DeviceInfo dev;
+    int st = mbs::current_device(&dev);
+    if (st) return st;
+    const Plan pl = make_plan(M, N, K, dev.num_sms, true);
+    const QuantLayout q = quant_layout(pl, M, K);
+    if (workspace_bytes < q.total)
+        return mbs::fail(MBS_ERR_WORKSPACE,
+                         "mbs_quant_gemm_a4w4_packed_launch: workspace of %zu bytes needed, %zu given", q.total,
+                         workspace_bytes);
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    uint8_t* qa = ws + q.a;
+    uint8_t* qs = ws + q.s;
+    Problem pb{qa, packedB, qs, nullptr, AFactor, BFactor, out, M, N, K, mbs::round_up(M, 32),
+               mbs::scale_n_pad(K), 0, false};
+    pb.packed = true;
+    st = validate(pb);
+    if (st) return st;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    pb.qx = x_bf16;
+    pb.qx_ld = ld_x;
+    if (in_stage_quant(pb, pl) == 0)
+    {
+        // more rows than the in-stage quantiser takes: the stand-alone quantiser first
+        pb.qx = nullptr;
+        st = mbs_quantize_mxfp4(x_bf16, M, K, ld_x, qa, qs, 1, stream);
+        if (st) return st;
+        mbs::clear_error();
+    }
+    return dispatch(pb, pl, dev, ws, s);
 }
 
 extern "C" int mbs_gemm_a4w4_macro_launch_ws(const uint8_t* A, const uint8_t* B,

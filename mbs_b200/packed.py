@@ -14,7 +14,7 @@ import torch
 from . import _lib
 from .mbs_gemm_a4w4 import _bytes, _out_buffer, _ptr, _round_up, cached_workspace, scale_n_pad
 
-__all__ = ["PackedWeight", "pack_weight", "gemm_a4w4_packed"]
+__all__ = ["PackedWeight", "pack_weight", "gemm_a4w4_packed", "quant_gemm_a4w4_packed"]
 
 
 class PackedWeight:
@@ -74,3 +74,43 @@ def gemm_a4w4_packed(A: torch.Tensor, W: PackedWeight, A_scale: torch.Tensor,
                   _ptr(Bfc), o.data_ptr(), M, N, K, Mpad, snp, _ptr(ws), 0 if ws is None else ws.numel(),
                   torch.cuda.current_stream(A.device).cuda_stream)
     return o.narrow(0, 0, M)
+
+
+_qws_size_cache: dict = {}
+
+
+def _quant_workspace(M, N, K, device, fresh=False):
+    key = (M, N, K, device.index)
+    need = None if fresh else _qws_size_cache.get(key)
+    if need is None:
+        need = int(_lib.lib().mbs_quant_gemm_a4w4_packed_workspace_size(M, N, K))
+        _qws_size_cache[key] = need
+    return cached_workspace(max(need, 1), device)
+
+
+def quant_gemm_a4w4_packed(x: torch.Tensor, W: PackedWeight, A_factor: torch.Tensor | None = None,
+                           B_factor: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Dynamic-quant + GEMM with a packed weight (mbs_quant_gemm_a4w4_packed_launch):
+    bf16 activations x [M, K]; bit-identical to quantize_mxfp4(x, shuffle=True)
+    followed by gemm_a4w4_packed.  Up to 16 rows, one launch that converts
+    each stage's bf16 rows in shared memory."""
+    from .mbs_gemm_a4w4 import _launch, _on_device
+    from .quant import _check_x
+    if not x.is_cuda or x.device != W.device:
+        raise RuntimeError("quant_gemm_a4w4_packed: x and the packed weight must be on the same CUDA device")
+    x, M, K = _check_x(x)
+    N = W.N
+    if K != W.K:
+        raise RuntimeError(f"quant_gemm_a4w4_packed: x has K={K}, the packed weight K={W.K}")
+    fa = None if A_factor is None else _bytes(A_factor)
+    fb = None if B_factor is None else _bytes(B_factor)
+    if fa is not None and fa.numel() != M:
+        raise RuntimeError(f"quant_gemm_a4w4_packed: A_factor must hold M = {M} bytes")
+    if fb is not None and fb.numel() != N:
+        raise RuntimeError(f"quant_gemm_a4w4_packed: B_factor must hold N = {N} bytes")
+    o = _out_buffer(out, _round_up(M, 32), M, N, x.device)
+    with _on_device(x.device):
+        _launch("mbs_quant_gemm_a4w4_packed_launch", (x.data_ptr(), int(x.stride(0)), W.data.data_ptr(),
+                                                      _ptr(fa), _ptr(fb), o.data_ptr(), M, N, K),
+                M, N, K, x.device, ws_fn=_quant_workspace)
+    return o if o.size(0) == M else o.narrow(0, 0, M)

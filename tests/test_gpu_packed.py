@@ -95,3 +95,75 @@ def test_packed_decode_full_size_sampled():
     ref = O.gemm_ref(qa.cpu().numpy(), qw[tc].cpu().numpy(), sa.cpu().numpy(), sw[tc].cpu().numpy())
     bound = O.gemm_abs_bound(qa.cpu().numpy(), qw[tc].cpu().numpy(), sa.cpu().numpy(), sw[tc].cpu().numpy())
     assert_gemm_close(out[:, tc], ref, bound, "packed decode")
+
+
+_PACKED_FUSED_PLANS = {
+    "auto": dict(),
+    "stream_k": dict(schedule=1, grid=17),
+    "dp_single": dict(schedule=2, pair=0),
+    "ksplit": dict(ksplit=4),
+}
+
+
+@pytest.mark.parametrize("sched,M,N,K", [
+    ("auto", 1, 57344, 8192), ("auto", 8, 57344, 8192), ("auto", 16, 57344, 8192),  # config[1]
+    ("auto", 12, 8192, 8192),                        # skinny cluster split-K
+    ("stream_k", 9, 2048, 1088), ("stream_k", 16, 1024, 576),
+    ("dp_single", 13, 272, 320), ("dp_single", 5, 256, 64),
+    ("ksplit", 16, 2048, 4096), ("ksplit", 3, 2048, 4096),
+    ("auto", 17, 4096, 2048), ("auto", 40, 2048, 1024),  # past 16 rows: the stand-alone quantiser first
+])
+def test_fused_quant_with_packed_weights(plan, sched, M, N, K):
+    """quant_gemm_a4w4_packed (bf16 activations, packed weights) is bit-identical
+    to quantize_mxfp4 + gemm_a4w4_packed: up to 8 rows converted in shared memory
+    by one warp, up to 16 by two, more by the stand-alone quantiser first; and
+    within the oracle's tolerance where that is cheap to compute."""
+    import mbs_b200
+    from tests.gpu_helpers import seeded_bf16, bf16_bits
+    w = seeded_bf16(N, K, N + K, std=0.02).cuda()
+    qw, sw = mbs_b200.quantize_mxfp4(w, shuffle=False)
+    W = mbs_b200.pack_weight(mbs_b200.shuffle_weight(qw), mbs_b200.shuffle_scales(sw, K))
+    x = seeded_bf16(M, K, M, outlier_frac=0.01).cuda()
+    g = torch.Generator(device="cuda").manual_seed(M + 3)
+    fa = torch.randint(0, 256, (M,), dtype=torch.uint8, device="cuda", generator=g)
+    fb = torch.randint(0, 256, (N,), dtype=torch.uint8, device="cuda", generator=g)
+    plan(**_PACKED_FUSED_PLANS[sched])
+    q, s = mbs_b200.quantize_mxfp4(x, shuffle=True)
+    ref2 = mbs_b200.gemm_a4w4_packed(q, W, s, fa, fb)
+    for call in range(2):  # the second call reuses the cached workspace
+        got = mbs_b200.quant_gemm_a4w4_packed(x, W, fa, fb)
+        torch.cuda.synchronize()
+        assert torch.equal(got, ref2), f"call {call}: differs from quantise + gemm_a4w4_packed"
+    assert mbs_b200.device_error() == 0
+    if M * N <= 1 << 22:
+        qa, sa = O.quantize_mxfp4(bf16_bits(x.cpu()))
+        wq, ws = qw.cpu().numpy(), sw.cpu().numpy()
+        ref = O.gemm_ref(qa, wq, sa, ws, fa.cpu().numpy(), fb.cpu().numpy())
+        assert_gemm_close(got, ref, O.gemm_abs_bound(qa, wq, sa, ws), f"fused packed {sched} {M}x{N}x{K}")
+
+
+@pytest.mark.parametrize("M", [14, 6])
+def test_fused_quant_with_packed_weights_special_values(M):
+    """Inf / NaN / zero / -0 / near-maximum blocks through the in-stage
+    quantiser with packed weights: the same bytes as the stand-alone quantiser,
+    so the outputs agree bit for bit (NaN patterns included)."""
+    import mbs_b200
+    from tests.gpu_helpers import seeded_bf16
+    N, K = 2048, 2048
+    w = seeded_bf16(N, K, 9, std=0.02).cuda()
+    qw, sw = mbs_b200.quantize_mxfp4(w, shuffle=False)
+    W = mbs_b200.pack_weight(mbs_b200.shuffle_weight(qw), mbs_b200.shuffle_scales(sw, K))
+    x = seeded_bf16(M, K, 3).cuda()
+    x[0, 5] = float("inf")
+    x[1, 40] = float("-inf")
+    x[2, 77] = float("nan")
+    x[3, :64] = 0.0
+    x[4, 64:96] = -0.0
+    x[5, 96:128] = 3.0e38
+    x[M - 1, 128:160] = -1.0e-38
+    q, s = mbs_b200.quantize_mxfp4(x, shuffle=True)
+    ref2 = mbs_b200.gemm_a4w4_packed(q, W, s)
+    got = mbs_b200.quant_gemm_a4w4_packed(x, W)
+    torch.cuda.synchronize()
+    assert torch.equal(got.view(torch.int16), ref2.view(torch.int16))
+    assert mbs_b200.device_error() == 0
