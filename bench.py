@@ -66,6 +66,9 @@ def parse():
                     help="decode-fused: config[1] from bf16 activations, quantised inside the GEMM "
                          "(quant_gemm_a4w4)")
     ap.add_argument("--m", type=int, default=None, help="M for --workload decode (default 16)")
+    ap.add_argument("--packed", action="store_true",
+                    help="decode workloads: the weights in the one-time packed layout (gemm_a4w4_packed, "
+                         "or quant_gemm_a4w4_packed from bf16 activations, up to 16 rows)")
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--chunks", type=int, default=None,
                     help="--workload sharded: row chunks whose exchange overlaps the next chunk's GEMM "
@@ -83,17 +86,24 @@ def parse():
     ap.add_argument("--soak-s", type=float, default=1.5,
                     help="seconds of untimed steps right before the timed region, so the "
                          "clock sampler sees the GPU under this load")
-    return ap.parse_args()
+    args = ap.parse_args()
+    if args.packed and args.workload not in ("decode", "decode-fused"):
+        ap.error("--packed applies to --workload decode and decode-fused")
+    if args.packed and args.workload == "decode-fused" and (args.m or 16) > 16:
+        ap.error("--packed with decode-fused: one launch per call up to M = 16")
+    return args
 
 
 def workload_shape(args):
+    packed = " with packed weights" if getattr(args, "packed", False) else ""
     if args.workload == "decode":
         M = args.m or 16
-        return M, 57344, 8192, f"cfg1 decode M={M} N=57344 K=8192 (Llama-3-70B gate+up)"
+        return M, 57344, 8192, f"cfg1 decode M={M} N=57344 K=8192 (Llama-3-70B gate+up){packed}"
     if args.workload == "decode-fused":
         M = args.m or 16
+        op = "quant_gemm_a4w4_packed" if packed else "quant_gemm_a4w4"
         return M, 57344, 8192, (f"cfg1 decode M={M} N=57344 K=8192 from bf16 activations, quantised inside "
-                                "the GEMM (quant_gemm_a4w4)")
+                                f"the GEMM ({op}){packed}")
     return 8192, 8192, 8192, "cfg2 prefill M=N=K=8192"
 
 
@@ -164,7 +174,9 @@ def load_traffic(workload, M):
     try:
         with open(os.path.join(REPO, "profiles", "traffic.json")) as f:
             d = json.load(f)
-        key = {"prefill": "prefill_8192", "decode": f"decode_m{M}", "decode-fused": f"decode_fused_m{M}"}.get(workload)
+        key = {"prefill": "prefill_8192", "decode": f"decode_m{M}", "decode-fused": f"decode_fused_m{M}",
+               "decode-packed": f"decode_packed_m{M}",
+               "decode-fused-packed": f"decode_fused_packed_m{M}"}.get(workload)
         return d.get(key) if key else None
     except (OSError, ValueError):
         return None
@@ -218,6 +230,7 @@ def run_mbs(args):
     if args.workload == "decode-fused":
         x_bf16 = torch.randn(M, K, device=dev, generator=torch.Generator(device=dev).manual_seed(5)).to(
             torch.bfloat16)
+    packed_w = mbs_b200.pack_weight(B, Bs) if args.packed else None
     out = torch.empty(((M + 31) // 32 * 32, N), dtype=torch.bfloat16, device=dev)
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.int32, device=dev)
     flush_rd = torch.zeros(L2_FLUSH_BYTES // 4, dtype=torch.int32, device=dev)
@@ -230,8 +243,12 @@ def run_mbs(args):
     stream = torch.cuda.current_stream(dev)
 
     def step():
-        if x_bf16 is not None:
+        if x_bf16 is not None and packed_w is not None:
+            mbs_b200.quant_gemm_a4w4_packed(x_bf16, packed_w, out=out)
+        elif x_bf16 is not None:
             mbs_b200.quant_gemm_a4w4(x_bf16, B, Bs, out=out)
+        elif packed_w is not None:
+            mbs_b200.gemm_a4w4_packed(A, packed_w, As, out=out)
         else:
             mbs_b200.gemm_a4w4(A, B, As, Bs, out=out)
 
@@ -343,13 +360,17 @@ def run_mbs(args):
     # own device and host buffers, so one step's result copy (device to host)
     # overlaps the next step's operand copies (host to device) on the other
     # copy engine, as a serving loop would run them.
-    hA, hB = A.cpu().pin_memory(), B.cpu().pin_memory()
-    hAs, hBs = As.cpu().pin_memory(), Bs.cpu().pin_memory()
+    # the same operator as the timed step: activations (quantised, or bf16 for
+    # the dynamic-quant call) and weights (preshuffled, or packed) from the host
+    acts = [x_bf16] if x_bf16 is not None else [A, As]
+    wts = [packed_w.data] if packed_w is not None else [B, Bs]
+    hosts = [t.cpu().pin_memory() for t in acts + wts]
+    n_act = len(acts)
     lanes = []
     for _ in range(2):
         lanes.append({
             "stream": torch.cuda.Stream(dev),
-            "dev": [torch.empty_like(t, device=dev) for t in (hA, hB, hAs, hBs)],
+            "dev": [torch.empty_like(t, device=dev) for t in hosts],
             "out": torch.empty(((M + 31) // 32 * 32, N), dtype=torch.bfloat16, device=dev),
             "hout": torch.empty((M, N), dtype=torch.bfloat16).pin_memory(),
         })
@@ -357,12 +378,16 @@ def run_mbs(args):
     def e2e_step(i):
         ln = lanes[i % 2]
         with torch.cuda.stream(ln["stream"]):
-            dA, dB, dAs, dBs = ln["dev"]
-            dA.copy_(hA, non_blocking=True)
-            dB.copy_(hB, non_blocking=True)
-            dAs.copy_(hAs, non_blocking=True)
-            dBs.copy_(hBs, non_blocking=True)
-            o = mbs_b200.gemm_a4w4(dA, dB, dAs, dBs, out=ln["out"])
+            for d, h in zip(ln["dev"], hosts):
+                d.copy_(h, non_blocking=True)
+            da, dw = ln["dev"][:n_act], ln["dev"][n_act:]
+            pw = mbs_b200.PackedWeight(dw[0], N, K) if packed_w is not None else None
+            if x_bf16 is not None:
+                o = (mbs_b200.quant_gemm_a4w4_packed(da[0], pw, out=ln["out"]) if pw is not None
+                     else mbs_b200.quant_gemm_a4w4(da[0], dw[0], dw[1], out=ln["out"]))
+            else:
+                o = (mbs_b200.gemm_a4w4_packed(da[0], pw, da[1], out=ln["out"]) if pw is not None
+                     else mbs_b200.gemm_a4w4(da[0], dw[0], da[1], dw[1], out=ln["out"]))
             ln["hout"].copy_(o, non_blocking=True)
 
     e2e_step(0)
@@ -384,11 +409,11 @@ def run_mbs(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
     hout = lanes[0]["hout"]
-    h2d = sum(t.numel() * t.element_size() for t in (hA, hB, hAs, hBs))
+    h2d = sum(t.numel() * t.element_size() for t in hosts)
     d2h = hout.numel() * hout.element_size()
 
     peaks, src = load_peaks()
-    traffic = load_traffic(args.workload, M)
+    traffic = load_traffic(args.workload + ("-packed" if args.packed else ""), M)
     if args.workload == "prefill":
         # MEASURED_PEAKS.json holds no FP4 figure: the denominator is the mxf4
         # tensor-pipe rate measured here by the probe (the prefill kernel's own
