@@ -465,7 +465,7 @@ def run_mbs(args):
     if rank == 0 and world == 1:
         line["cpu_baseline"] = cpu_baseline(M, N, K)
     if args.workload == "prefill" and not args.no_extra_configs:
-        del A, B, As, Bs, out, flush, flush_rd, lanes, hA, hB, hAs, hBs
+        del A, B, As, Bs, out, flush, flush_rd, lanes, hosts, acts, wts
         torch.cuda.empty_cache()
         if world == 1:
             line["decode"] = decode_object(dev, peaks)

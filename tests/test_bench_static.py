@@ -33,6 +33,29 @@ def _undefined_names(path):
     return bad
 
 
+def _deleted_but_never_bound(path):
+    """`del x` inside a function that never binds x (symtable counts the
+    `del` itself as a binding, so the check above cannot see it)."""
+    bad = []
+    for fn in ast.walk(ast.parse(open(path).read())):
+        if not isinstance(fn, (ast.FunctionDef, ast.AsyncFunctionDef)):
+            continue
+        bound = {a.arg for a in fn.args.args + fn.args.kwonlyargs + fn.args.posonlyargs}
+        deleted = []
+        for node in ast.walk(fn):
+            if isinstance(node, ast.Name) and isinstance(node.ctx, ast.Store):
+                bound.add(node.id)
+            elif isinstance(node, ast.Name) and isinstance(node.ctx, ast.Del):
+                deleted.append(node.id)
+            elif isinstance(node, (ast.FunctionDef, ast.AsyncFunctionDef)) and node is not fn:
+                bound.add(node.name)
+            elif isinstance(node, (ast.Import, ast.ImportFrom)):
+                bound.update((a.asname or a.name).split(".")[0] for a in node.names)
+        bad += [f"{fn.name}:{n}" for n in deleted if n not in bound]
+    return bad
+
+
 def test_bench_has_no_undefined_names():
     ast.parse(open(os.path.join(REPO, "bench.py")).read())
     assert _undefined_names(os.path.join(REPO, "bench.py")) == []
+    assert _deleted_but_never_bound(os.path.join(REPO, "bench.py")) == []
