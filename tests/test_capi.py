@@ -79,7 +79,7 @@ def test_quant_and_shuffle_validation_without_device(lib):
 
 
 def test_multi_output_and_fused_quant_validation_without_device(lib):
-    """The several-copies entry point and the dynamic-quant entry point reject
+    """The several-copies entry point and the dynamic-quant entry points reject
     bad arguments in host-side validation, before any CUDA call."""
     def multi(dsts, n=None, ldc=16):
         arr = None if dsts is None else (ctypes.c_void_p * max(1, len(dsts)))(*dsts)
@@ -103,6 +103,14 @@ def test_multi_output_and_fused_quant_validation_without_device(lib):
     assert qg(ld_x=68) == 1                                   # ld_x % 8
     assert qg(x=4096 + 2) == 1                                # x not 16-byte aligned
     assert qg(ws=8192 + 16) == 3                              # workspace not 256-byte aligned
+
+    def qp(x=4096, ld_x=64, K=64, ws=8192):
+        return lib.mbs_quant_gemm_a4w4_packed_launch(x, ld_x, 1024, None, None, 2048, 8, 16, K, ws, 1 << 20, None)
+    assert qp(x=None) == 1
+    assert qp(ws=None) == 1
+    assert qp(ld_x=32) == 1 and b"ld_x" in lib.mbs_last_error_message()
+    assert qp(x=4096 + 2) == 1
+    assert qp(ws=8192 + 16) == 3
 
 
 def test_workspace_size_is_host_only(lib):
