@@ -116,7 +116,9 @@ def quant_gemm_a4w4(x: torch.Tensor, B: torch.Tensor, B_scale: torch.Tensor,
     activations x [M, K] against a preshuffled MXFP4 weight B [N, K/2] with
     shuffled scales.  Bit-identical to quantize_mxfp4(x, shuffle=True)
     followed by gemm_a4w4; for skinny and small M the quantiser runs inside
-    the GEMM kernel (one launch)."""
+    the GEMM kernel (one launch: up to 8 rows each pipeline stage converts
+    its bf16 rows in shared memory, more rows are quantised by idle warps
+    behind a grid barrier)."""
     from .mbs_gemm_a4w4 import _bytes, _launch, _on_device, _out_buffer, _ptr, cached_workspace
     x, M, K = _check_x(x)
     Bu, Bsc = _bytes(B), _bytes(B_scale)
