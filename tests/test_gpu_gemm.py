@@ -44,6 +44,18 @@ def test_ragged_shapes_with_factors(M, N, K):
     assert_gemm_close(out, ref, bound, f"{M}x{N}x{K}")
 
 
+@pytest.mark.parametrize("M,N,K", [(777, 1040, 2048), (8000, 48, 512), (1000, 48, 1024), (8000, 1040, 256)])
+def test_tuning_log_ragged_shapes(M, N, K):
+    """The ragged M and N the reference's tuning log lists as passing
+    (asm_vs_wg_kernel.md:184-187: M = 1000, 777, 33, 300, 8000; N = 48, 1040),
+    on the planner's own schedule, full output against the oracle."""
+    c = Case(M, N, K, seed=M + 7 * N + K, factors=True)
+    out = _gemm(c)
+    torch.cuda.synchronize()
+    ref, bound = c.reference()
+    assert_gemm_close(out, ref, bound, f"tuning-log {M}x{N}x{K}")
+
+
 @pytest.mark.parametrize("M,N,K", [(2, 2048, 4096), (24, 1024, 2048), (48, 4096, 1024),
                                    (512, 1024, 2048)])
 @pytest.mark.parametrize("grid", [3, 17, 148])
