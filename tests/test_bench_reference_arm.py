@@ -42,3 +42,12 @@ def test_reference_arm_other_ranks_exit_without_work():
                 "MASTER_PORT": "29598"}, ("--gpus", "2"))
     assert res.returncode == 0, res.stderr[-2000:]
     assert not [ln for ln in res.stdout.splitlines() if ln.startswith("{")]
+
+
+def test_packed_flag_is_validated():
+    """--packed applies to the decode workloads only, and the fused one takes
+    at most 16 rows (one launch per call)."""
+    for args in (["--workload", "prefill", "--packed"], ["--workload", "decode-fused", "--packed", "--m", "32"]):
+        res = subprocess.run([sys.executable, "bench.py", *args], cwd=REPO, capture_output=True, text=True,
+                             timeout=300)
+        assert res.returncode == 2 and "--packed" in res.stderr, (args, res.stderr[-500:])
